@@ -1,0 +1,198 @@
+/*
+ * megamoe: B200-native (sm_100a) routed-MoE chain behind a C ABI.
+ *
+ * The chain: router GEMV -> sigmoid/softmax top-k with bias -> token-to-expert
+ * permutation (route record) -> MXFP4 block-scaled grouped gate_up GEMM ->
+ * SwiGLU + MXFP8 requant -> grouped down GEMM -> slot-order weighted combine.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t
+ * (passed as void*), returns an int status (MM_OK = 0) and never throws.
+ * Nothing here allocates or synchronizes inside a step: scratch is owned by
+ * the layer handle and allocated in mm_layer_create. Launches go to the given
+ * stream with programmatic dependent launch, so the calls are graph-capturable.
+ * The message of the last failure on the calling thread is mm_last_error().
+ *
+ * Reference interfaces replaced (paths within sgl-project/sgl-nvidia-mega):
+ *   mm_router_gemv       sgl_nvidia_mega/deepseek_v41/sm103/moe/src/router_mma.cu:101
+ *                        (host: deepseek_v41/sm103/moe/router_mma.py:64-80)
+ *   mm_gate_topk         sgl_nvidia_mega/deepseek_v41/sm103/moe/src/gate_topk.cuh:296
+ *                        (host: routed_expert_gemm.py:776, launch at :867);
+ *                        glm5_3/sm103/moe/routing.py:73 (MoeRouteTop8)
+ *   mm_route             deepseek_v41/sm103/moe/src/route.cu:23 and route_wide.cu:62
+ *                        (record layout route.cuh:6-46; host routed_expert_gemm.py:916)
+ *   mm_route_words       routed_expert_gemm.py:107-120 (max_ctas / cta_words / route_words)
+ *   mm_layer_create      RoutedExpertGemm.__init__, routed_expert_gemm.py:537-657
+ *   mm_layer_experts     RoutedExpertGemm.__call__, routed_expert_gemm.py:703-774
+ *   mm_layer_gate_experts RoutedExpertGemm.gate_topk_and_gemms, routed_expert_gemm.py:776-870
+ *   mm_finalize          deepseek_v41/sm103/all_reduce_mhc.py:402-662 (finalize arithmetic);
+ *                        glm5_3/sm103/moe/finalize.py:1-27
+ *   mm_layer_forward     deepseek_v41/moe/step.py:101 (one MoE step: router -> combine)
+ */
+#ifndef MEGAMOE_H
+#define MEGAMOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define MM_OK 0
+#define MM_ERR_INVALID 1        /* bad shape, pointer, alignment or argument   */
+#define MM_ERR_UNSUPPORTED 2    /* a valid request this build does not serve  */
+#define MM_ERR_CUDA 3           /* a CUDA runtime / driver call failed         */
+#define MM_ERR_DEVICE_TIMEOUT 4 /* a bounded device wait gave up (error word)  */
+#define MM_ERR_DEVICE 5         /* another device-side check failed            */
+
+/* ---- routing score functions ------------------------------------------- */
+#define MM_SCORE_SIGMOID 0      /* s = 1/(1+exp(-x)), key = s + bias            */
+#define MM_SCORE_SOFTMAX 1      /* key = x + bias, w = softmax over the top-k   */
+#define MM_SCORE_SQRTSOFTPLUS 2 /* s = sqrt(log1p(exp(x))), key = s + bias     */
+
+/* ---- expert weight formats ---------------------------------------------- */
+#define MM_WEIGHT_MXFP4 0 /* E2M1 codes + one E8M0 scale per 32 along K      */
+
+/* One group of experts in the canonical layout (SGLang FusedMoE w13/w2):
+ *   w13       u8 [n, 2*I, H/2]  E2M1 pairs, low nibble = even element;
+ *                               rows [0, I) are gate (w1), rows [I, 2I) up (w3)
+ *   w13_scale u8 [n, 2*I, H/32] E8M0 (value 2^(byte-127)) per 32 elements
+ *   w2        u8 [n, H, I/2]
+ *   w2_scale  u8 [n, H, I/32]
+ * w13 and w2 must be 32-byte aligned (TMA unpacking of 4-bit data). */
+typedef struct mm_expert_weights {
+  const void *w13;
+  const void *w13_scale;
+  const void *w2;
+  const void *w2_scale;
+} mm_expert_weights;
+
+typedef struct mm_layer_desc {
+  int32_t hidden;         /* H: multiple of 1024                                   */
+  int32_t intermediate;   /* I (this rank's slice): multiple of 256                */
+  int32_t experts;        /* local routed experts (this rank's window)             */
+  int32_t router_experts; /* experts the router scores (>= expert_offset+experts)  */
+  int32_t expert_offset;  /* router id of local expert 0 (expert parallelism)      */
+  int32_t top_k;          /* 1..16                                                 */
+  int32_t max_tokens;     /* largest T a call may pass: 1..256                     */
+  int32_t weight_format;  /* MM_WEIGHT_MXFP4                                       */
+  int32_t act_terms;      /* 2: activations as hi+lo MXFP8 (default numerics);
+                             1: single MXFP8 (the reference kernels' numerics)     */
+  int32_t device;         /* CUDA device ordinal the weights live on               */
+  mm_expert_weights routed; /* n = experts                                         */
+  mm_expert_weights shared; /* n = 1; shared.w13 == NULL: no shared expert          */
+  const float *clamp;       /* [experts] SwiGLU clamp limit or NULL (no clamp)      */
+  const float *shared_clamp;/* [1] or NULL                                          */
+} mm_layer_desc;
+
+typedef struct mm_layer mm_layer; /* opaque handle */
+
+/* Routing arguments of one call (gate_topk_and_gemms / moe_fused_gate). */
+typedef struct mm_gate_args {
+  const float *logits;       /* [T, router_experts] fp32                          */
+  const float *bias;         /* [router_experts] fp32 or NULL                     */
+  const int32_t *num_valid;  /* device int32 [1] or NULL: rows >= *num_valid get
+                                id -1 and weight 0 (padded graph rows)            */
+  int32_t score_func;        /* MM_SCORE_*                                        */
+  int32_t renormalize;       /* 1: w = s / sum(selected s) (always for softmax)   */
+  float routed_scaling;      /* multiplies every weight                           */
+  float renorm_eps;          /* > 0: divide by sum + eps; else by the guarded sum */
+  float *weights;            /* out [T, top_k] fp32                               */
+  int32_t *ids;              /* out [T, top_k] int32 (router ids)                 */
+} mm_gate_args;
+
+/* Sizes of the caller-owned buffers of a layer call. */
+typedef struct mm_layer_info {
+  int32_t hidden, intermediate, experts, router_experts, expert_offset, top_k;
+  int32_t max_tokens;
+  int32_t has_shared;
+  int64_t rows_capacity;   /* rows of the rows_out buffer (bf16 [rows, H])       */
+  int64_t shared_row_base; /* first rows_out row of the shared expert's T rows    */
+  int64_t route_words;     /* int32 words of the route record at max_tokens       */
+  int64_t weight_bytes;    /* algorithmic FP4 + scale bytes of one expert         */
+} mm_layer_info;
+
+/* Whole-step arguments (mm_layer_forward). */
+typedef struct mm_forward_args {
+  const uint16_t *x;        /* bf16 [T, H]                                       */
+  const uint16_t *router_w; /* bf16 [router_experts, H] or NULL (then logits)    */
+  const float *logits;      /* fp32 [T, router_experts] when router_w is NULL    */
+  float *logits_out;        /* fp32 [T, router_experts] scratch/out (router_w)   */
+  const float *bias;        /* [router_experts] or NULL                          */
+  const int32_t *num_valid; /* device [1] or NULL                                */
+  int32_t score_func, renormalize;
+  float routed_scaling, renorm_eps;
+  int32_t tokens;           /* T */
+  float *weights;           /* out [T, top_k]                                    */
+  int32_t *ids;             /* out [T, top_k]                                    */
+  int32_t *permuted;        /* out [T, top_k]                                    */
+  int32_t *record;          /* out route record (mm_route_words words)           */
+  uint16_t *rows;           /* out bf16 [rows_capacity, H] (deferred rows)       */
+  uint16_t *out;            /* out bf16 [T, H] combined, or NULL                 */
+  float *partial;           /* out fp32 [2, T, H] (routed, shared) un-rounded
+                               partial sums for a cross-rank all-reduce, or NULL */
+} mm_forward_args;
+
+/* ---- library ------------------------------------------------------------ */
+const char *mm_last_error(void);
+int mm_version(void);
+
+/* ---- stateless kernels ---------------------------------------------------- */
+/* logits[t, e] = sum_h x[t, h] * w[e, h] in a fixed summation order
+ * (replicated bit for bit by the CPU oracle). H % 1024 == 0. */
+int mm_router_gemv(const uint16_t *x, const uint16_t *w, float *logits, int32_t tokens,
+                   int32_t experts, int32_t hidden, void *stream);
+
+/* Router top-k of T rows (one CTA per row). E <= 1024, 1 <= top_k <= 16. */
+int mm_gate_topk(const mm_gate_args *args, int32_t tokens, int32_t router_experts,
+                 int32_t top_k, void *stream);
+
+/* int32 words of the route record for (T, top_k, local experts). */
+int64_t mm_route_words(int32_t tokens, int32_t top_k, int32_t experts);
+
+/* Route record + slot -> row map from top-k ids, bit for bit the reference's
+ * (route.cuh:6-46, route_wide.cu:1-14). expert_offset >= 0. T <= 256. */
+int mm_route(const int32_t *ids, int32_t *permuted, int32_t *record, int32_t tokens,
+             int32_t top_k, int32_t experts, int32_t expert_offset, void *stream);
+
+/* out[t] = bf16(bf16(sum_k w[t,k] * rows[perm[t,k]]) + shared[t]) in slot order
+ * (rows with perm -1 are skipped); shared_rows may be NULL. partial (fp32
+ * [2, T, H]) receives the un-rounded routed sum and the shared row instead
+ * when non-NULL (out may then be NULL). */
+int mm_finalize(const uint16_t *rows, const float *weights, const int32_t *permuted,
+                const uint16_t *shared_rows, uint16_t *out, float *partial,
+                int32_t tokens, int32_t top_k, int32_t hidden, void *stream);
+
+/* out = bf16(bf16(sum_r routed_r) + sum_r shared_r) from an all-reduced partial. */
+int mm_finalize_partial(const float *partial, uint16_t *out, int32_t tokens,
+                        int32_t hidden, void *stream);
+
+/* ---- layer ---------------------------------------------------------------- */
+int mm_layer_create(const mm_layer_desc *desc, mm_layer **out);
+int mm_layer_destroy(mm_layer *layer);
+int mm_layer_get_info(const mm_layer *layer, mm_layer_info *info);
+
+/* Route + gate_up + down from given top-k ids (RoutedExpertGemm.__call__):
+ * rows[permuted[t, k]] is slot (t, k)'s expert output (bf16 [rows_capacity, H]);
+ * the shared expert's rows start at info.shared_row_base. */
+int mm_layer_experts(mm_layer *layer, const uint16_t *x, const int32_t *ids,
+                     int32_t tokens, int32_t *permuted, int32_t *record,
+                     uint16_t *rows, void *stream);
+
+/* Top-k from router logits + route + gate_up + down (gate_topk_and_gemms). */
+int mm_layer_gate_experts(mm_layer *layer, const uint16_t *x, const mm_gate_args *gate,
+                          int32_t tokens, int32_t *permuted, int32_t *record,
+                          uint16_t *rows, void *stream);
+
+/* The whole MoE step: [router GEMV] -> top-k -> route -> experts -> combine. */
+int mm_layer_forward(mm_layer *layer, const mm_forward_args *args, void *stream);
+
+/* Synchronizes the layer's device and reads (then clears) its device error
+ * word: MM_OK, MM_ERR_DEVICE_TIMEOUT or MM_ERR_DEVICE. */
+int mm_layer_check(mm_layer *layer);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MEGAMOE_H */

@@ -1,0 +1,282 @@
+"""CPU oracle of the routed-MoE chain (TEST INFRASTRUCTURE, never the product).
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline / reference legs
+import this module. It restates the reference's algorithm for each step:
+
+  * bit-exact parts in C (oracle/mm_oracle.c, loaded through ctypes): the router
+    GEMV in the kernel's summation order, deterministic scores, top-k with bias,
+    the route record, MXFP8 quantization, the slot-order combine;
+  * the dense expert MLP by dequantize -> fp32 matmul (torch on the CPU), in two
+    numerics: "exact" (bf16 input, fp32 throughout: BASELINE's tolerance
+    reference) and "kernel" (the inputs of both GEMMs passed through the same
+    MXFP8 terms the kernels use, outputs rounded to bf16 rows).
+
+MXFP4 codec: OCP MX E2M1 (+-{0, .5, 1, 1.5, 2, 3, 4, 6}), byte = element 2j in the
+low nibble and 2j+1 in the high nibble; E8M0 scale 2^(byte - 127) per 32
+elements along K (glm5_3/sm103/moe/api.py:39-53, route_quant.cuh:1-15).
+Expert MLP: gemm1.cu:6-7 + epilogue :656-1000 (clamped SwiGLU: up in [-L, L],
+gate <= L, h = up * gate * sigmoid(gate)), gemm2.cu:6-7. Combine:
+all_reduce_mhc.py:528-640.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from ctypes import c_float, c_int, c_uint8, c_void_p
+from typing import Optional
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB = os.path.join(HERE, "_build", "liboracle.so")
+REF_LIB = os.path.join(HERE, "_ref", "libref_route.so")
+
+E2M1 = np.array([0, 0.5, 1, 1.5, 2, 3, 4, 6, -0.0, -0.5, -1, -1.5, -2, -3, -4, -6], dtype=np.float32)
+
+_lib = None
+
+
+def build(ref: bool = False) -> None:
+    """Compile the C oracle (and, with ``ref`` and the reference tree present,
+    the reference's route kernels for the CPU)."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    if ref and os.path.isdir("/root/reference"):
+        subprocess.run(["make", "-s", "-C", HERE, "ref"], check=True)
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB) or os.path.getmtime(LIB) < os.path.getmtime(os.path.join(HERE, "mm_oracle.c")):
+            build()
+        h = ctypes.CDLL(LIB)
+        h.or_det_exp.restype = c_float
+        h.or_det_exp.argtypes = [c_float]
+        h.or_sigmoid.restype = c_float
+        h.or_sigmoid.argtypes = [c_float]
+        h.or_e4m3.restype = c_uint8
+        h.or_e4m3.argtypes = [c_float]
+        h.or_route_words.restype = c_int
+        h.or_gate_topk.argtypes = [c_void_p, c_void_p, c_int, c_int, c_int, c_float, c_float, c_int, c_int, c_int,
+                                   c_void_p, c_void_p]
+        _lib = h
+    return _lib
+
+
+def _p(a: Optional[np.ndarray]):
+    return None if a is None else a.ctypes.data_as(c_void_p)
+
+
+# --------------------------------------------------------------------- bit-exact steps
+def router_gemv(x_bf16: np.ndarray, w_bf16: np.ndarray) -> np.ndarray:
+    """x, w as uint16 bf16 bit patterns [T, H], [E, H] -> fp32 logits [T, E]."""
+    x = np.ascontiguousarray(x_bf16, dtype=np.uint16)
+    w = np.ascontiguousarray(w_bf16, dtype=np.uint16)
+    T, H = x.shape
+    E = w.shape[0]
+    out = np.empty((T, E), dtype=np.float32)
+    lib().or_router_gemv(_p(x), _p(w), _p(out), T, E, H)
+    return out
+
+
+def gate_topk(logits: np.ndarray, bias: Optional[np.ndarray], top_k: int, *, score: str = "sigmoid",
+              renormalize: bool = True, scale: float = 1.0, eps: float = 0.0, num_valid: Optional[int] = None):
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    T, E = logits.shape
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+    w = np.empty((T, top_k), dtype=np.float32)
+    ids = np.empty((T, top_k), dtype=np.int32)
+    sf = {"sigmoid": 0, "softmax": 1}[score]
+    lib().or_gate_topk(_p(logits), _p(b), T if num_valid is None else int(num_valid), sf, int(renormalize),
+                       c_float(scale), c_float(eps), T, E, top_k, _p(w), _p(ids))
+    return w, ids
+
+
+def route_words(T: int, K: int, experts: int) -> int:
+    return int(lib().or_route_words(T, K, experts))
+
+
+def route(ids: np.ndarray, experts: int, offset: int = 0):
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    T, K = ids.shape
+    perm = np.empty((T, K), dtype=np.int32)
+    rec = np.empty(route_words(T, K, experts), dtype=np.int32)
+    lib().or_route(_p(ids), _p(perm), _p(rec), T, K, experts, offset)
+    return perm, rec
+
+
+def mxfp8_quant(v: np.ndarray, terms: int = 2):
+    """fp32 [..., K] (K % 32 == 0) -> (q_hi, q_lo, s_hi, s_lo) uint8 arrays."""
+    v = np.ascontiguousarray(v, dtype=np.float32)
+    nb = v.size // 32
+    qh = np.zeros(v.shape, dtype=np.uint8)
+    ql = np.zeros(v.shape, dtype=np.uint8)
+    sh = np.zeros(v.shape[:-1] + (v.shape[-1] // 32,), dtype=np.uint8)
+    sl = np.zeros_like(sh)
+    lib().or_mxfp8_quant(_p(v), nb, terms, _p(qh), _p(ql), _p(sh), _p(sl))
+    return qh, ql, sh, sl
+
+
+def e4m3_table() -> np.ndarray:
+    h = lib()
+    h.or_e4m3_value.restype = c_float
+    h.or_e4m3_value.argtypes = [c_uint8]
+    return np.array([h.or_e4m3_value(i) for i in range(256)], dtype=np.float32)
+
+
+_E4M3 = None
+
+
+def mxfp8_dequant(q: np.ndarray, s: np.ndarray) -> np.ndarray:
+    global _E4M3
+    if _E4M3 is None:
+        _E4M3 = e4m3_table()
+    vals = _E4M3[q]
+    scale = np.exp2(s.astype(np.float32) - 127.0).astype(np.float32)
+    return (vals.reshape(*s.shape, 32) * scale[..., None]).reshape(q.shape)
+
+
+def mxfp8_roundtrip(v: np.ndarray, terms: int = 2) -> np.ndarray:
+    """The value the kernels multiply in place of v: sum of the MXFP8 terms."""
+    qh, ql, sh, sl = mxfp8_quant(v, terms)
+    out = mxfp8_dequant(qh, sh)
+    if terms > 1:
+        out = out + mxfp8_dequant(ql, sl)
+    return out
+
+
+def finalize(rows_bf16: np.ndarray, weights: np.ndarray, permuted: np.ndarray,
+             shared_bf16: Optional[np.ndarray]) -> np.ndarray:
+    rows = np.ascontiguousarray(rows_bf16, dtype=np.uint16)
+    w = np.ascontiguousarray(weights, dtype=np.float32)
+    perm = np.ascontiguousarray(permuted, dtype=np.int32)
+    sh = None if shared_bf16 is None else np.ascontiguousarray(shared_bf16, dtype=np.uint16)
+    T, K = perm.shape
+    H = rows.shape[1]
+    out = np.empty((T, H), dtype=np.uint16)
+    lib().or_finalize(_p(rows), _p(w), _p(perm), _p(sh), _p(out), T, K, H)
+    return out
+
+
+def ref_route_lib() -> Optional[ctypes.CDLL]:
+    """The reference's own route kernels compiled for the CPU (oracle/_ref), or None."""
+    if not os.path.exists(REF_LIB):
+        return None
+    return ctypes.CDLL(REF_LIB)
+
+
+# --------------------------------------------------------------------- codecs / MLP
+def bf16_bits(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def bits_to_f32(b: np.ndarray) -> np.ndarray:
+    return (b.astype(np.uint32) << 16).view(np.float32)
+
+
+def dequant_mxfp4(codes: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    """u8 [..., K/2] codes + u8 [..., K/32] E8M0 -> fp32 [..., K] (exact)."""
+    lut = torch.from_numpy(E2M1)
+    lo = lut[(codes & 0x0F).long()]
+    hi = lut[(codes >> 4).long()]
+    vals = torch.stack([lo, hi], dim=-1).reshape(*codes.shape[:-1], codes.shape[-1] * 2)
+    sc = torch.exp2(scales.float() - 127.0)
+    return (vals.reshape(*scales.shape, 32) * sc[..., None]).reshape(vals.shape)
+
+
+def expert_mlp(x: torch.Tensor, w13: torch.Tensor, s13: torch.Tensor, w2: torch.Tensor, s2: torch.Tensor,
+               clamp: Optional[float], numerics: str, terms: int = 2) -> torch.Tensor:
+    """fp32 [n, H] of one expert on fp32 rows x [n, H] (CPU)."""
+    inter = w13.shape[0] // 2
+    W13 = dequant_mxfp4(w13, s13)
+    xin = x
+    if numerics == "kernel":
+        xin = torch.from_numpy(mxfp8_roundtrip(x.numpy(), terms))
+    gu = xin @ W13.T
+    gate, up = gu[:, :inter], gu[:, inter:]
+    if clamp is not None:
+        up = up.clamp(-clamp, clamp)
+        gate = gate.clamp(max=clamp)
+    h = up * (gate * torch.sigmoid(gate))
+    if numerics == "kernel":
+        h = torch.from_numpy(mxfp8_roundtrip(h.numpy(), terms))
+    W2 = dequant_mxfp4(w2, s2)
+    return h @ W2.T
+
+
+def moe_layer(x_bf16: torch.Tensor, ids: np.ndarray, weights: np.ndarray, layer: dict, *, numerics: str = "exact",
+              terms: int = 2, expert_offset: int = 0, local_experts: Optional[int] = None):
+    """Oracle of one MoE layer given routing. Returns (out fp32 [T, H] before
+    bf16 rounding of the final sum, per-slot rows fp32 {(t, k): [H]}, shared
+    fp32 [T, H] or None). Weights are CPU uint8 tensors in the canonical layout."""
+    x = x_bf16.float()
+    T = x.shape[0]
+    w13, s13, w2, s2 = layer["w13"], layer["w13_scale"], layer["w2"], layer["w2_scale"]
+    E = w13.shape[0] if local_experts is None else local_experts
+    clamp = layer.get("clamp")
+    rows = {}
+    by_expert = {}
+    for t in range(T):
+        for k in range(ids.shape[1]):
+            e = int(ids[t, k]) - expert_offset
+            if 0 <= e < E:
+                by_expert.setdefault(e, []).append((t, k))
+    for e, slots in sorted(by_expert.items()):
+        toks = torch.tensor([t for t, _ in slots])
+        lim = None if clamp is None else float(clamp[e])
+        y = expert_mlp(x[toks], w13[e], s13[e], w2[e], s2[e], lim, numerics, terms)
+        for j, slot in enumerate(slots):
+            rows[slot] = y[j]
+    shared = None
+    if layer.get("shared") is not None:
+        sw = layer["shared"]
+        lim = layer.get("shared_clamp")
+        shared = expert_mlp(x, sw[0][0], sw[1][0], sw[2][0], sw[3][0], lim, numerics, terms)
+    out = torch.zeros_like(x)
+    for (t, k), y in rows.items():
+        out[t] += float(weights[t, k]) * y
+    if shared is not None:
+        out = out + shared
+    return out, rows, shared
+
+
+# --------------------------------------------------------------------- seeded inputs
+def make_layer(H: int, I: int, E: int, *, shared: bool, seed: int, scale_lo: int = 117, scale_hi: int = 121,
+               clamp: Optional[float] = None, generator_device: str = "cpu") -> dict:
+    """Seeded MXFP4 layer (canonical layout): E2M1 codes uniform over the 16
+    nibbles, E8M0 bytes uniform in [scale_lo, scale_hi] (exponents -10..-6)."""
+    g = torch.Generator(device=generator_device).manual_seed(seed)
+
+    def rnd(shape, lo, hi):
+        return torch.randint(lo, hi + 1, shape, dtype=torch.uint8, generator=g, device=generator_device)
+
+    layer = {
+        "w13": rnd((E, 2 * I, H // 2), 0, 255),
+        "w13_scale": rnd((E, 2 * I, H // 32), scale_lo, scale_hi),
+        "w2": rnd((E, H, I // 2), 0, 255),
+        "w2_scale": rnd((E, H, I // 32), scale_lo, scale_hi),
+        "clamp": None if clamp is None else torch.full((E,), float(clamp)),
+        "shared": None,
+    }
+    if shared:
+        layer["shared"] = (rnd((1, 2 * I, H // 2), 0, 255), rnd((1, 2 * I, H // 32), scale_lo, scale_hi),
+                           rnd((1, H, I // 2), 0, 255), rnd((1, H, I // 32), scale_lo, scale_hi))
+    return layer
+
+
+def make_inputs(T: int, H: int, E: int, seed: int, router: bool = True):
+    """x bf16 ~ N(0, 1) [T, H], router weight bf16 ~ N(0, 0.02) [E, H], bias ~ N(0, 0.01)."""
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn((T, H), generator=g).to(torch.bfloat16)
+    w = (torch.randn((E, H), generator=g) * 0.02).to(torch.bfloat16) if router else None
+    bias = (torch.randn((E,), generator=g) * 0.01).float()
+    return x, w, bias
+
+
+def max_abs_rel(got: np.ndarray, ref: np.ndarray) -> float:
+    got = np.asarray(got, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    return float(np.abs(got - ref).max() / max(np.abs(ref).max(), 1e-30))

@@ -1,0 +1,532 @@
+// The C ABI of libmegamoe (include/megamoe.h): validation, layer creation
+// (scale repack, TMA tensor maps, scratch), and the programmatic-dependent-launch
+// chains of the routed-MoE step. Nothing here allocates after mm_layer_create.
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "megamoe.h"
+#include "mm_kernels.cuh"
+#include "mm_layout.cuh"
+#include "mm_ptx.cuh"
+
+using namespace mm;
+
+namespace {
+
+thread_local std::string g_error;
+
+int fail(int code, const char *fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_error = buf;
+  return code;
+}
+
+#define MM_CUDA(call)                                                                      \
+  do {                                                                                     \
+    cudaError_t e_ = (call);                                                               \
+    if (e_ != cudaSuccess)                                                                 \
+      return fail(MM_ERR_CUDA, "%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, \
+                  __LINE__);                                                               \
+  } while (0)
+
+bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Launch with programmatic stream serialization: the kernel may start while its
+// predecessor runs; it reads the predecessor's outputs after griddepcontrol.wait.
+template <typename... KArgs, typename... Args>
+cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, void *stream,
+                   Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int get_encode(EncodeTiledFn *fn) {
+  static EncodeTiledFn cached = nullptr;
+  if (cached == nullptr) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    MM_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    if (p == nullptr || q != cudaDriverEntryPointSuccess)
+      return fail(MM_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    cached = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  *fn = cached;
+  return MM_OK;
+}
+
+// 3-D map of packed E2M1 codes [n][rows][k/2] u8 as {k, rows, n} 4-bit elements,
+// box {128, box_rows, 1}, unpacked to 8-bit slots, 128-byte swizzle.
+int encode_fp4_map(CUtensorMap *map, const void *base, int k, int rows, int n, int box_rows) {
+  EncodeTiledFn enc;
+  int rc = get_encode(&enc);
+  if (rc) return rc;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows),
+                              static_cast<cuuint64_t>(n)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(k) / 2,
+                                 static_cast<cuuint64_t>(k) / 2 * static_cast<cuuint64_t>(rows)};
+  const cuuint32_t box[3] = {128u, static_cast<cuuint32_t>(box_rows), 1u};
+  const cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 3, const_cast<void *>(base), dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MM_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return MM_OK;
+}
+
+}  // namespace
+
+struct mm_layer {
+  mm_layer_desc d;
+  int H, I, E, R, offset, K, Tmax, terms;
+  int m1, m2, ks1, ks2;
+  int max_ctas, rows_cap, shared_row_base, route_words_max, max_segs;
+  int has_shared;
+  int num_sms;
+  uint8_t *sfa13 = nullptr, *sfa2 = nullptr, *ssfa13 = nullptr, *ssfa2 = nullptr;
+  uint8_t *xq = nullptr, *xs = nullptr, *hq = nullptr, *hs = nullptr;
+  int4 *segs = nullptr;
+  int *ctrl = nullptr, *flags = nullptr;
+  uint32_t *err = nullptr;
+  float *logits = nullptr, *weights = nullptr;
+  int *ids = nullptr, *permuted = nullptr, *record = nullptr;
+  ExpertArgs ea;
+};
+
+extern "C" {
+
+const char *mm_last_error(void) { return g_error.c_str(); }
+int mm_version(void) { return 1; }
+
+int64_t mm_route_words(int32_t tokens, int32_t top_k, int32_t experts) {
+  if (tokens < 1 || top_k < 1 || experts < 1) return 0;
+  return route_words(tokens, top_k, experts);
+}
+
+int mm_router_gemv(const uint16_t *x, const uint16_t *w, float *logits, int32_t tokens,
+                   int32_t experts, int32_t hidden, void *stream) {
+  if (!x || !w || !logits) return fail(MM_ERR_INVALID, "mm_router_gemv: null pointer");
+  if (tokens < 1 || experts < 1 || hidden < 1024 || hidden % 1024)
+    return fail(MM_ERR_INVALID, "mm_router_gemv: tokens %d experts %d hidden %d (hidden %% 1024 == 0)",
+                tokens, experts, hidden);
+  if (!aligned(x, 16) || !aligned(w, 16)) return fail(MM_ERR_INVALID, "mm_router_gemv: x and w must be 16-byte aligned");
+  dim3 grid(experts, (tokens + 7) / 8);
+  MM_CUDA(launch(router_gemv_kernel, grid, dim3(128), 0, stream, x, w, logits, tokens, experts, hidden));
+  return MM_OK;
+}
+
+static int check_gate(const mm_gate_args *a, int tokens, int E, int K) {
+  if (!a || !a->logits || !a->weights || !a->ids) return fail(MM_ERR_INVALID, "gate: null pointer");
+  if (tokens < 1 || tokens > kMaxTokens) return fail(MM_ERR_INVALID, "gate: tokens %d outside 1..%d", tokens, kMaxTokens);
+  if (E < 1 || E > kMaxRouterExperts) return fail(MM_ERR_INVALID, "gate: %d experts outside 1..%d", E, kMaxRouterExperts);
+  if (K < 1 || K > kMaxTopK || K > E) return fail(MM_ERR_INVALID, "gate: top_k %d outside 1..min(16, experts)", K);
+  if (a->score_func != MM_SCORE_SIGMOID && a->score_func != MM_SCORE_SOFTMAX)
+    return fail(MM_ERR_UNSUPPORTED, "gate: score function %d is not built (sigmoid, softmax)", a->score_func);
+  return MM_OK;
+}
+
+static GateArgs gate_args(const mm_gate_args *a, int E, int K) {
+  GateArgs g;
+  g.logits = a->logits;
+  g.bias = a->bias;
+  g.num_valid = a->num_valid;
+  g.score_func = a->score_func;
+  g.renormalize = a->renormalize;
+  g.routed_scaling = a->routed_scaling;
+  g.renorm_eps = a->renorm_eps;
+  g.router_experts = E;
+  g.top_k = K;
+  g.weights_out = a->weights;
+  g.ids_out = a->ids;
+  return g;
+}
+
+int mm_gate_topk(const mm_gate_args *args, int32_t tokens, int32_t router_experts, int32_t top_k,
+                 void *stream) {
+  int rc = check_gate(args, tokens, router_experts, top_k);
+  if (rc) return rc;
+  MM_CUDA(launch(gate_topk_kernel, dim3(tokens), dim3(512), 0, stream, gate_args(args, router_experts, top_k)));
+  return MM_OK;
+}
+
+static size_t route_smem_bytes(int tokens, int experts) {
+  const int words = (tokens + 31) / 32;
+  return static_cast<size_t>(experts) * words * 4 + static_cast<size_t>(experts) * 4 * 3 + 32 * 4;
+}
+
+int mm_route(const int32_t *ids, int32_t *permuted, int32_t *record, int32_t tokens, int32_t top_k,
+             int32_t experts, int32_t expert_offset, void *stream) {
+  if (!ids || !permuted || !record) return fail(MM_ERR_INVALID, "mm_route: null pointer");
+  if (tokens < 1 || tokens > kMaxTokens) return fail(MM_ERR_INVALID, "mm_route: tokens %d outside 1..%d", tokens, kMaxTokens);
+  if (top_k < 1 || top_k > kMaxTopK) return fail(MM_ERR_INVALID, "mm_route: top_k %d outside 1..%d", top_k, kMaxTopK);
+  if (experts < 1 || experts > kMaxRouterExperts) return fail(MM_ERR_INVALID, "mm_route: %d experts outside 1..%d", experts, kMaxRouterExperts);
+  if (expert_offset < 0) return fail(MM_ERR_UNSUPPORTED, "mm_route: balanced dealing (negative expert_offset) is not built");
+  RouteArgs r = {};
+  r.ids = ids;
+  r.permuted = permuted;
+  r.record = record;
+  r.tokens = tokens;
+  r.top_k = top_k;
+  r.experts = experts;
+  r.expert_offset = expert_offset;
+  const size_t smem = route_smem_bytes(tokens, experts);
+  MM_CUDA(cudaFuncSetAttribute(route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+  MM_CUDA(launch(route_kernel, dim3(1), dim3(512), smem, stream, r));
+  return MM_OK;
+}
+
+int mm_finalize(const uint16_t *rows, const float *weights, const int32_t *permuted,
+                const uint16_t *shared_rows, uint16_t *out, float *partial, int32_t tokens,
+                int32_t top_k, int32_t hidden, void *stream) {
+  if (!rows || !weights || !permuted || (!out && !partial)) return fail(MM_ERR_INVALID, "mm_finalize: null pointer");
+  if (tokens < 1 || top_k < 1 || hidden < 8 || hidden % 8) return fail(MM_ERR_INVALID, "mm_finalize: bad sizes");
+  if (!aligned(rows, 16) || (shared_rows && !aligned(shared_rows, 16)) || (out && !aligned(out, 16)) ||
+      (partial && !aligned(partial, 16)))
+    return fail(MM_ERR_INVALID, "mm_finalize: buffers must be 16-byte aligned");
+  FinalizeArgs a = {rows, weights, permuted, shared_rows, out, partial, tokens, top_k, hidden};
+  dim3 grid(tokens, (hidden + 2047) / 2048);
+  MM_CUDA(launch(finalize_kernel, grid, dim3(256), 0, stream, a));
+  return MM_OK;
+}
+
+int mm_finalize_partial(const float *partial, uint16_t *out, int32_t tokens, int32_t hidden, void *stream) {
+  if (!partial || !out || tokens < 1 || hidden < 1) return fail(MM_ERR_INVALID, "mm_finalize_partial: bad arguments");
+  const size_t n = static_cast<size_t>(tokens) * hidden;
+  const int blocks = static_cast<int>((n + 255) / 256 < 1184 ? (n + 255) / 256 : 1184);
+  MM_CUDA(launch(finalize_partial_kernel, dim3(blocks), dim3(256), 0, stream, partial, out, tokens, hidden));
+  return MM_OK;
+}
+
+// ---------------------------------------------------------------------------
+static void free_layer(mm_layer *L) {
+  if (!L) return;
+  void *ptrs[] = {L->sfa13, L->sfa2, L->ssfa13, L->ssfa2, L->xq, L->xs, L->hq, L->hs, L->segs,
+                  L->ctrl, L->flags, L->err, L->logits, L->weights, L->ids, L->permuted, L->record};
+  for (void *p : ptrs)
+    if (p) cudaFree(p);
+  delete L;
+}
+
+static int check_weights(const mm_expert_weights &w, const char *what) {
+  if (!w.w13 || !w.w13_scale || !w.w2 || !w.w2_scale) return fail(MM_ERR_INVALID, "%s: null weight pointer", what);
+  if (!aligned(w.w13, 32) || !aligned(w.w2, 32))
+    return fail(MM_ERR_INVALID, "%s: packed weights must be 32-byte aligned", what);
+  return MM_OK;
+}
+
+int mm_layer_create(const mm_layer_desc *desc, mm_layer **out) {
+  if (!desc || !out) return fail(MM_ERR_INVALID, "mm_layer_create: null pointer");
+  *out = nullptr;
+  const mm_layer_desc &d = *desc;
+  if (d.hidden < 256 || d.hidden % 256) return fail(MM_ERR_INVALID, "hidden %d must be a positive multiple of 256", d.hidden);
+  if (d.intermediate < 256 || d.intermediate % 256)
+    return fail(MM_ERR_INVALID, "intermediate %d must be a positive multiple of 256", d.intermediate);
+  if (d.experts < 1 || d.experts > kMaxRouterExperts) return fail(MM_ERR_INVALID, "experts %d outside 1..%d", d.experts, kMaxRouterExperts);
+  if (d.router_experts < d.experts || d.router_experts > kMaxRouterExperts)
+    return fail(MM_ERR_INVALID, "router_experts %d outside experts..%d", d.router_experts, kMaxRouterExperts);
+  if (d.expert_offset < 0 || d.expert_offset + d.experts > d.router_experts)
+    return fail(MM_ERR_INVALID, "local experts [%d, %d) outside the router's %d", d.expert_offset,
+                d.expert_offset + d.experts, d.router_experts);
+  if (d.top_k < 1 || d.top_k > kMaxTopK) return fail(MM_ERR_INVALID, "top_k %d outside 1..%d", d.top_k, kMaxTopK);
+  if (d.max_tokens < 1 || d.max_tokens > kMaxTokens) return fail(MM_ERR_INVALID, "max_tokens %d outside 1..%d", d.max_tokens, kMaxTokens);
+  if (d.weight_format != MM_WEIGHT_MXFP4) return fail(MM_ERR_UNSUPPORTED, "weight format %d is not built (MXFP4)", d.weight_format);
+  if (d.act_terms != 1 && d.act_terms != 2) return fail(MM_ERR_INVALID, "act_terms %d must be 1 or 2", d.act_terms);
+  int rc = check_weights(d.routed, "routed");
+  if (rc) return rc;
+  const int has_shared = d.shared.w13 != nullptr;
+  if (has_shared && (rc = check_weights(d.shared, "shared"))) return rc;
+
+  MM_CUDA(cudaSetDevice(d.device));
+  mm_layer *L = new mm_layer();
+  L->d = d;
+  L->H = d.hidden;
+  L->I = d.intermediate;
+  L->E = d.experts;
+  L->R = d.router_experts;
+  L->offset = d.expert_offset;
+  L->K = d.top_k;
+  L->Tmax = d.max_tokens;
+  L->terms = d.act_terms;
+  L->has_shared = has_shared;
+  L->m1 = L->I / 64;
+  L->m2 = L->H / 128;
+  L->ks1 = L->H / kStageK;
+  L->ks2 = L->I / kStageK;
+  L->max_ctas = route_max_ctas(L->Tmax, L->K, L->E);
+  L->shared_row_base = kTile * L->max_ctas;
+  L->rows_cap = L->shared_row_base + L->Tmax;
+  L->route_words_max = route_words(L->Tmax, L->K, L->E);
+  L->max_segs = L->max_ctas + (L->Tmax + kSegRows - 1) / kSegRows + 1;
+  int dev_sms = 0;
+  cudaError_t ce = cudaDeviceGetAttribute(&dev_sms, cudaDevAttrMultiProcessorCount, d.device);
+  if (ce != cudaSuccess) {
+    free_layer(L);
+    return fail(MM_ERR_CUDA, "cudaDeviceGetAttribute: %s", cudaGetErrorString(ce));
+  }
+  L->num_sms = dev_sms;
+
+#define ALLOC(ptr, bytes)                                                                \
+  do {                                                                                   \
+    cudaError_t e_ = cudaMalloc(reinterpret_cast<void **>(&(ptr)), (bytes));             \
+    if (e_ != cudaSuccess) {                                                             \
+      free_layer(L);                                                                     \
+      return fail(MM_ERR_CUDA, "cudaMalloc(%zu): %s", static_cast<size_t>(bytes), cudaGetErrorString(e_)); \
+    }                                                                                    \
+  } while (0)
+
+  const size_t E = L->E, H = L->H, I = L->I;
+  const size_t sfa13_bytes = E * L->m1 * L->ks1 * 1024;
+  const size_t sfa2_bytes = E * L->m2 * L->ks2 * 1024;
+  ALLOC(L->sfa13, sfa13_bytes);
+  ALLOC(L->sfa2, sfa2_bytes);
+  if (has_shared) {
+    ALLOC(L->ssfa13, static_cast<size_t>(L->m1) * L->ks1 * 1024);
+    ALLOC(L->ssfa2, static_cast<size_t>(L->m2) * L->ks2 * 1024);
+  }
+  ALLOC(L->xq, 2 * static_cast<size_t>(L->Tmax) * H);
+  ALLOC(L->xs, 2 * static_cast<size_t>(L->Tmax) * H / 32);
+  ALLOC(L->hq, 2 * static_cast<size_t>(L->rows_cap) * I);
+  ALLOC(L->hs, 2 * static_cast<size_t>(L->rows_cap) * I / 32);
+  ALLOC(L->segs, sizeof(int4) * L->max_segs);
+  ALLOC(L->ctrl, sizeof(int) * kCtrlWords);
+  ALLOC(L->flags, sizeof(int) * L->max_segs);
+  ALLOC(L->err, sizeof(uint32_t));
+  ALLOC(L->logits, sizeof(float) * L->Tmax * L->R);
+  ALLOC(L->weights, sizeof(float) * L->Tmax * L->K);
+  ALLOC(L->ids, sizeof(int) * L->Tmax * L->K);
+  ALLOC(L->permuted, sizeof(int) * L->Tmax * L->K);
+  ALLOC(L->record, sizeof(int) * L->route_words_max);
+#undef ALLOC
+  ce = cudaMemset(L->ctrl, 0, sizeof(int) * kCtrlWords);
+  if (ce == cudaSuccess) ce = cudaMemset(L->err, 0, sizeof(uint32_t));
+  if (ce == cudaSuccess) ce = cudaMemset(L->hq, 0, 2 * static_cast<size_t>(L->rows_cap) * I);
+  if (ce == cudaSuccess) ce = cudaMemset(L->hs, 0, 2 * static_cast<size_t>(L->rows_cap) * I / 32);
+  if (ce == cudaSuccess) ce = cudaMemset(L->xq, 0, 2 * static_cast<size_t>(L->Tmax) * H);
+  if (ce == cudaSuccess) ce = cudaMemset(L->xs, 0, 2 * static_cast<size_t>(L->Tmax) * H / 32);
+  if (ce != cudaSuccess) {
+    free_layer(L);
+    return fail(MM_ERR_CUDA, "cudaMemset: %s", cudaGetErrorString(ce));
+  }
+
+  // scale repack (once): canonical E8M0 -> UMMA scale chunks
+  auto repack = [&](const void *src, uint8_t *dst, int n, int rows, int k, int gate_up) -> int {
+    const size_t total = static_cast<size_t>(n) * (rows / 128) * (k / kStageK) * 1024;
+    const int blocks = static_cast<int>(total / 256 < 65536 ? (total + 255) / 256 : 65536);
+    repack_scales_kernel<<<blocks, 256>>>(static_cast<const uint8_t *>(src), dst, n, rows, k, gate_up, L->I);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(MM_ERR_CUDA, "repack_scales_kernel: %s", cudaGetErrorString(e));
+    return MM_OK;
+  };
+  if ((rc = repack(d.routed.w13_scale, L->sfa13, L->E, 2 * L->I, L->H, 1)) ||
+      (rc = repack(d.routed.w2_scale, L->sfa2, L->E, L->H, L->I, 0)) ||
+      (has_shared && (rc = repack(d.shared.w13_scale, L->ssfa13, 1, 2 * L->I, L->H, 1))) ||
+      (has_shared && (rc = repack(d.shared.w2_scale, L->ssfa2, 1, L->H, L->I, 0)))) {
+    free_layer(L);
+    return rc;
+  }
+  ce = cudaDeviceSynchronize();
+  if (ce != cudaSuccess) {
+    free_layer(L);
+    return fail(MM_ERR_CUDA, "scale repack: %s", cudaGetErrorString(ce));
+  }
+
+  ExpertArgs &ea = L->ea;
+  memset(&ea, 0, sizeof(ea));
+  const mm_expert_weights &sw = has_shared ? d.shared : d.routed;  // placeholder maps when no shared
+  if ((rc = encode_fp4_map(&ea.w13_map, d.routed.w13, L->H, 2 * L->I, L->E, 64)) ||
+      (rc = encode_fp4_map(&ea.w2_map, d.routed.w2, L->I, L->H, L->E, 128)) ||
+      (rc = encode_fp4_map(&ea.sw13_map, sw.w13, L->H, 2 * L->I, 1, 64)) ||
+      (rc = encode_fp4_map(&ea.sw2_map, sw.w2, L->I, L->H, 1, 128))) {
+    free_layer(L);
+    return rc;
+  }
+  ea.sfa13 = L->sfa13;
+  ea.sfa2 = L->sfa2;
+  ea.ssfa13 = has_shared ? L->ssfa13 : L->sfa13;
+  ea.ssfa2 = has_shared ? L->ssfa2 : L->sfa2;
+  ea.xq = L->xq;
+  ea.xs = L->xs;
+  ea.hq = L->hq;
+  ea.hs = L->hs;
+  ea.segs = L->segs;
+  ea.ctrl = L->ctrl;
+  ea.flags = L->flags;
+  ea.err = L->err;
+  ea.clamp = d.clamp;
+  ea.shared_clamp = d.shared_clamp;
+  ea.hidden = L->H;
+  ea.inter = L->I;
+  ea.max_tokens = L->Tmax;
+  ea.rows_cap = L->rows_cap;
+  ea.terms = L->terms;
+  ea.m1 = L->m1;
+  ea.m2 = L->m2;
+  ea.ks1 = L->ks1;
+  ea.ks2 = L->ks2;
+
+  ce = cudaFuncSetAttribute(expert_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc);
+  if (ce == cudaSuccess)
+    ce = cudaFuncSetAttribute(front_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(route_smem_bytes(kMaxTokens, kMaxRouterExperts)));
+  if (ce != cudaSuccess) {
+    free_layer(L);
+    return fail(MM_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(ce));
+  }
+  *out = L;
+  return MM_OK;
+}
+
+int mm_layer_destroy(mm_layer *layer) {
+  if (!layer) return MM_OK;
+  cudaSetDevice(layer->d.device);
+  free_layer(layer);
+  return MM_OK;
+}
+
+int mm_layer_get_info(const mm_layer *L, mm_layer_info *info) {
+  if (!L || !info) return fail(MM_ERR_INVALID, "mm_layer_get_info: null pointer");
+  info->hidden = L->H;
+  info->intermediate = L->I;
+  info->experts = L->E;
+  info->router_experts = L->R;
+  info->expert_offset = L->offset;
+  info->top_k = L->K;
+  info->max_tokens = L->Tmax;
+  info->has_shared = L->has_shared;
+  info->rows_capacity = L->rows_cap;
+  info->shared_row_base = L->shared_row_base;
+  info->route_words = L->route_words_max;
+  info->weight_bytes = 3LL * L->H * L->I / 2 + 3LL * L->H * L->I / 32;
+  return MM_OK;
+}
+
+// front (gate or given ids) + experts
+static int run_front_and_experts(mm_layer *L, const uint16_t *x, const mm_gate_args *gate,
+                                 const int32_t *ids, int tokens, int32_t *permuted, int32_t *record,
+                                 uint16_t *rows, void *stream) {
+  if (!x || !permuted || !record || !rows) return fail(MM_ERR_INVALID, "layer call: null pointer");
+  if (tokens < 1 || tokens > L->Tmax) return fail(MM_ERR_INVALID, "tokens %d outside 1..%d", tokens, L->Tmax);
+  if (!aligned(x, 16) || !aligned(rows, 16)) return fail(MM_ERR_INVALID, "x and rows must be 16-byte aligned");
+  FrontArgs f = {};
+  if (gate) {
+    int rc = check_gate(gate, tokens, L->R, L->K);
+    if (rc) return rc;
+    f.gate = gate_args(gate, L->R, L->K);
+    f.route.ids = gate->ids;
+  } else {
+    if (!ids) return fail(MM_ERR_INVALID, "layer call: null ids");
+    f.gate.logits = nullptr;
+    f.route.ids = ids;
+  }
+  f.route.permuted = permuted;
+  f.route.record = record;
+  f.route.tokens = tokens;
+  f.route.top_k = L->K;
+  f.route.experts = L->E;
+  f.route.expert_offset = L->offset;
+  f.route.segs = L->segs;
+  f.route.ctrl = L->ctrl;
+  f.route.flags = L->flags;
+  f.route.has_shared = L->has_shared;
+  f.route.shared_row_base = L->shared_row_base;
+  f.route.m1 = L->m1;
+  f.route.m2 = L->m2;
+  f.x = x;
+  f.xq = L->xq;
+  f.xs = L->xs;
+  f.hidden = L->H;
+  f.max_tokens = L->Tmax;
+  f.terms = L->terms;
+  MM_CUDA(cudaSetDevice(L->d.device));
+  MM_CUDA(launch(front_kernel, dim3(tokens), dim3(512), route_smem_bytes(tokens, L->E), stream, f));
+  ExpertArgs ea = L->ea;
+  ea.rows_out = rows;
+  ea.record = record;
+  ea.token_off = 4 + 2 * route_cta_words(route_max_ctas(tokens, L->K, L->E));
+  MM_CUDA(launch(expert_kernel, dim3(L->num_sms), dim3(kExpertThreads), kSmemAlloc, stream, ea));
+  return MM_OK;
+}
+
+int mm_layer_experts(mm_layer *L, const uint16_t *x, const int32_t *ids, int32_t tokens,
+                     int32_t *permuted, int32_t *record, uint16_t *rows, void *stream) {
+  if (!L) return fail(MM_ERR_INVALID, "null layer");
+  return run_front_and_experts(L, x, nullptr, ids, tokens, permuted, record, rows, stream);
+}
+
+int mm_layer_gate_experts(mm_layer *L, const uint16_t *x, const mm_gate_args *gate, int32_t tokens,
+                          int32_t *permuted, int32_t *record, uint16_t *rows, void *stream) {
+  if (!L || !gate) return fail(MM_ERR_INVALID, "null layer or gate arguments");
+  return run_front_and_experts(L, x, gate, nullptr, tokens, permuted, record, rows, stream);
+}
+
+int mm_layer_forward(mm_layer *L, const mm_forward_args *a, void *stream) {
+  if (!L || !a) return fail(MM_ERR_INVALID, "mm_layer_forward: null pointer");
+  const int T = a->tokens;
+  if (T < 1 || T > L->Tmax) return fail(MM_ERR_INVALID, "tokens %d outside 1..%d", T, L->Tmax);
+  const float *logits = a->logits;
+  if (a->router_w) {
+    float *lo = a->logits_out ? a->logits_out : L->logits;
+    int rc = mm_router_gemv(a->x, a->router_w, lo, T, L->R, L->H, stream);
+    if (rc) return rc;
+    logits = lo;
+  }
+  if (!logits) return fail(MM_ERR_INVALID, "mm_layer_forward: neither router_w nor logits");
+  mm_gate_args g = {};
+  g.logits = logits;
+  g.bias = a->bias;
+  g.num_valid = a->num_valid;
+  g.score_func = a->score_func;
+  g.renormalize = a->renormalize;
+  g.routed_scaling = a->routed_scaling;
+  g.renorm_eps = a->renorm_eps;
+  g.weights = a->weights ? a->weights : L->weights;
+  g.ids = a->ids ? a->ids : L->ids;
+  int32_t *perm = a->permuted ? a->permuted : L->permuted;
+  int32_t *rec = a->record ? a->record : L->record;
+  if (!a->rows) return fail(MM_ERR_INVALID, "mm_layer_forward: null rows buffer");
+  int rc = run_front_and_experts(L, a->x, &g, nullptr, T, perm, rec, a->rows, stream);
+  if (rc) return rc;
+  if (a->out || a->partial) {
+    const uint16_t *shared = L->has_shared ? a->rows + static_cast<size_t>(L->shared_row_base) * L->H : nullptr;
+    rc = mm_finalize(a->rows, g.weights, perm, shared, a->out, a->partial, T, L->K, L->H, stream);
+    if (rc) return rc;
+  }
+  return MM_OK;
+}
+
+int mm_layer_check(mm_layer *L) {
+  if (!L) return fail(MM_ERR_INVALID, "null layer");
+  MM_CUDA(cudaSetDevice(L->d.device));
+  MM_CUDA(cudaDeviceSynchronize());
+  uint32_t word = 0;
+  MM_CUDA(cudaMemcpy(&word, L->err, sizeof(word), cudaMemcpyDeviceToHost));
+  if (word == 0) return MM_OK;
+  MM_CUDA(cudaMemset(L->err, 0, sizeof(uint32_t)));
+  if (word & kErrTimeoutMask) return fail(MM_ERR_DEVICE_TIMEOUT, "device wait timed out (error word 0x%x)", word);
+  return fail(MM_ERR_DEVICE, "device check failed (error word 0x%x)", word);
+}
+
+}  // extern "C"

@@ -1,0 +1,494 @@
+// The persistent expert kernel (K2 + K3): every routed expert's gate_up GEMM
+// with the SwiGLU (+ clamp) and MXFP8 requant epilogue, then every expert's down
+// GEMM, in one launch of one CTA per SM.
+//
+// Work: a segment is up to 16 consecutive permuted rows of one expert (the
+// shared expert's tokens form segments too). A gate_up unit streams one 128-row
+// tile of w13 (64 gate rows + the 64 matching up rows) through all of H and
+// multiplies it with the segment's rows; a down unit streams one 128-row tile of
+// w2 through all of I. Units are claimed from a global counter in the order
+// [all gate_up units][all down units], so every gate_up unit is claimed before
+// any down unit; a down unit's activations wait on its segment's mailbox (the
+// number of finished gate_up tiles), while its weights stream before that wait.
+// Reference semantics: gemm1.cu:6-7 (h = MXFP8(clamped SwiGLU(x W13^T))),
+// gemm2.cu:6-7 (rows = h W2^T in bf16, deferred-finalize rows).
+//
+// Warp roles (224 threads):
+//   warp 0    producer: claims units, TMA-loads w tiles (E2M1 unpacked to 8-bit
+//             slots by the 16U4_ALIGN16B tensor map) and bulk-loads the scale chunks;
+//   warp 1    MMA: TMEM owner; copies scale chunks to TMEM (tcgen05.cp) and issues
+//             tcgen05.mma kind::mxf8f6f4.block_scale, M = 128, N = rows (8/16), K = 32;
+//   warp 2    B loader: gathers the segment's MXFP8 activation rows (hi, lo) with
+//             cp.async into the 128-byte-swizzled K-major layout;
+//   warps 3-6 epilogue: TMEM -> registers; SwiGLU + requant (gate_up) or bf16 rows
+//             (down).
+// No TMA multicast is used anywhere (one CTA per cluster).
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "mm_kernels.cuh"
+#include "mm_layout.cuh"
+#include "mm_numerics.cuh"
+#include "mm_ptx.cuh"
+
+namespace mm {
+
+namespace {
+
+constexpr uint32_t kATxBytes = 128 * kStageK / 2;  // packed E2M1 bytes of one stage
+
+__device__ __forceinline__ void decode_unit(int u, int nseg, int m1, int m2, bool &g2, int &seg,
+                                            int &m) {
+  const int n1 = nseg * m1;
+  if (u < n1) {
+    g2 = false;
+    seg = u / m1;
+    m = u - seg * m1;
+  } else {
+    g2 = true;
+    const int v = u - n1;
+    seg = v / m2;
+    m = v - seg * m2;
+  }
+}
+
+__device__ __forceinline__ int ld_acquire(const int *p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ int ld_shared_volatile(const int *p) {
+  return *reinterpret_cast<const volatile int *>(p);
+}
+
+// Wait until `flag` >= target; false (and the error word set) on timeout.
+__device__ bool wait_flag(const int *flag, int target, uint32_t *err) {
+  if (ld_acquire(flag) >= target) return true;
+  const uint64_t t0 = globaltimer();
+#pragma unroll 1
+  for (uint32_t i = 0;; ++i) {
+    __nanosleep(64);
+    if (ld_acquire(flag) >= target) return true;
+    if ((i & 15u) == 0u) {
+      if (error_set(err)) return false;
+      if (globaltimer() - t0 > kWaitBudgetNs) {
+        error_raise(err, kErrTimeoutFlag);
+        return false;
+      }
+    }
+  }
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kExpertThreads, 1) expert_kernel(const __grid_constant__ ExpertArgs p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  unsigned char *sbase = smem_raw + (base - raw);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t bars = base + kSmemBar;
+  auto bar = [&](int i) -> uint32_t { return bars + 8u * static_cast<uint32_t>(i); };
+  int *work_ids = reinterpret_cast<int *>(sbase + kSmemWorkIds);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sbase + kSmemTmemBase);
+  uint32_t *err = p.err;
+
+  pdl_launch_dependents();
+
+  // ---- set-up ----------------------------------------------------------------
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(bar(kBarFull + s), 1 + 32);  // producer's expect_tx + 32 loader lanes
+      mbar_init(bar(kBarEmpty + s), 1);      // MMA commit
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(bar(kBarAccFull + a), 1);
+      mbar_init(bar(kBarAccEmpty + a), 4);
+    }
+    for (int w = 0; w < kWorkSlots; ++w) {
+      mbar_init(bar(kBarWorkFull + w), 1);
+      mbar_init(bar(kBarWorkEmpty + w), 6);
+    }
+    mbar_init(bar(kBarDrain), 1);
+    mbar_init(bar(kBarExFull), 2);  // the two up-row warps
+    mbar_init(bar(kBarExFree), 2);  // the two gate-row warps
+    fence_barrier_init();
+  }
+  {  // zero the activation and B-scale areas once: rows a unit does not load stay finite
+    uint4 *z = reinterpret_cast<uint4 *>(sbase + kSmemB);
+    const int n16 = (kSmemEpi - kSmemB) / 16;
+    for (int i = threadIdx.x; i < n16; i += blockDim.x) z[i] = make_uint4(0u, 0u, 0u, 0u);
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *reinterpret_cast<volatile uint32_t *>(tmem_slot);
+
+  if (warp == 0) {
+    // =========================== producer ===================================
+    if (lane == 0) {
+      tma_prefetch_desc(&p.w13_map);
+      tma_prefetch_desc(&p.w2_map);
+      tma_prefetch_desc(&p.sw13_map);
+      tma_prefetch_desc(&p.sw2_map);
+      pdl_wait();
+      const int nseg = p.ctrl[kCtrlSegments];
+      const int total = p.ctrl[kCtrlUnits];
+      const uint64_t policy = policy_evict_first();
+      uint32_t stage = 0, phase = 0, ws = 0, wphase = 0;
+      int next = atomicAdd(&p.ctrl[kCtrlClaim], 1);
+      bool ok = true;
+#pragma unroll 1
+      while (ok) {
+        const int u = next;
+        const bool have = u < total;
+        if (have) next = atomicAdd(&p.ctrl[kCtrlClaim], 1);  // claim ahead
+        if (!mbar_wait(bar(kBarWorkEmpty + ws), wphase ^ 1u, err, kErrTimeoutWork)) break;
+        work_ids[ws] = have ? u : -1;
+        mbar_arrive(bar(kBarWorkFull + ws));
+        if (++ws == kWorkSlots) { ws = 0; wphase ^= 1u; }
+        if (!have) break;
+        bool g2;
+        int seg, m;
+        decode_unit(u, nseg, p.m1, p.m2, g2, seg, m);
+        const int4 sg = p.segs[seg];
+        const int e = sg.x < 0 ? 0 : sg.x;
+        const bool sh = sg.x < 0;
+        const CUtensorMap *map = g2 ? (sh ? &p.sw2_map : &p.w2_map) : (sh ? &p.sw13_map : &p.w13_map);
+        const int ks_n = g2 ? p.ks2 : p.ks1;
+        const uint8_t *sfa = g2 ? (sh ? p.ssfa2 : p.sfa2) : (sh ? p.ssfa13 : p.sfa13);
+        sfa += (static_cast<size_t>(e) * (g2 ? p.m2 : p.m1) + m) * static_cast<size_t>(ks_n) * 1024u;
+#pragma unroll 1
+        for (int ks = 0; ks < ks_n; ++ks) {
+          if (!mbar_wait(bar(kBarEmpty + stage), phase ^ 1u, err, kErrTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          const uint32_t full = bar(kBarFull + stage);
+          mbar_expect_tx(full, kATxBytes + kSfaStageBytes);
+          const uint32_t sa = base + kSmemA + stage * kAStageBytes;
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const int x = ks * kStageK + c * 128;
+            if (!g2) {
+              tma_load_3d(sa + c * kAChunkBytes, map, x, 64 * m, e, full, policy);
+              tma_load_3d(sa + c * kAChunkBytes + 64 * 128, map, x, p.inter + 64 * m, e, full, policy);
+            } else {
+              tma_load_3d(sa + c * kAChunkBytes, map, x, 128 * m, e, full, policy);
+            }
+          }
+          bulk_load(base + kSmemSfa + stage * kSfaStageBytes, sfa + static_cast<size_t>(ks) * 1024u,
+                    kSfaStageBytes, full, policy);
+          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        }
+      }
+      // drain: every stage filled so far has been consumed, so no copy is in flight
+      for (int i = 0; i < kStages; ++i) {
+        mbar_wait(bar(kBarEmpty + stage), phase ^ 1u, err, kErrTimeoutEmpty);
+        if (++stage == kStages) { stage = 0; phase ^= 1u; }
+      }
+    }
+  } else if (warp == 1) {
+    // ============================== MMA =====================================
+    if (lane == 0) {
+      pdl_wait();
+      const int nseg = p.ctrl[kCtrlSegments];
+      uint32_t stage = 0, phase = 0, ws = 0, wphase = 0, acc = 0, acc_phase = 0;
+#pragma unroll 1
+      while (true) {
+        if (!mbar_wait(bar(kBarWorkFull + ws), wphase, err, kErrTimeoutWork)) break;
+        const int u = ld_shared_volatile(work_ids + ws);
+        mbar_arrive(bar(kBarWorkEmpty + ws));
+        if (++ws == kWorkSlots) { ws = 0; wphase ^= 1u; }
+        if (u < 0) break;
+        bool g2;
+        int seg, m;
+        decode_unit(u, nseg, p.m1, p.m2, g2, seg, m);
+        const int4 sg = p.segs[seg];
+        const uint32_t n = static_cast<uint32_t>((sg.z + 7) & ~7);
+        const int ks_n = g2 ? p.ks2 : p.ks1;
+        if (!mbar_wait(bar(kBarAccEmpty + acc), acc_phase ^ 1u, err, kErrTimeoutAcc)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tbase + kTmemAcc + acc * kSegRows;
+        bool ok = true;
+#pragma unroll 1
+        for (int ks = 0; ks < ks_n; ++ks) {
+          if (!mbar_wait(bar(kBarFull + stage), phase, err, kErrTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          fence_proxy_async_smem();  // activation rows and B scales arrived via cp.async
+          const uint32_t sfa_t = tbase + kTmemSfa + stage * 8;
+          const uint32_t sfb_t = tbase + kTmemSfb + stage * 16;
+          const uint32_t sfa_s = base + kSmemSfa + stage * kSfaStageBytes;
+          const uint32_t sfb_s = base + kSmemSfb + stage * kSfbStageBytes;
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            tc_cp_32x128b_warpx4(sfa_t + 4 * c, smem_desc(sfa_s + 512 * c, 0, 128, kLayoutNone));
+            for (int t = 0; t < p.terms; ++t)
+              tc_cp_32x128b_warpx4(sfb_t + 8 * t + 4 * c,
+                                   smem_desc(sfb_s + kSfbTermBytes * t + 512 * c, 0, 128, kLayoutNone));
+          }
+          const uint32_t sa = base + kSmemA + stage * kAStageBytes;
+          const uint32_t sb = base + kSmemB + stage * kBStageBytes;
+#pragma unroll
+          for (int kk = 0; kk < kStageK / 32; ++kk) {
+            const uint32_t c = kk >> 2, j = kk & 3;
+            const uint64_t adesc = smem_desc(sa + c * kAChunkBytes + j * 32, 0, 1024, kLayoutSw128);
+            const uint32_t idesc = idesc_mxf4_e4m3(n, j, j);
+            for (int t = 0; t < p.terms; ++t) {
+              const uint64_t bdesc =
+                  smem_desc(sb + t * kBTermBytes + c * kBChunkBytes + j * 32, 0, 1024, kLayoutSw128);
+              tc_mma_mxf8f6f4(d_tmem, adesc, bdesc, idesc, sfa_t + 4 * c, sfb_t + 8 * t + 4 * c,
+                              (ks | kk | t) != 0 ? 1u : 0u);
+            }
+          }
+          tc_commit(bar(kBarEmpty + stage));
+          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        tc_commit(bar(kBarAccFull + acc));
+        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      }
+      // every tcgen05 operation issued above has completed before teardown
+      tc_commit(bar(kBarDrain));
+      mbar_wait(bar(kBarDrain), 0, err, kErrTimeoutAcc);
+    }
+  } else if (warp == 2) {
+    // ============================ B loader ===================================
+    pdl_wait();
+    const int nseg = p.ctrl[kCtrlSegments];
+    uint32_t stage = 0, phase = 0, ws = 0, wphase = 0;
+#pragma unroll 1
+    while (true) {
+      int u = -1, okw = 1;
+      if (lane == 0) {
+        okw = mbar_wait(bar(kBarWorkFull + ws), wphase, err, kErrTimeoutWork) ? 1 : 0;
+        if (okw) {
+          u = ld_shared_volatile(work_ids + ws);
+          mbar_arrive(bar(kBarWorkEmpty + ws));
+        }
+      }
+      u = __shfl_sync(0xffffffffu, u, 0);
+      okw = __shfl_sync(0xffffffffu, okw, 0);
+      if (++ws == kWorkSlots) { ws = 0; wphase ^= 1u; }
+      if (!okw || u < 0) break;
+      bool g2;
+      int seg, m;
+      decode_unit(u, nseg, p.m1, p.m2, g2, seg, m);
+      const int4 sg = p.segs[seg];
+      const int rows = sg.z;
+      const int n = (rows + 7) & ~7;
+      if (g2) {
+        int okf = 1;
+        if (lane == 0) okf = wait_flag(p.flags + seg, 2 * p.m1, err) ? 1 : 0;
+        okf = __shfl_sync(0xffffffffu, okf, 0);
+        if (!okf) break;
+      }
+      // source row of segment row `lane` (lanes >= rows: row 0, never read)
+      int src = 0;
+      if (lane < rows) {
+        if (g2) src = sg.y + lane;
+        else src = sg.w >= 0 ? sg.w + lane : __ldg(p.record + p.token_off + sg.y + lane);
+      }
+      const int K = g2 ? p.inter : p.hidden;
+      const int ks_n = g2 ? p.ks2 : p.ks1;
+      const uint8_t *dq = g2 ? p.hq : p.xq;
+      const uint8_t *dsc = g2 ? p.hs : p.xs;
+      const size_t term_q = static_cast<size_t>(g2 ? p.rows_cap : p.max_tokens) * K;
+      const size_t term_s = term_q >> 5;
+      const int data_pieces = p.terms * n * 16;  // 16-byte pieces per stage (multiple of 32)
+      const int scale_pieces = p.terms * n * 2;  // 4-byte pieces per stage
+#pragma unroll 1
+      for (int ks = 0; ks < ks_n; ++ks) {
+        int oke = 1;
+        if (lane == 0) oke = mbar_wait(bar(kBarEmpty + stage), phase ^ 1u, err, kErrTimeoutEmpty) ? 1 : 0;
+        oke = __shfl_sync(0xffffffffu, oke, 0);
+        if (!oke) break;
+        const uint32_t sb = base + kSmemB + stage * kBStageBytes;
+        const uint32_t ssb = base + kSmemSfb + stage * kSfbStageBytes;
+#pragma unroll 1
+        for (int i0 = 0; i0 < data_pieces; i0 += 32) {
+          const int idx = i0 + lane;
+          const int t = idx / (n * 16);
+          const int rem = idx - t * n * 16;
+          const int r = rem >> 4, pc = rem & 15;
+          const int c = pc >> 3, j = pc & 7;
+          const int sr = __shfl_sync(0xffffffffu, src, r & 31);
+          const uint8_t *g = dq + t * term_q + static_cast<size_t>(sr) * K + ks * kStageK + c * 128 + j * 16;
+          const uint32_t d = sb + t * kBTermBytes + c * kBChunkBytes + (r >> 3) * 1024 + (r & 7) * 128 +
+                             ((j ^ (r & 7)) << 4);
+          cp_async_16(d, g, r < rows ? 16u : 0u);
+        }
+#pragma unroll 1
+        for (int i0 = 0; i0 < scale_pieces; i0 += 32) {
+          const int idx = i0 + lane;
+          const int t = idx / (n * 2);
+          const int rem = idx - t * n * 2;
+          const int r = rem >> 1, c = rem & 1;
+          const int sr = __shfl_sync(0xffffffffu, src, r & 31);
+          if (idx < scale_pieces) {
+            const uint8_t *g = dsc + t * term_s + static_cast<size_t>(sr) * (K >> 5) + ks * 8 + c * 4;
+            const uint32_t d = ssb + t * kSfbTermBytes + c * 512 + r * 16;
+            cp_async_4(d, g, r < rows ? 4u : 0u);
+          }
+        }
+        cp_async_arrive_noinc(bar(kBarFull + stage));
+        if (++stage == kStages) { stage = 0; phase ^= 1u; }
+      }
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+  } else {
+    // ============================ epilogue ===================================
+    // No block-level barrier here: the gate_up hand-off between the up-row and
+    // gate-row warps goes through two mbarriers with bounded waits, and each
+    // gate-row warp publishes its own h rows to the segment mailbox.
+    pdl_wait();
+    const int nseg = p.ctrl[kCtrlSegments];
+    const int q = warp & 3;             // TMEM lane quadrant of this warp
+    const int row = 32 * q + lane;      // accumulator row (weight-tile row)
+    float *ex = reinterpret_cast<float *>(sbase + kSmemEpi);
+    uint32_t ws = 0, wphase = 0, acc = 0, acc_phase = 0, ex_phase = 0;
+#pragma unroll 1
+    while (true) {
+      int u = -1, okw = 1;
+      if (lane == 0) {
+        okw = mbar_wait(bar(kBarWorkFull + ws), wphase, err, kErrTimeoutWork) ? 1 : 0;
+        if (okw) {
+          u = ld_shared_volatile(work_ids + ws);
+          mbar_arrive(bar(kBarWorkEmpty + ws));
+        }
+      }
+      u = __shfl_sync(0xffffffffu, u, 0);
+      okw = __shfl_sync(0xffffffffu, okw, 0);
+      if (++ws == kWorkSlots) { ws = 0; wphase ^= 1u; }
+      if (!okw || u < 0) break;
+      bool g2;
+      int seg, m;
+      decode_unit(u, nseg, p.m1, p.m2, g2, seg, m);
+      const int4 sg = p.segs[seg];
+      const int rows = sg.z;
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait(bar(kBarAccFull + acc), acc_phase, err, kErrTimeoutAcc) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t v[16];
+      tc_ld_32x32b_x16(tbase + (static_cast<uint32_t>(32 * q) << 16) + kTmemAcc + acc * kSegRows, v);
+      tc_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kBarAccEmpty + acc));
+      if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      if (!g2) {
+        // rows 0..63: gate of features 64m + row; rows 64..127: up of the same features
+        if (q >= 2) {
+          if (lane == 0) ok = mbar_wait(bar(kBarExFree), ex_phase ^ 1u, err, kErrTimeoutAcc) ? 1 : 0;
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+          if (!ok) break;
+#pragma unroll
+          for (int j = 0; j < kSegRows; ++j) ex[(row - 64) * kSegRows + j] = __uint_as_float(v[j]);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(kBarExFull));
+        } else {
+          if (lane == 0) ok = mbar_wait(bar(kBarExFull), ex_phase, err, kErrTimeoutAcc) ? 1 : 0;
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+          if (!ok) break;
+          float upv[kSegRows];
+#pragma unroll
+          for (int j = 0; j < kSegRows; ++j) upv[j] = ex[row * kSegRows + j];
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(kBarExFree));
+          const float *lim = sg.x < 0 ? p.shared_clamp : p.clamp;
+          const bool clamped = lim != nullptr;
+          const float L = clamped ? lim[sg.x < 0 ? 0 : sg.x] : 0.0f;
+          const int f = 64 * m + 32 * q + lane;  // feature (column of h)
+          const size_t lo_q = static_cast<size_t>(p.rows_cap) * p.inter;
+#pragma unroll
+          for (int j = 0; j < kSegRows; ++j) {
+            if (j >= rows) break;
+            float g = __uint_as_float(v[j]);
+            float up = upv[j];
+            if (clamped) {
+              up = fminf(fmaxf(up, -L), L);
+              g = fminf(g, L);
+            }
+            const float h = __fmul_rn(up, __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
+            // MXFP8 hi / lo of the 32 features of this warp for token row j
+            const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(h))));
+            const uint32_t code = mx_scale_code(amax);
+            const uint8_t qh = static_cast<uint8_t>(e4m3x2(__fmul_rn(h, mx_inverse(code)), 0.0f) & 0xffu);
+            const size_t prow = static_cast<size_t>(sg.y + j);
+            p.hq[prow * p.inter + f] = qh;
+            if (lane == 0) p.hs[prow * (p.inter >> 5) + (f >> 5)] = static_cast<uint8_t>(code);
+            if (p.terms > 1) {
+              const float r = __fsub_rn(h, __fmul_rn(e4m3_value(qh), mx_scale_value(code)));
+              const float amax2 = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(r))));
+              const uint32_t code2 = mx_scale_code(amax2);
+              const uint8_t ql = static_cast<uint8_t>(e4m3x2(__fmul_rn(r, mx_inverse(code2)), 0.0f) & 0xffu);
+              p.hq[lo_q + prow * p.inter + f] = ql;
+              if (lane == 0) p.hs[(lo_q >> 5) + prow * (p.inter >> 5) + (f >> 5)] = static_cast<uint8_t>(code2);
+            }
+          }
+          // publish this warp's 32 features of every row: two increments per unit
+          __threadfence();
+          __syncwarp();
+          if (lane == 0) asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(p.flags + seg) : "memory");
+        }
+        ex_phase ^= 1u;
+      } else {
+        // features 128m + row of the segment's rows, bf16
+        const size_t col = static_cast<size_t>(128 * m + row);
+#pragma unroll
+        for (int j = 0; j < kSegRows; ++j) {
+          if (j >= rows) break;
+          p.rows_out[static_cast<size_t>(sg.y + j) * p.hidden + col] = float_to_bf16_bits(__uint_as_float(v[j]));
+        }
+      }
+    }
+  }
+
+  // ---- teardown --------------------------------------------------------------
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, kTmemCols);
+  }
+}
+
+// ============================================================================
+// Scale repack (layer creation): canonical E8M0 [n][rows][K/32] -> UMMA scale
+// chunks [n][tile][K/256][2][32 m0][4 m1][4 kk]. gate_up tiles take gate rows
+// 64t + r (r < 64) and up rows I + 64t + r - 64; down tiles rows 128t + r.
+// ============================================================================
+__global__ void repack_scales_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst,
+                                     int n, int rows, int k, int gate_up, int inter) {
+  const int ks_n = k / kStageK;
+  const int tiles = gate_up ? rows / 128 : rows / 128;
+  const size_t total = static_cast<size_t>(n) * tiles * ks_n * 1024;
+  for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int b = static_cast<int>(idx & 1023);
+    size_t rest = idx >> 10;
+    const int ks = static_cast<int>(rest % ks_n);
+    rest /= ks_n;
+    const int t = static_cast<int>(rest % tiles);
+    const int e = static_cast<int>(rest / tiles);
+    const int c = b >> 9, w = b & 511;
+    const int m0 = w >> 4, m1 = (w >> 2) & 3, kk = w & 3;
+    const int r = m0 + 32 * m1;
+    const int kb = ks * 8 + 4 * c + kk;
+    const int srow = gate_up ? (r < 64 ? 64 * t + r : inter + 64 * t + (r - 64)) : 128 * t + r;
+    dst[idx] = src[(static_cast<size_t>(e) * rows + srow) * (k >> 5) + kb];
+  }
+}
+
+}  // namespace mm

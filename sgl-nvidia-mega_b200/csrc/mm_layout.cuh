@@ -1,0 +1,105 @@
+// Data layouts shared by the host side and the kernels of the routed-MoE chain.
+//
+// HBM, per layer (all device memory, allocated once at layer creation):
+//   weights     caller-owned canonical MXFP4 (E2M1 codes, [n, rows, K/2] u8) read
+//               in place by TMA with on-the-fly 4-bit -> 8-bit-slot unpacking;
+//   sfa13/sfa2  the E8M0 weight scales re-laid once as UMMA scale chunks:
+//               [n][m_tile][k_stage][2 chunks][32 m0][4 m1][4 kk] bytes, so one
+//               1 KB bulk copy per pipeline stage lands them ready for tcgen05.cp;
+//   xq/xs       the routed input, two MXFP8 terms (hi, lo): [term][T][H] E4M3 and
+//               [term][T][H/32] E8M0, written by the front kernel;
+//   hq/hs       the SwiGLU output of gate_up, [term][rows][I] and [term][rows][I/32],
+//               rows in the reference's padded permuted order;
+//   segs/ctrl   work tables built by the front kernel (below);
+//   err         the device error word.
+#pragma once
+#include <cstdint>
+
+namespace mm {
+
+// ---- route record (bit for bit the reference's, route.cuh:6-46) ---------------
+constexpr int kTile = 8;
+__host__ __device__ inline int route_max_ctas(int rows, int top_k, int experts) {
+  const int slots = rows * top_k;
+  const int filled = experts < slots ? experts : slots;
+  return filled + (slots - filled) / kTile;
+}
+__host__ __device__ inline int route_cta_words(int max_ctas) { return (max_ctas + 3) / 4 * 4; }
+__host__ __device__ inline int route_words(int rows, int top_k, int experts) {
+  const int m = route_max_ctas(rows, top_k, experts);
+  return 4 + 2 * route_cta_words(m) + kTile * m;
+}
+
+// ---- expert work -----------------------------------------------------------------
+// A segment is up to kSegRows consecutive permuted rows of one expert; one work
+// unit streams one 128-row weight tile of that expert through the whole K and
+// multiplies it with all the segment's rows (N = rows rounded up to 8).
+constexpr int kSegRows = 16;
+constexpr int kMaxTokens = 256;
+constexpr int kMaxTopK = 16;
+constexpr int kMaxRouterExperts = 1024;
+
+struct Segment {   // int4 in memory
+  int expert;      // local expert index, -1 for the shared expert
+  int row_base;    // first permuted row (rows_out / hq row)
+  int rows;        // 1..kSegRows
+  int token_base;  // shared expert: token of row_base; routed: -1 (tokens from the record)
+};
+
+// ctrl words
+constexpr int kCtrlSegments = 0;  // number of segments
+constexpr int kCtrlUnits = 1;     // gate_up units + down units
+constexpr int kCtrlClaim = 2;     // next unit to claim (reset to 0 by the front kernel)
+constexpr int kCtrlTicket = 3;    // front kernel's last-CTA ticket (reset by the last CTA)
+constexpr int kCtrlWords = 8;
+
+// ---- the persistent expert kernel's shared memory -----------------------------------
+constexpr int kStages = 5;
+constexpr int kStageK = 256;                  // K elements per pipeline stage
+constexpr int kAStageBytes = 128 * kStageK;   // 4-bit codes in 8-bit slots: 32 KB
+constexpr int kAChunkBytes = 128 * 128;       // one 128-K chunk of 128 rows
+constexpr int kBTermBytes = kSegRows * kStageK;  // 16 rows x 256 B
+constexpr int kBStageBytes = 2 * kBTermBytes;    // hi + lo
+constexpr int kBChunkBytes = kSegRows * 128;     // one 128-K chunk of the 16 rows
+constexpr int kSfaStageBytes = 1024;          // 2 chunks x 512 B
+constexpr int kSfbTermBytes = 1024;           // 2 chunks x 512 B
+constexpr int kSfbStageBytes = 2 * kSfbTermBytes;
+constexpr int kEpiBytes = 128 * kSegRows * 4; // epilogue exchange / transpose
+constexpr int kWorkSlots = 4;
+
+constexpr int kSmemA = 0;
+constexpr int kSmemB = kSmemA + kStages * kAStageBytes;
+constexpr int kSmemSfa = kSmemB + kStages * kBStageBytes;
+constexpr int kSmemSfb = kSmemSfa + kStages * kSfaStageBytes;
+constexpr int kSmemEpi = kSmemSfb + kStages * kSfbStageBytes;
+constexpr int kSmemBar = kSmemEpi + kEpiBytes;
+// barriers: full[S], empty[S], acc_full[2], acc_empty[2], work_full[W], work_empty[W], drain,
+// epilogue staging full / free
+constexpr int kBarFull = 0;
+constexpr int kBarEmpty = kStages;
+constexpr int kBarAccFull = 2 * kStages;
+constexpr int kBarAccEmpty = 2 * kStages + 2;
+constexpr int kBarWorkFull = 2 * kStages + 4;
+constexpr int kBarWorkEmpty = 2 * kStages + 4 + kWorkSlots;
+constexpr int kBarDrain = 2 * kStages + 4 + 2 * kWorkSlots;
+constexpr int kBarExFull = kBarDrain + 1;   // gate_up epilogue: up rows staged
+constexpr int kBarExFree = kBarDrain + 2;   // gate_up epilogue: staging consumed
+constexpr int kNumBars = kBarDrain + 3;
+constexpr int kSmemWorkIds = kSmemBar + 8 * kNumBars;
+constexpr int kSmemTmemBase = kSmemWorkIds + 4 * kWorkSlots;
+constexpr int kSmemTotal = kSmemTmemBase + 16;
+constexpr int kSmemAlloc = kSmemTotal + 1024;  // room to align the base to 1 KB
+static_assert(kSmemAlloc <= 232448, "expert kernel shared memory over the 227 KB limit");
+static_assert(kSmemB % 1024 == 0 && kSmemSfa % 128 == 0 && kSmemSfb % 128 == 0, "alignment");
+
+// TMEM columns: 2 accumulators of kSegRows fp32 columns, then per stage the
+// A scale chunks (8 columns) and the B scale chunks of both terms (16 columns).
+constexpr int kTmemAcc = 0;
+constexpr int kTmemSfa = 2 * kSegRows;
+constexpr int kTmemSfb = kTmemSfa + kStages * 8;
+constexpr int kTmemCols = 256;
+static_assert(kTmemSfb + kStages * 16 <= kTmemCols, "TMEM columns");
+
+constexpr int kExpertThreads = 224;  // 7 warps: producer, MMA, B loader, 4 epilogue
+
+}  // namespace mm

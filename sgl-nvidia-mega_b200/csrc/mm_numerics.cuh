@@ -1,0 +1,118 @@
+// Deterministic fp32 arithmetic of the routing and activation-quantization steps.
+//
+// Every function here is a fixed sequence of IEEE-754 binary32 operations with
+// round-to-nearest-even (the __f*_rn intrinsics, so no contraction or fast-math
+// rewrite applies), plus exact bit manipulations. The CPU oracle evaluates the
+// same sequences with C99 float arithmetic and fmaf, so scores, routing keys,
+// top-k ids, routing weights and MX scale/code bytes match it bit for bit.
+//
+// Reference numerics followed:
+//  * routing keys, ties and NaN rules: deepseek_v41/sm103/moe/src/gate_topk.cuh:129-145
+//    (order-preserving u32 key of score + bias, -0 ranked as +0) and
+//    glm5_3/sm103/primitives/ptx_tc.py:393-402 (NaN ranks as -inf);
+//    the lowest expert id wins a tie (gate_topk.cuh:211-290, routing.py:32-70).
+//  * weights: gate_topk.cuh:187-198 (score / (sum + eps) or the guarded sum, then
+//    the routed scale); glm5_3/sm103/moe/routing.py:3-11 (sigmoid + bias, renorm).
+//  * MXFP8 quantization: deepseek_v41/sm103/moe/src/route_quant.cuh:1-15 and
+//    gemm1.cu:905-1000 (block-32 amax, times fp32(1/448), E8M0 rounded up,
+//    multiply by the exact inverse power of two, e4m3 RN satfinite).
+// The sigmoid uses this file's own exp (Cody-Waite reduction + Taylor
+// polynomial) instead of the reference's tanh.approx, whose bits no CPU code
+// can reproduce; everything else is the reference's rule.
+#pragma once
+#include <cstdint>
+#include <cuda_bf16.h>
+
+namespace mm {
+
+// exp(x): x = n ln2 + r with n = rint(x log2e) and r by a two-constant
+// Cody-Waite reduction, e^r by the degree-7 Taylor polynomial in Horner form,
+// then an exact scaling by 2^n (two steps outside the normal exponent range).
+__device__ __forceinline__ float det_exp(float x) {
+  if (x != x) return x;
+  if (x > 0x1.62e430p+6f) return __int_as_float(0x7f800000);
+  if (x < -0x1.a00000p+6f) return 0.0f;  // below -104: under half the least subnormal
+  const float kLog2e = 0x1.715476p+0f;
+  const float kMagic = 0x1.8p+23f;  // adding 1.5 * 2^23 rounds to an integer
+  const float kLn2Hi = 0x1.62e400p-1f;
+  const float kLn2Lo = 0x1.7f7d1cp-20f;
+  const float t = __fmaf_rn(x, kLog2e, kMagic);
+  const float n = __fsub_rn(t, kMagic);
+  float r = __fmaf_rn(-n, kLn2Hi, x);
+  r = __fmaf_rn(-n, kLn2Lo, r);
+  float p = 0x1.a01a02p-13f;  // 1/5040
+  p = __fmaf_rn(p, r, 0x1.6c16c2p-10f);  // 1/720
+  p = __fmaf_rn(p, r, 0x1.111112p-7f);   // 1/120
+  p = __fmaf_rn(p, r, 0x1.555556p-5f);   // 1/24
+  p = __fmaf_rn(p, r, 0x1.555556p-3f);   // 1/6
+  p = __fmaf_rn(p, r, 0x1.000000p-1f);   // 1/2
+  p = __fmaf_rn(p, r, 1.0f);
+  p = __fmaf_rn(p, r, 1.0f);
+  const int ni = static_cast<int>(n);
+  if (ni > 127) return __fmul_rn(__fmul_rn(p, __int_as_float((ni - 1 + 127) << 23)), 2.0f);
+  if (ni < -126)
+    return __fmul_rn(__fmul_rn(p, __int_as_float((ni + 100 + 127) << 23)),
+                     __int_as_float((-100 + 127) << 23));
+  return __fmul_rn(p, __int_as_float((ni + 127) << 23));
+}
+
+__device__ __forceinline__ float det_sigmoid(float x) {
+  return __fdiv_rn(1.0f, __fadd_rn(1.0f, det_exp(-x)));
+}
+
+// Order-preserving key of v (larger key = better candidate); -0 ranks as +0
+// and NaN ranks below every number (key 0).
+__device__ __forceinline__ uint32_t routing_key(float v) {
+  if (v != v) return 0u;
+  const uint32_t bits = __float_as_uint(__fadd_rn(v, 0.0f));
+  return (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);
+}
+
+// ---- MXFP8 (E4M3 codes + E8M0 block scale) ------------------------------------
+// E8M0 code of a block whose absolute maximum is `amax`: the exponent of
+// amax * fp32(1/448), rounded up when the mantissa is non-zero.
+__device__ __forceinline__ uint32_t mx_scale_code(float amax) {
+  const float numerator = amax == 0.0f ? 448.0f : amax;
+  const uint32_t bits = __float_as_uint(__fmul_rn(numerator, 0x1.24924ap-9f));
+  const uint32_t exponent = (bits >> 23) & 0xffu;
+  const uint32_t mantissa = bits & 0x7fffffu;
+  uint32_t code = exponent;
+  if (mantissa != 0u && exponent != 254u) {
+    if (exponent != 0u) code = exponent + 1u;
+    else if (mantissa > 0x400000u) code = 1u;
+  }
+  if (exponent == 255u) code = 255u;
+  return code;
+}
+// 2^(127 - code): the exact multiplier that maps the block into E4M3 range.
+__device__ __forceinline__ float mx_inverse(uint32_t code) {
+  return code == 254u ? __uint_as_float(0x400000u) : __uint_as_float((254u - code) << 23);
+}
+// 2^(code - 127).
+__device__ __forceinline__ float mx_scale_value(uint32_t code) {
+  return code == 0u ? __uint_as_float(0x400000u) : __uint_as_float(code << 23);
+}
+// Two floats -> two E4M3 codes (RN, saturating to +-448); lo in the low byte.
+__device__ __forceinline__ uint16_t e4m3x2(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ float e4m3_value(uint8_t code) {
+  // exact decode of an E4M3 (fn) byte
+  const uint32_t s = code >> 7, e = (code >> 3) & 15u, m = code & 7u;
+  float v;
+  if (e == 0u) v = static_cast<float>(m) * 0x1p-9f;
+  else if (e == 15u && m == 7u) v = __uint_as_float(0x7fc00000u);
+  else v = __uint_as_float(((e + 120u) << 23) | (m << 20));
+  return s ? -v : v;
+}
+
+__device__ __forceinline__ float bf16_bits_to_float(uint16_t b) {
+  return __uint_as_float(static_cast<uint32_t>(b) << 16);
+}
+__device__ __forceinline__ uint16_t float_to_bf16_bits(float f) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+
+}  // namespace mm

@@ -1,0 +1,392 @@
+// Front of the routed-MoE chain: router GEMV (K0), top-k with bias (K1a), the
+// route record and slot -> row map (K1b), the two-term MXFP8 quantization of
+// the routed input, and the segment / work tables of the expert kernel.
+//
+// The route record is bit for bit the reference's (route.cuh:6-46,94-161 for
+// up to 8 rows, route_wide.cu:1-14,62-163 beyond): local experts in ascending
+// id order, each one's rows in ascending token order, every expert's segment
+// padded to 8-row tiles, an expert chosen by more than 8 rows owning
+// consecutive tiles. The construction here is our own (multi-word row masks in
+// shared memory and one block scan, for up to 256 rows).
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "mm_kernels.cuh"
+#include "mm_layout.cuh"
+#include "mm_numerics.cuh"
+#include "mm_ptx.cuh"
+
+namespace mm {
+
+// ============================================================================
+// K0: router GEMV. logits[t, e] = sum_h x[t, h] w[e, h], fp32.
+//
+// Summation order (the CPU oracle replays it): the hidden dimension is cut in
+// four parts of H/4 (one warp each); lane l of a part accumulates, for
+// j = 0, 1, ..., the eight elements h = part*H/4 + 8*(l + 32 j) + i (i = 0..7)
+// with acc = fma(x, w, acc) from acc = 0; the 32 lane sums are combined by the
+// butterfly acc += shfl_xor(acc, 16, 8, 4, 2, 1); the part sums as
+// (p0 + p1) + (p2 + p3). bf16 x bf16 products are exact in fp32.
+// grid (E, ceil(T/8)), block 128.
+// ============================================================================
+__global__ void __launch_bounds__(128) router_gemv_kernel(const uint16_t *__restrict__ x,
+                                                          const uint16_t *__restrict__ w,
+                                                          float *__restrict__ logits, int tokens,
+                                                          int experts, int hidden) {
+  pdl_launch_dependents();
+  const int e = blockIdx.x;
+  const int t0 = blockIdx.y * 8;
+  const int nt = min(8, tokens - t0);
+  const int part = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kp = hidden >> 2;
+  const int nvec = kp >> 8;  // 16-byte vectors per lane
+  __shared__ float part_sum[4][8];
+  // The weights are static: stream them before waiting for the producer of x.
+  const uint4 *wrow = reinterpret_cast<const uint4 *>(w + static_cast<size_t>(e) * hidden + part * kp);
+  pdl_wait();
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+#pragma unroll 1
+  for (int j = 0; j < nvec; ++j) {
+    const int v = lane + 32 * j;
+    const uint4 wv = __ldg(wrow + v);
+    const uint32_t wq[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+    for (int tt = 0; tt < 8; ++tt) {
+      if (tt < nt) {
+        const uint4 xv = __ldg(reinterpret_cast<const uint4 *>(
+                                   x + static_cast<size_t>(t0 + tt) * hidden + part * kp) +
+                               v);
+        const uint32_t xq[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          acc[tt] = __fmaf_rn(__uint_as_float(xq[q] << 16), __uint_as_float(wq[q] << 16), acc[tt]);
+          acc[tt] = __fmaf_rn(__uint_as_float(xq[q] & 0xffff0000u),
+                              __uint_as_float(wq[q] & 0xffff0000u), acc[tt]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int tt = 0; tt < 8; ++tt) {
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1)
+      acc[tt] = __fadd_rn(acc[tt], __shfl_xor_sync(0xffffffffu, acc[tt], off));
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int tt = 0; tt < 8; ++tt) part_sum[part][tt] = acc[tt];
+  }
+  __syncthreads();
+  if (threadIdx.x < nt) {
+    const int tt = threadIdx.x;
+    const float s = __fadd_rn(__fadd_rn(part_sum[0][tt], part_sum[1][tt]),
+                              __fadd_rn(part_sum[2][tt], part_sum[3][tt]));
+    logits[static_cast<size_t>(t0 + tt) * experts + e] = s;
+  }
+}
+
+// ============================================================================
+// K1a: one row's top-k (block of 512 threads, experts e = tid and tid + 512).
+// ============================================================================
+struct GateSmem {
+  float score[kMaxRouterExperts];
+  float logit[kMaxRouterExperts];
+  unsigned long long cand[16][kMaxTopK];
+  int sel[kMaxTopK];
+};
+
+__device__ __forceinline__ unsigned long long pack_key(uint32_t key, int e) {
+  return (static_cast<unsigned long long>(key) << 32) | static_cast<uint32_t>(0xffffffffu - e);
+}
+__device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long v) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    const unsigned long long o = __shfl_xor_sync(0xffffffffu, v, off);
+    v = o > v ? o : v;
+  }
+  return v;
+}
+
+// Computes ids/weights of row `row` and writes them to ids_out/weights_out.
+__device__ void gate_row(const GateArgs &g, int row, int valid_rows, GateSmem &sm) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int E = g.router_experts, K = g.top_k;
+  const float *lrow = g.logits + static_cast<size_t>(row) * E;
+  unsigned long long pk[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int e = tid + 512 * h;
+    pk[h] = 0ull;
+    if (e < E) {
+      const float l = lrow[e];
+      const float b = g.bias != nullptr ? g.bias[e] : 0.0f;
+      float s;
+      if (g.score_func == 0) s = det_sigmoid(l);
+      else s = l;  // softmax: rank the (biased) logits
+      sm.score[e] = s;
+      sm.logit[e] = l;
+      pk[h] = pack_key(routing_key(__fadd_rn(s, b)), e);
+    }
+  }
+  // per-warp top-K candidates (every global winner is in its warp's top-K)
+  for (int k = 0; k < K; ++k) {
+    const unsigned long long mine = pk[0] > pk[1] ? pk[0] : pk[1];
+    const unsigned long long top = warp_max_u64(mine);
+    if (lane == 0) sm.cand[warp][k] = top;
+    if (pk[0] == top) pk[0] = 0ull;
+    if (pk[1] == top) pk[1] = 0ull;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    // merge 16 warps x K candidates: lane l holds warps' entries l, l+32, ...
+    constexpr int kPer = 16 * kMaxTopK / 32;
+    unsigned long long c[kPer];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int idx = lane + 32 * j;  // idx = warp_id * kMaxTopK + k
+      const int cw = idx / kMaxTopK, ck = idx % kMaxTopK;
+      c[j] = (ck < K) ? sm.cand[cw][ck] : 0ull;
+    }
+    for (int k = 0; k < K; ++k) {
+      unsigned long long best = 0ull;
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) best = c[j] > best ? c[j] : best;
+      const unsigned long long top = warp_max_u64(best);
+#pragma unroll
+      for (int j = 0; j < kPer; ++j)
+        if (c[j] == top) c[j] = 0ull;
+      if (lane == 0) sm.sel[k] = static_cast<int>(0xffffffffu - static_cast<uint32_t>(top));
+    }
+    __syncwarp();
+    if (lane == 0) {
+      const bool valid = row < valid_rows;
+      float w[kMaxTopK];
+      if (g.score_func == 1) {
+        float m = sm.logit[sm.sel[0]];
+        for (int k = 1; k < K; ++k) m = fmaxf(m, sm.logit[sm.sel[k]]);
+        float sum = 0.0f;
+        for (int k = 0; k < K; ++k) {
+          w[k] = det_exp(__fsub_rn(sm.logit[sm.sel[k]], m));
+          sum = __fadd_rn(sum, w[k]);
+        }
+        for (int k = 0; k < K; ++k) w[k] = __fmul_rn(__fdiv_rn(w[k], sum), g.routed_scaling);
+      } else {
+        float sum = 0.0f;
+        for (int k = 0; k < K; ++k) {
+          w[k] = sm.score[sm.sel[k]];
+          sum = __fadd_rn(sum, w[k]);
+        }
+        if (g.renormalize) {
+          const float norm = g.renorm_eps > 0.0f ? __fadd_rn(sum, g.renorm_eps)
+                                                 : (sum > 0.0f ? sum : 1.0f);
+          for (int k = 0; k < K; ++k) w[k] = __fmul_rn(__fdiv_rn(w[k], norm), g.routed_scaling);
+        } else {
+          for (int k = 0; k < K; ++k) w[k] = __fmul_rn(w[k], g.routed_scaling);
+        }
+      }
+      for (int k = 0; k < K; ++k) {
+        g.ids_out[static_cast<size_t>(row) * K + k] = valid ? sm.sel[k] : -1;
+        g.weights_out[static_cast<size_t>(row) * K + k] = valid ? w[k] : 0.0f;
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(512) gate_topk_kernel(GateArgs g) {
+  pdl_launch_dependents();
+  __shared__ GateSmem sm;
+  pdl_wait();
+  const int valid = g.num_valid != nullptr ? *g.num_valid : static_cast<int>(gridDim.x);
+  gate_row(g, blockIdx.x, valid, sm);
+}
+
+// ============================================================================
+// Two-term MXFP8 quantization of one bf16 row (block of 512 threads).
+// term 0: q = e4m3(v * 2^(127-c)) with c the E8M0 code of the block's amax;
+// term 1: the same rule applied to the residual v - q * 2^(c-127).
+// ============================================================================
+__device__ void quantize_row(const uint16_t *__restrict__ xrow, uint8_t *__restrict__ q_hi,
+                             uint8_t *__restrict__ q_lo, uint8_t *__restrict__ s_hi,
+                             uint8_t *__restrict__ s_lo, int hidden, int terms) {
+  const int blocks = hidden >> 5;
+  for (int b = threadIdx.x; b < blocks; b += blockDim.x) {
+    const uint4 *src = reinterpret_cast<const uint4 *>(xrow + 32 * b);
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 u = src[i];
+      const uint32_t q[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        v[8 * i + 2 * j] = __uint_as_float(q[j] << 16);
+        v[8 * i + 2 * j + 1] = __uint_as_float(q[j] & 0xffff0000u);
+      }
+    }
+    quantize_block32(v, q_hi + 32 * b, q_lo + 32 * b, s_hi + b, s_lo + b, terms);
+  }
+}
+
+// ============================================================================
+// K1b: the route record (block of 512 threads). Dynamic shared memory:
+// rowmask[experts][words] u32, first_cta[experts] int, warp totals.
+// ============================================================================
+__device__ void block_exclusive_scan_512(int *vals /*[1024] pairs*/, int n, int *warp_tot,
+                                         int &total) {
+  // vals[0..n) in place -> exclusive prefix; n <= 1024; each thread two entries
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int a = 2 * tid < n ? vals[2 * tid] : 0;
+  const int b = 2 * tid + 1 < n ? vals[2 * tid + 1] : 0;
+  const int local = a + b;
+  int inc = local;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int up = __shfl_up_sync(0xffffffffu, inc, off);
+    if (lane >= off) inc += up;
+  }
+  if (lane == 31) warp_tot[warp] = inc;
+  __syncthreads();
+  if (warp == 0) {
+    int t = lane < 16 ? warp_tot[lane] : 0;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int up = __shfl_up_sync(0xffffffffu, t, off);
+      if (lane >= off) t += up;
+    }
+    if (lane < 16) warp_tot[lane] = t;
+  }
+  __syncthreads();
+  const int base = inc - local + (warp > 0 ? warp_tot[warp - 1] : 0);
+  total = warp_tot[15];
+  if (2 * tid < n) vals[2 * tid] = base;
+  if (2 * tid + 1 < n) vals[2 * tid + 1] = base + a;
+  __syncthreads();
+}
+
+__device__ void build_route(const RouteArgs &r, unsigned char *smem_raw) {
+  const int tid = threadIdx.x;
+  const int T = r.tokens, K = r.top_k, E = r.experts;
+  const int words = (T + 31) >> 5;
+  uint32_t *rowmask = reinterpret_cast<uint32_t *>(smem_raw);
+  int *first = reinterpret_cast<int *>(rowmask + E * words);
+  int *seg_first = first + E;
+  int *warp_tot = seg_first + E;
+  int *counts = warp_tot + 32;
+  const int slots = T * K;
+  const int max_ctas = route_max_ctas(T, K, E);
+  const int cw = route_cta_words(max_ctas);
+  const int limit_off = 4 + cw, token_off = 4 + 2 * cw;
+  const int rec_words = token_off + kTile * max_ctas;
+  for (int i = tid; i < E * words; i += blockDim.x) rowmask[i] = 0u;
+  for (int i = tid; i < rec_words; i += blockDim.x) r.record[i] = 0;
+  __syncthreads();
+  for (int s = tid; s < slots; s += blockDim.x) {
+    const int t = s / K;
+    const int e = r.ids[s] - r.expert_offset;
+    if (e >= 0 && e < E) atomicOr(&rowmask[e * words + (t >> 5)], 1u << (t & 31));
+  }
+  __syncthreads();
+  for (int e = tid; e < E; e += blockDim.x) {
+    int c = 0;
+    for (int wd = 0; wd < words; ++wd) c += __popc(rowmask[e * words + wd]);
+    counts[e] = c;
+    first[e] = (c + kTile - 1) / kTile;               // tiles
+    seg_first[e] = (c + kSegRows - 1) / kSegRows;     // segments
+  }
+  __syncthreads();
+  int total_ctas = 0, total_segs = 0;
+  block_exclusive_scan_512(first, E, warp_tot, total_ctas);
+  block_exclusive_scan_512(seg_first, E, warp_tot, total_segs);
+  if (tid == 0) {
+    r.record[0] = total_ctas * kTile;
+    r.record[1] = total_ctas;
+  }
+  for (int s = tid; s < slots; s += blockDim.x) {
+    const int t = s / K;
+    const int e = r.ids[s] - r.expert_offset;
+    if (e < 0 || e >= E) {
+      r.permuted[s] = -1;
+      continue;
+    }
+    int rank = 0;
+    const uint32_t *m = rowmask + e * words;
+    for (int wd = 0; wd < (t >> 5); ++wd) rank += __popc(m[wd]);
+    rank += __popc(m[t >> 5] & ((1u << (t & 31)) - 1u));
+    const int base_row = first[e] * kTile;
+    r.permuted[s] = base_row + rank;
+    r.record[token_off + base_row + rank] = t;
+    if (rank % kTile == 0) {
+      const int cta = first[e] + rank / kTile;
+      r.record[4 + cta] = e;
+      r.record[limit_off + cta] = min((cta + 1) * kTile, base_row + counts[e]);
+    }
+  }
+  // expert-kernel work tables (shared expert's segments first)
+  if (r.segs != nullptr) {
+    const int shared_segs = r.has_shared ? (T + kSegRows - 1) / kSegRows : 0;
+    for (int j = tid; j < shared_segs; j += blockDim.x) {
+      const int rows = min(kSegRows, T - j * kSegRows);
+      r.segs[j] = make_int4(-1, r.shared_row_base + j * kSegRows, rows, j * kSegRows);
+    }
+    for (int e = tid; e < E; e += blockDim.x) {
+      const int c = counts[e];
+      const int nseg = (c + kSegRows - 1) / kSegRows;
+      for (int j = 0; j < nseg; ++j) {
+        const int rows = min(kSegRows, c - j * kSegRows);
+        r.segs[shared_segs + seg_first[e] + j] =
+            make_int4(e, first[e] * kTile + j * kSegRows, rows, -1);
+      }
+    }
+    const int nseg = shared_segs + total_segs;
+    for (int j = tid; j < nseg; j += blockDim.x) r.flags[j] = 0;
+    if (tid == 0) {
+      r.ctrl[kCtrlSegments] = nseg;
+      r.ctrl[kCtrlUnits] = nseg * (r.m1 + r.m2);
+      r.ctrl[kCtrlClaim] = 0;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(512) route_kernel(RouteArgs r) {
+  pdl_launch_dependents();
+  extern __shared__ __align__(16) unsigned char route_smem[];
+  pdl_wait();
+  build_route(r, route_smem);
+}
+
+// ============================================================================
+// The fused front kernel: grid = T rows, block 512. Each CTA ranks its row
+// (or takes given ids) and quantizes its token; the last CTA to finish builds
+// the route record and the work tables.
+// ============================================================================
+__global__ void __launch_bounds__(512) front_kernel(FrontArgs f) {
+  pdl_launch_dependents();
+  extern __shared__ __align__(16) unsigned char front_smem[];
+  __shared__ GateSmem gsm;
+  __shared__ int is_last;
+  pdl_wait();
+  const int row = blockIdx.x;
+  if (f.gate.logits != nullptr) {
+    const int valid = f.gate.num_valid != nullptr ? *f.gate.num_valid : f.route.tokens;
+    gate_row(f.gate, row, valid, gsm);
+  }
+  const size_t th = static_cast<size_t>(f.max_tokens) * f.hidden;
+  const size_t ts = th >> 5;
+  quantize_row(f.x + static_cast<size_t>(row) * f.hidden, f.xq + static_cast<size_t>(row) * f.hidden,
+               f.xq + th + static_cast<size_t>(row) * f.hidden, f.xs + static_cast<size_t>(row) * (f.hidden >> 5),
+               f.xs + ts + static_cast<size_t>(row) * (f.hidden >> 5), f.hidden, f.terms);
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int ticket = atomicAdd(&f.route.ctrl[kCtrlTicket], 1);
+    is_last = ticket == static_cast<int>(gridDim.x) - 1;
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  build_route(f.route, front_smem);
+  if (threadIdx.x == 0) f.route.ctrl[kCtrlTicket] = 0;
+}
+
+}  // namespace mm

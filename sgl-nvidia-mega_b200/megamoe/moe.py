@@ -1,0 +1,391 @@
+"""Host-side mirror of the reference's routed-MoE step API over libmegamoe.
+
+RoutedMoE keeps the shape of sgl-nvidia-mega's RoutedExpertGemm
+(deepseek_v41/sm103/moe/routed_expert_gemm.py:534-870) and of the deferred
+finalize that consumes its output (deepseek_v41/sm103/all_reduce_mhc.py:1484,
+glm5_3/sm103/moe/finalize.py):
+
+  * ``__call__(x, topk_ids, topk_weights)`` -> the deferred-finalize triple
+    (gemm2 rows, weights, slot -> row), like RoutedExpertGemm.__call__;
+  * ``gate_topk_and_gemms(x, logits, bias, routed_scaling_factor, num_valid, ...)``
+    -> (rows, weights, permuted, ids), like RoutedExpertGemm.gate_topk_and_gemms;
+  * ``finalize(rows, weights, permuted)`` -> the combined bf16 MoE output;
+  * ``forward(x, router_weight=..., bias=...)`` -> one whole MoE step.
+
+Differences from the reference's interface: the routed input is passed as bf16
+(the chain quantizes it itself, as gate_route_quant does), weights are the
+canonical MXFP4 layout (not FlashInfer-shuffled), and errors raise ValueError
+(shape/argument) or RuntimeError (device), as the reference's do.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Sequence
+
+import torch
+
+from . import _lib
+from ._lib import check, lib
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _expect(t: torch.Tensor, shape: Sequence[int], name: str, nbytes: int = 1) -> torch.Tensor:
+    if tuple(t.shape) != tuple(shape) or t.element_size() != nbytes or not t.is_contiguous():
+        raise ValueError(
+            f"{name}: expected a contiguous {tuple(shape)} {nbytes}-byte tensor, "
+            f"got {tuple(t.shape)} {t.dtype}"
+        )
+    return t
+
+
+def _u8(t: torch.Tensor) -> torch.Tensor:
+    return t.view(torch.uint8) if t.element_size() == 1 and t.dtype != torch.uint8 else t
+
+
+class RoutedMoE:
+    """The routed-MoE chain bound to one MoE layer's MXFP4 weights.
+
+    Weights (canonical layout, read in place; see include/megamoe.h):
+      w13 u8 [E, 2I, H/2], w13_scale u8 [E, 2I, H/32], w2 u8 [E, H, I/2],
+      w2_scale u8 [E, H, I/32]; ``shared`` = the same four tensors with E = 1.
+    ``router_experts``: the router's expert count (default: the local ones);
+    ``expert_offset``: router id of local expert 0 (expert parallelism);
+    ``clamp``: fp32 [E] SwiGLU clamp limits or None;
+    ``act_terms``: 2 (hi + lo MXFP8 activations, default) or 1 (single MXFP8,
+    the reference kernels' numerics).
+    """
+
+    def __init__(
+        self,
+        w13: torch.Tensor,
+        w13_scale: torch.Tensor,
+        w2: torch.Tensor,
+        w2_scale: torch.Tensor,
+        top_k: int,
+        max_rows: int,
+        *,
+        clamp: Optional[torch.Tensor] = None,
+        router_experts: Optional[int] = None,
+        expert_offset: int = 0,
+        shared: Optional[Sequence[torch.Tensor]] = None,
+        shared_clamp: Optional[torch.Tensor] = None,
+        act_terms: int = 2,
+    ):
+        w13, w13_scale, w2, w2_scale = (_u8(t) for t in (w13, w13_scale, w2, w2_scale))
+        if w13.dim() != 3:
+            raise ValueError(f"w13: expected [E, 2I, H/2], got {tuple(w13.shape)}")
+        experts, two_i, half_h = w13.shape
+        hidden, inter = 2 * half_h, two_i // 2
+        _expect(w13, (experts, 2 * inter, hidden // 2), "w13")
+        _expect(w13_scale, (experts, 2 * inter, hidden // 32), "w13_scale")
+        _expect(w2, (experts, hidden, inter // 2), "w2")
+        _expect(w2_scale, (experts, hidden, inter // 32), "w2_scale")
+        if not w13.is_cuda:
+            raise ValueError("weights must be CUDA tensors")
+        self.device = w13.device
+        self.hidden, self.inter, self.experts = hidden, inter, experts
+        self.router_experts = experts if router_experts is None else int(router_experts)
+        self.expert_offset = int(expert_offset)
+        self.top_k = int(top_k)
+        self.max_rows = int(max_rows)
+        self.act_terms = int(act_terms)
+        if clamp is not None:
+            _expect(clamp, (experts,), "clamp", 4)
+            if clamp.dtype != torch.float32:
+                raise ValueError("clamp must be fp32 [E]")
+        keep = [w13, w13_scale, w2, w2_scale, clamp]
+        desc = _lib.MMLayerDesc()
+        desc.hidden, desc.intermediate, desc.experts = hidden, inter, experts
+        desc.router_experts = self.router_experts
+        desc.expert_offset = self.expert_offset
+        desc.top_k = self.top_k
+        desc.max_tokens = self.max_rows
+        desc.weight_format = _lib.MM_WEIGHT_MXFP4
+        desc.act_terms = self.act_terms
+        desc.device = self.device.index if self.device.index is not None else torch.cuda.current_device()
+        desc.routed = _lib.MMExpertWeights(*(t.data_ptr() for t in (w13, w13_scale, w2, w2_scale)))
+        self.has_shared = shared is not None
+        if shared is not None:
+            s13, s13s, s2, s2s = (_u8(t) for t in shared)
+            _expect(s13, (1, 2 * inter, hidden // 2), "shared w13")
+            _expect(s13s, (1, 2 * inter, hidden // 32), "shared w13_scale")
+            _expect(s2, (1, hidden, inter // 2), "shared w2")
+            _expect(s2s, (1, hidden, inter // 32), "shared w2_scale")
+            desc.shared = _lib.MMExpertWeights(*(t.data_ptr() for t in (s13, s13s, s2, s2s)))
+            keep += [s13, s13s, s2, s2s, shared_clamp]
+        desc.clamp = _ptr(clamp)
+        desc.shared_clamp = _ptr(shared_clamp)
+        handle = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            check(lib().mm_layer_create(ctypes.byref(desc), ctypes.byref(handle)), "mm_layer_create")
+        self._handle = handle
+        self._tensors = keep  # the layer reads them in place
+        info = _lib.MMLayerInfo()
+        check(lib().mm_layer_get_info(handle, ctypes.byref(info)), "mm_layer_get_info")
+        self.rows_capacity = int(info.rows_capacity)
+        self.shared_row_base = int(info.shared_row_base)
+        self.route_words_max = int(info.route_words)
+        self.expert_weight_bytes = int(info.weight_bytes)
+
+    def __del__(self):
+        handle = getattr(self, "_handle", None)
+        if handle is not None and handle.value:
+            try:
+                lib().mm_layer_destroy(handle)
+            except Exception:
+                pass
+            self._handle = None
+
+    # ------------------------------------------------------------------ helpers
+    def _check_x(self, x: torch.Tensor) -> int:
+        if x.dtype != torch.bfloat16 or x.dim() != 2 or x.size(1) != self.hidden or not x.is_contiguous():
+            raise ValueError(f"x: expected a contiguous bf16 [T, {self.hidden}] tensor, got {tuple(x.shape)} {x.dtype}")
+        rows = x.size(0)
+        if not 1 <= rows <= self.max_rows:
+            raise ValueError(f"{rows} rows outside 1..{self.max_rows}")
+        return rows
+
+    def _outputs(self, rows: int):
+        dev = self.device
+        permuted = torch.empty((rows, self.top_k), dtype=torch.int32, device=dev)
+        record = torch.empty(route_words(rows, self.top_k, self.experts), dtype=torch.int32, device=dev)
+        out_rows = torch.empty((self.rows_capacity, self.hidden), dtype=torch.bfloat16, device=dev)
+        return permuted, record, out_rows
+
+    def shared_rows(self, rows: torch.Tensor, tokens: int) -> Optional[torch.Tensor]:
+        """The shared expert's bf16 [T, H] output inside a rows buffer."""
+        if not self.has_shared:
+            return None
+        return rows[self.shared_row_base : self.shared_row_base + tokens]
+
+    # ------------------------------------------------------------------ API
+    def __call__(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: Optional[torch.Tensor] = None):
+        """Route + gate_up + down on the current stream from given top-k ids;
+        returns (rows, weights, permuted): rows[permuted[t, k]] is slot (t, k)'s
+        expert output (-1: an expert another rank holds)."""
+        rows = self._check_x(x)
+        if topk_ids.dim() != 2 or tuple(topk_ids.shape) != (rows, self.top_k):
+            raise ValueError(f"topk_ids: expected [{rows}, {self.top_k}], got {tuple(topk_ids.shape)}")
+        ids = topk_ids.to(torch.int32).contiguous()
+        permuted, record, out_rows = self._outputs(rows)
+        check(
+            lib().mm_layer_experts(
+                self._handle, x.data_ptr(), ids.data_ptr(), rows, permuted.data_ptr(), record.data_ptr(),
+                out_rows.data_ptr(), _stream(self.device),
+            ),
+            "mm_layer_experts",
+        )
+        self.last_record = record
+        w = None if topk_weights is None else topk_weights.contiguous().view(rows, self.top_k)
+        return out_rows, w, permuted
+
+    def gate_topk_and_gemms(
+        self,
+        x: torch.Tensor,
+        logits: torch.Tensor,
+        bias: Optional[torch.Tensor],
+        routed_scaling_factor: float,
+        num_valid: Optional[torch.Tensor] = None,
+        *,
+        score: str = "sigmoid",
+        renormalize: bool = True,
+        renormalize_epsilon: float = 0.0,
+        ids_out: Optional[torch.Tensor] = None,
+    ):
+        """Top-k from fp32 router logits, then route + gate_up + down. Returns
+        (rows, weights, permuted, ids)."""
+        rows = self._check_x(x)
+        if logits.dtype != torch.float32 or tuple(logits.shape) != (rows, self.router_experts) or not logits.is_contiguous():
+            raise ValueError(f"logits: expected contiguous fp32 [{rows}, {self.router_experts}]")
+        weights = torch.empty((rows, self.top_k), dtype=torch.float32, device=self.device)
+        ids = ids_out[:rows] if ids_out is not None else torch.empty((rows, self.top_k), dtype=torch.int32, device=self.device)
+        g = gate_args(logits, bias, num_valid, score, renormalize, routed_scaling_factor, renormalize_epsilon, weights, ids)
+        permuted, record, out_rows = self._outputs(rows)
+        check(
+            lib().mm_layer_gate_experts(
+                self._handle, x.data_ptr(), ctypes.byref(g), rows, permuted.data_ptr(), record.data_ptr(),
+                out_rows.data_ptr(), _stream(self.device),
+            ),
+            "mm_layer_gate_experts",
+        )
+        self.last_record = record
+        return out_rows, weights, permuted, ids
+
+    def finalize(self, rows: torch.Tensor, weights: torch.Tensor, permuted: torch.Tensor,
+                 shared_output: Optional[torch.Tensor] = None, partial: bool = False):
+        """Slot-order weighted combine (+ the shared expert). ``shared_output``
+        defaults to the shared expert's rows inside ``rows``. With ``partial``
+        returns the fp32 [2, T, H] un-rounded (routed, shared) sums instead."""
+        tokens = permuted.size(0)
+        if shared_output is None:
+            shared_output = self.shared_rows(rows, tokens)
+        return finalize(rows, weights, permuted, shared_output, partial=partial)
+
+    def forward(
+        self,
+        x: torch.Tensor,
+        *,
+        router_weight: Optional[torch.Tensor] = None,
+        logits: Optional[torch.Tensor] = None,
+        bias: Optional[torch.Tensor] = None,
+        routed_scaling_factor: float = 1.0,
+        num_valid: Optional[torch.Tensor] = None,
+        score: str = "sigmoid",
+        renormalize: bool = True,
+        renormalize_epsilon: float = 0.0,
+        partial: bool = False,
+        buffers: Optional[dict] = None,
+    ):
+        """One whole MoE step on the current stream. Returns the bf16 [T, H]
+        output (or the fp32 [2, T, H] partial sums with ``partial``). ``buffers``
+        (optional dict) receives the intermediate tensors and may carry
+        preallocated ones (keys: logits, weights, ids, permuted, record, rows,
+        out, partial) so repeated calls allocate nothing."""
+        tokens = self._check_x(x)
+        b = {} if buffers is None else buffers
+        dev = self.device
+        if router_weight is not None:
+            if router_weight.dtype != torch.bfloat16 or tuple(router_weight.shape) != (self.router_experts, self.hidden):
+                raise ValueError(f"router_weight: expected bf16 [{self.router_experts}, {self.hidden}]")
+            if b.get("logits") is None or b["logits"].shape[0] != tokens:
+                b["logits"] = torch.empty((tokens, self.router_experts), dtype=torch.float32, device=dev)
+        elif logits is None:
+            raise ValueError("forward needs router_weight or logits")
+
+        def buf(name, shape, dtype):
+            t = b.get(name)
+            if t is None or tuple(t.shape) != tuple(shape) or t.dtype != dtype:
+                t = torch.empty(shape, dtype=dtype, device=dev)
+                b[name] = t
+            return t
+
+        weights = buf("weights", (tokens, self.top_k), torch.float32)
+        ids = buf("ids", (tokens, self.top_k), torch.int32)
+        permuted = buf("permuted", (tokens, self.top_k), torch.int32)
+        record = buf("record", (route_words(tokens, self.top_k, self.experts),), torch.int32)
+        rows = buf("rows", (self.rows_capacity, self.hidden), torch.bfloat16)
+        out = None if partial else buf("out", (tokens, self.hidden), torch.bfloat16)
+        part = buf("partial", (2, tokens, self.hidden), torch.float32) if partial else None
+        a = _lib.MMForwardArgs()
+        a.x = x.data_ptr()
+        a.router_w = _ptr(router_weight)
+        a.logits = _ptr(logits)
+        a.logits_out = _ptr(b.get("logits")) if router_weight is not None else None
+        a.bias = _ptr(bias)
+        a.num_valid = _ptr(num_valid)
+        a.score_func = _lib.SCORES[score]
+        a.renormalize = int(bool(renormalize))
+        a.routed_scaling = float(routed_scaling_factor)
+        a.renorm_eps = float(renormalize_epsilon)
+        a.tokens = tokens
+        a.weights, a.ids, a.permuted, a.record = (t.data_ptr() for t in (weights, ids, permuted, record))
+        a.rows = rows.data_ptr()
+        a.out = _ptr(out)
+        a.partial = _ptr(part)
+        check(lib().mm_layer_forward(self._handle, ctypes.byref(a), _stream(dev)), "mm_layer_forward")
+        return part if partial else out
+
+    def check(self) -> None:
+        """Synchronize and raise if a bounded device wait of this layer timed out."""
+        check(lib().mm_layer_check(self._handle), "mm_layer_check")
+
+
+# ---------------------------------------------------------------------- stateless ops
+def route_words(rows: int, top_k: int, experts: int) -> int:
+    """int32 length of the route record (routed_expert_gemm.py:107-120)."""
+    return int(lib().mm_route_words(rows, top_k, experts))
+
+
+def gate_args(logits, bias, num_valid, score, renormalize, scale, eps, weights, ids) -> _lib.MMGateArgs:
+    if score not in _lib.SCORES:
+        raise ValueError(f"unknown score function {score!r}")
+    if bias is not None and (bias.dtype != torch.float32 or not bias.is_contiguous()):
+        raise ValueError("bias must be a contiguous fp32 tensor")
+    g = _lib.MMGateArgs()
+    g.logits = logits.data_ptr()
+    g.bias = _ptr(bias)
+    g.num_valid = _ptr(num_valid)
+    g.score_func = _lib.SCORES[score]
+    g.renormalize = int(bool(renormalize))
+    g.routed_scaling = float(scale)
+    g.renorm_eps = float(eps)
+    g.weights = weights.data_ptr()
+    g.ids = ids.data_ptr()
+    return g
+
+
+def router_gemv(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    """fp32 logits [T, E] = x bf16 [T, H] @ weight bf16 [E, H]^T (fixed summation order)."""
+    if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise ValueError("router_gemv takes bf16 x and weight")
+    x, weight = x.contiguous(), weight.contiguous()
+    tokens, hidden = x.shape
+    experts = weight.size(0)
+    logits = torch.empty((tokens, experts), dtype=torch.float32, device=x.device)
+    check(
+        lib().mm_router_gemv(x.data_ptr(), weight.data_ptr(), logits.data_ptr(), tokens, experts, hidden, _stream(x.device)),
+        "mm_router_gemv",
+    )
+    return logits
+
+
+def gate_topk(logits: torch.Tensor, bias: Optional[torch.Tensor], top_k: int, *, score: str = "sigmoid",
+              renormalize: bool = True, routed_scaling_factor: float = 1.0, renormalize_epsilon: float = 0.0,
+              num_valid: Optional[torch.Tensor] = None):
+    """(weights fp32 [T, k], ids int32 [T, k]) of the router top-k."""
+    logits = logits.contiguous()
+    tokens, experts = logits.shape
+    weights = torch.empty((tokens, top_k), dtype=torch.float32, device=logits.device)
+    ids = torch.empty((tokens, top_k), dtype=torch.int32, device=logits.device)
+    g = gate_args(logits, bias, num_valid, score, renormalize, routed_scaling_factor, renormalize_epsilon, weights, ids)
+    check(lib().mm_gate_topk(ctypes.byref(g), tokens, experts, top_k, _stream(logits.device)), "mm_gate_topk")
+    return weights, ids
+
+
+def route(ids: torch.Tensor, experts: int, expert_offset: int = 0):
+    """(permuted int32 [T, k], record int32) of given top-k ids (route.cu / route_wide.cu)."""
+    ids = ids.to(torch.int32).contiguous()
+    tokens, top_k = ids.shape
+    permuted = torch.empty_like(ids)
+    record = torch.empty(route_words(tokens, top_k, experts), dtype=torch.int32, device=ids.device)
+    check(
+        lib().mm_route(ids.data_ptr(), permuted.data_ptr(), record.data_ptr(), tokens, top_k, experts, expert_offset,
+                       _stream(ids.device)),
+        "mm_route",
+    )
+    return permuted, record
+
+
+def finalize(rows: torch.Tensor, weights: torch.Tensor, permuted: torch.Tensor,
+             shared_output: Optional[torch.Tensor] = None, partial: bool = False) -> torch.Tensor:
+    """out[t] = bf16(bf16(sum_k w * rows[perm]) + shared[t]) in slot order."""
+    tokens, top_k = permuted.shape
+    hidden = rows.size(1)
+    dev = rows.device
+    out = None if partial else torch.empty((tokens, hidden), dtype=torch.bfloat16, device=dev)
+    part = torch.empty((2, tokens, hidden), dtype=torch.float32, device=dev) if partial else None
+    w = weights.to(torch.float32).contiguous()
+    perm = permuted.to(torch.int32).contiguous()
+    check(
+        lib().mm_finalize(rows.data_ptr(), w.data_ptr(), perm.data_ptr(), _ptr(shared_output), _ptr(out), _ptr(part),
+                          tokens, top_k, hidden, _stream(dev)),
+        "mm_finalize",
+    )
+    return part if partial else out
+
+
+def finalize_partial(partial: torch.Tensor) -> torch.Tensor:
+    """bf16 output from an all-reduced fp32 [2, T, H] partial."""
+    _, tokens, hidden = partial.shape
+    out = torch.empty((tokens, hidden), dtype=torch.bfloat16, device=partial.device)
+    check(lib().mm_finalize_partial(partial.data_ptr(), out.data_ptr(), tokens, hidden, _stream(partial.device)),
+          "mm_finalize_partial")
+    return out

@@ -1,0 +1,205 @@
+"""The CPU oracle against the reference: golden route fixtures generated from the
+reference's own route kernels, the live reference kernels when they are built
+here, and known-answer cases of the reference's routing / quantization rules."""
+
+import ctypes
+import math
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle.oracle as O
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "route_cases.npz")
+
+
+# ------------------------------------------------------------------ route record pins
+def test_route_matches_golden_fixtures():
+    data = np.load(GOLDEN)
+    n = int(data["count"][0])
+    assert n >= 50
+    for i in range(n):
+        ids = data[f"ids_{i}"]
+        local, offset = (int(v) for v in data[f"meta_{i}"])
+        perm, rec = O.route(ids, local, offset)
+        assert np.array_equal(perm, data[f"perm_{i}"]), i
+        assert np.array_equal(rec, data[f"rec_{i}"]), i
+
+
+@pytest.mark.skipif(O.ref_route_lib() is None, reason="reference route kernels not built here")
+def test_route_matches_live_reference():
+    ref = O.ref_route_lib()
+    P = lambda a: a.ctypes.data_as(ctypes.c_void_p)  # noqa: E731
+    rng = np.random.default_rng(5)
+    for _ in range(150):
+        T = int(rng.integers(1, 65))
+        K = int(rng.integers(1, 9))
+        E = int(rng.choice([32, 96, 128, 384]))
+        K = min(K, 512 // T)
+        ids = np.stack([rng.permutation(E)[:K] for _ in range(T)]).astype(np.int32)
+        local, offset = (E, 0) if rng.random() < 0.6 else (E // 2, int(rng.integers(0, 2)) * (E // 2))
+        perm, rec = O.route(ids, local, offset)
+        rp, rr = np.empty_like(perm), np.empty_like(rec)
+        ref.ref_route_wide(P(ids), P(rp), P(rr), T, K, local, offset)
+        assert np.array_equal(perm, rp) and np.array_equal(rec, rr)
+        if T <= 8 and local % 32 == 0:
+            barrier = np.zeros(1, np.uint32)
+            ref.ref_route(P(ids), P(rp), P(rr), P(barrier), T, K, local, offset)
+            assert np.array_equal(perm, rp) and np.array_equal(rec, rr)
+
+
+def test_route_record_layout_known_answer():
+    # two rows, top-2, 8 experts: row 0 -> {3, 1}, row 1 -> {1, 5}
+    ids = np.array([[3, 1], [1, 5]], np.int32)
+    perm, rec = O.route(ids, 8, 0)
+    # experts 1 (rows 0, 1), 3 (row 0), 5 (row 1) -> tiles 0, 1, 2
+    assert perm.tolist() == [[8, 0], [1, 16]]
+    m = 4  # max_ctas: min(8, 4) + 0
+    cw = 4
+    assert rec[0] == 24 and rec[1] == 3 and rec[2] == 0 and rec[3] == 0
+    assert rec[4:4 + 3].tolist() == [1, 3, 5]
+    assert rec[4 + cw:4 + cw + 3].tolist() == [2, 9, 17]
+    tok = rec[4 + 2 * cw:]
+    assert len(tok) == 8 * m
+    assert tok[0] == 0 and tok[1] == 1 and tok[8] == 0 and tok[16] == 1
+
+
+def test_route_words_matches_reference_formula():
+    # routed_expert_gemm.py:107-120
+    for T, K, E in [(1, 6, 384), (8, 8, 384), (64, 8, 384), (48, 6, 192), (256, 16, 1024)]:
+        slots = T * K
+        filled = min(E, slots)
+        m = filled + (slots - filled) // 8
+        assert O.route_words(T, K, E) == 4 + 2 * ((m + 3) // 4 * 4) + 8 * m
+
+
+# ------------------------------------------------------------------ scores and keys
+def test_det_exp_accuracy():
+    L = O.lib()
+    xs = np.concatenate([np.linspace(-103.9, 88.7, 40001), [0.0, -0.0, 1e-30, -1e-30, 1e-7]]).astype(np.float32)
+    got = np.array([L.or_det_exp(float(x)) for x in xs], dtype=np.float32)
+    ref = np.exp(xs.astype(np.float64))
+    ulp = np.abs(got.astype(np.float64) - ref) / np.spacing(ref.astype(np.float32)).astype(np.float64)
+    assert np.nanmax(ulp[ref > 1e-37]) < 1.0
+    assert L.or_det_exp(float("inf")) == float("inf")
+    assert L.or_det_exp(-1e30) == 0.0
+    assert math.isnan(L.or_det_exp(float("nan")))
+
+
+def test_routing_key_orders_and_nan_last():
+    L = O.lib()
+    L.or_routing_key.restype = ctypes.c_uint32
+    L.or_routing_key.argtypes = [ctypes.c_float]
+    vals = [-math.inf, -3.0, -1e-30, -0.0, 0.0, 1e-30, 2.0, math.inf]
+    keys = [L.or_routing_key(v) for v in vals]
+    assert keys == sorted(keys)
+    assert L.or_routing_key(-0.0) == L.or_routing_key(0.0)  # -0 ranks as +0
+    assert L.or_routing_key(float("nan")) < L.or_routing_key(-math.inf)
+
+
+def test_topk_ties_lowest_id_and_nan_rows():
+    # ties go to the lower expert id (gate_topk.cuh:211-290, routing.py:32-70)
+    logits = np.zeros((1, 16), np.float32)
+    logits[0, [3, 7, 11]] = 1.0
+    w, ids = O.gate_topk(logits, None, 4, score="sigmoid")
+    assert ids.tolist() == [[3, 7, 11, 0]]
+    # a NaN logit ranks below every number; an all-NaN row takes the lowest ids
+    logits = np.full((2, 8), np.nan, np.float32)
+    logits[0, 5] = -1e9
+    w, ids = O.gate_topk(logits, None, 2, score="sigmoid")
+    assert ids[0, 0] == 5 and ids[0, 1] == 0
+    assert ids[1].tolist() == [0, 1]
+    # padded rows: id -1, weight 0
+    w, ids = O.gate_topk(np.random.default_rng(0).standard_normal((4, 16)).astype(np.float32), None, 3,
+                         num_valid=2)
+    assert (ids[2:] == -1).all() and (w[2:] == 0).all() and (ids[:2] >= 0).all()
+
+
+def test_topk_weights_renormalized_and_scaled():
+    rng = np.random.default_rng(1)
+    logits = rng.standard_normal((5, 64)).astype(np.float32)
+    bias = (rng.standard_normal(64) * 0.01).astype(np.float32)
+    w, ids = O.gate_topk(logits, bias, 8, score="sigmoid", scale=2.5)
+    assert np.allclose(w.sum(1), 2.5, rtol=1e-6)
+    s = 1 / (1 + np.exp(-logits.astype(np.float64)))
+    keys = s + bias
+    for t in range(5):
+        assert set(ids[t]) == set(np.argsort(-keys[t], kind="stable")[:8])
+        assert np.allclose(w[t], 2.5 * s[t, ids[t]] / s[t, ids[t]].sum(), rtol=1e-5)
+    w, ids = O.gate_topk(logits, None, 6, score="softmax")
+    for t in range(5):
+        top = np.argsort(-logits[t], kind="stable")[:6]
+        assert ids[t].tolist() == top.tolist()
+        e = np.exp(logits[t, top].astype(np.float64) - logits[t, top].max())
+        assert np.allclose(w[t], e / e.sum(), rtol=1e-5)
+    w, _ = O.gate_topk(logits, None, 4, score="sigmoid", renormalize=False, scale=2.0)
+    assert (w <= 2.0).all()
+
+
+# ------------------------------------------------------------------ MX quantization
+def test_mx_scale_code_known_answers():
+    L = O.lib()
+    L.or_mx_scale_code.restype = ctypes.c_uint32
+    L.or_mx_scale_code.argtypes = [ctypes.c_float]
+    assert L.or_mx_scale_code(0.0) == 127     # zero block: scale 1
+    assert L.or_mx_scale_code(448.0) == 127   # exactly representable maximum
+    assert L.or_mx_scale_code(449.0) == 128   # rounded up: never saturates
+    assert L.or_mx_scale_code(224.0) == 126
+    assert L.or_mx_scale_code(1.0) == 119     # 1/448 -> 2^-9 * 1.14 -> exponent -8 after rounding up
+
+
+def test_e4m3_matches_torch_in_range():
+    L = O.lib()
+    v = np.concatenate([np.random.default_rng(2).standard_normal(20000) * 60,
+                        np.linspace(-0.05, 0.05, 4001), [448.0, -448.0, 0.0, -0.0]]).astype(np.float32)
+    v = v[np.abs(v) <= 448]
+    mine = np.array([L.or_e4m3(float(x)) for x in v], dtype=np.uint8)
+    ref = torch.tensor(v).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    assert np.array_equal(mine, ref)
+    assert L.or_e4m3(1e6) == 0x7E and L.or_e4m3(-1e6) == 0xFE  # saturating
+    assert L.or_e4m3(float("nan")) == 0x7F
+
+
+def test_two_term_mxfp8_is_near_exact():
+    v = np.random.default_rng(3).standard_normal((8, 1024)).astype(np.float32)
+    one = O.mxfp8_roundtrip(v, terms=1)
+    two = O.mxfp8_roundtrip(v, terms=2)
+    assert np.abs(one - v).max() / np.abs(v).max() < 2 ** -4
+    assert np.abs(two - v).max() / np.abs(v).max() < 2 ** -8
+
+
+# ------------------------------------------------------------------ GEMV order, combine
+def test_router_gemv_order_is_a_close_sum():
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn((3, 1024), generator=g).to(torch.bfloat16)
+    w = (torch.randn((16, 1024), generator=g) * 0.02).to(torch.bfloat16)
+    got = O.router_gemv(O.bf16_bits(x), O.bf16_bits(w))
+    ref = x.double() @ w.double().T
+    assert np.allclose(got, ref.numpy(), rtol=1e-5, atol=1e-6)
+
+
+def test_finalize_known_answer():
+    def bf(a):
+        return O.bf16_bits(torch.tensor(a, dtype=torch.float32).to(torch.bfloat16))
+
+    rows = bf([[1.0, 2.0], [3.0, -4.0], [100.0, 0.5]])
+    perm = np.array([[0, -1, 1]], np.int32)
+    w = np.array([[0.5, 9.0, 0.25]], np.float32)
+    shared = bf([[1.0, 1.0]])
+    out = O.finalize(rows, w, perm, shared)
+    vals = O.bits_to_f32(out)
+    assert vals.tolist() == [[0.5 + 0.75 + 1.0, 1.0 - 1.0 + 1.0]]
+
+
+def test_moe_layer_oracle_shapes_and_linearity():
+    H, I, E, K, T = 256, 256, 4, 2, 3
+    layer = O.make_layer(H, I, E, shared=True, seed=1)
+    x, _, _ = O.make_inputs(T, H, E, seed=1, router=False)
+    ids = np.array([[0, 1], [1, 2], [3, 0]], np.int32)
+    w = np.ones((T, K), np.float32)
+    out, rows, shared = O.moe_layer(x, ids, w, layer)
+    assert out.shape == (T, H) and len(rows) == T * K and shared.shape == (T, H)
+    out2, _, _ = O.moe_layer(x, ids, 2 * w, layer)
+    assert torch.allclose(out2 - shared, 2 * (out - shared), rtol=1e-5, atol=1e-5)
