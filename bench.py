@@ -1,0 +1,445 @@
+#!/usr/bin/env python
+"""Routed-MoE µs/layer and tokens/s on B200 (BASELINE.json metric).
+
+Workload (all synthetic, seeded; random-init MXFP4 weights of the named shape):
+  N = 1: BASELINE config 2 — one routed-MoE layer, hidden 7168, 384 routed experts
+         + 1 shared (intermediate 2048), sigmoid + fp32 bias top-8, routed scale
+         2.5, MXFP4 weights (E2M1 codes uniform over 16 nibbles, E8M0 exponents
+         uniform in [-10, -6]), 8 tokens of bf16 x ~ N(0, 1).
+  N > 1: the same layer tensor-parallel on the expert intermediate (2048 / N per
+         rank, shared expert split alike), routing replicated on every rank, the
+         fp32 partial sums combined by an NCCL all-reduce; total work fixed
+         ("scaling": "strong").
+A step is one MoE layer over one batch: router GEMV -> top-k -> route ->
+gate_up -> SwiGLU + requant -> down -> combine (-> all-reduce). Each step takes
+the next of 64 resident token batches (distinct routings); one step streams
+~1.4 GB of expert weights, far above the 126 MB L2, so no flush is needed.
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mm|reference]
+Under torchrun each rank drives one GPU; rank 0 prints one JSON line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+for _p in (REPO, os.path.join(REPO, "sgl-nvidia-mega_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+H, I, E, K, SCALE = 7168, 2048, 384, 8, 2.5
+METRIC = "routed-MoE tokens/s per layer (us/layer = 1e3 * ms_per_step)"
+POOL = 64
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--tokens", type=int, default=8)
+    ap.add_argument("--experts", type=int, default=384,
+                    help="routed experts (384 = config 2; fewer only for small profiling cases)")
+    ap.add_argument("--impl", choices=["mm", "reference"], default="mm")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def expert_bytes(hidden, inter):
+    """Algorithmic bytes of one expert's MXFP4 weights: 3 matrices of H x I,
+    half a byte per element plus one E8M0 byte per 32 elements."""
+    return 3 * hidden * inter // 2 + 3 * hidden * inter // 32
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples (every 200 ms) during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        try:
+            with open(self.path) as f:
+                for line in f:
+                    parts = [p.strip() for p in line.split(",")]
+                    if len(parts) >= 9:
+                        rows.append(parts)
+        except Exception:
+            pass
+        finally:
+            if self.path and os.path.exists(self.path):
+                os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# --------------------------------------------------------------------------- layer
+def build_layer(rank, world, tokens, device):
+    import megamoe
+
+    ir = I // world
+    g = torch.Generator(device=device).manual_seed(1000 + rank)
+
+    def rnd(shape, lo, hi):
+        return torch.randint(lo, hi + 1, shape, dtype=torch.uint8, device=device, generator=g)
+
+    w = [rnd((E, 2 * ir, H // 2), 0, 255), rnd((E, 2 * ir, H // 32), 117, 121),
+         rnd((E, H, ir // 2), 0, 255), rnd((E, H, ir // 32), 117, 121)]
+    shared = [rnd((1, 2 * ir, H // 2), 0, 255), rnd((1, 2 * ir, H // 32), 117, 121),
+              rnd((1, H, ir // 2), 0, 255), rnd((1, H, ir // 32), 117, 121)]
+    moe = megamoe.RoutedMoE(*w, K, max(tokens, 8), shared=shared)
+    gx = torch.Generator(device=device).manual_seed(7)  # identical on every rank: replicated routing
+    router = (torch.randn((E, H), device=device, generator=gx) * 0.02).to(torch.bfloat16)
+    bias = (torch.randn((E,), device=device, generator=gx) * 0.01).float()
+    xs = torch.randn((POOL, tokens, H), device=device, generator=gx).to(torch.bfloat16)
+    return moe, w, shared, router, bias, xs
+
+
+def run_mm(args):
+    import megamoe
+
+    global E
+    E = args.experts
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    T = args.tokens
+    moe, w, shared, router, bias, xs = build_layer(rank, world, T, dev)
+    bufs = {}
+    out_buf = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+
+    def step(x):
+        if world == 1:
+            return moe.forward(x, router_weight=router, bias=bias, routed_scaling_factor=SCALE, buffers=bufs)
+        part = moe.forward(x, router_weight=router, bias=bias, routed_scaling_factor=SCALE, partial=True,
+                           buffers=bufs)
+        dist.all_reduce(part)
+        megamoe.finalize_partial(part, out=out_buf)
+        return out_buf
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for i in range(max(args.warmup, 3)):
+        step(xs[i % POOL])
+    moe.check()
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record()
+        for i in range(args.steps):
+            step(xs[i % POOL])
+        end.record()
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    barrier()
+    if dist is not None:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    moe.check()
+    ms_step = ms / args.steps
+    value = T * args.steps / (ms / 1e3)
+
+    # distinct local experts per step (seeded routings, averaged over the pool)
+    distinct = []
+    for i in range(POOL):
+        step(xs[i])
+        distinct.append(int(torch.unique(bufs["ids"]).numel()))
+    torch.cuda.synchronize()
+    d_mean = float(np.mean(distinct))
+    eb = expert_bytes(H, I // world)
+    layer_bytes = (d_mean + 1) * eb + E * H * 2
+
+    # dominant kernel alone: the expert kernel relaunched on the last step's tables
+    last_d = distinct[-1]
+    reps = 200
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    for i in range(3):
+        moe.rerun_experts(T, bufs["record"], bufs["rows"])
+    for a, b in evs:
+        a.record()
+        moe.rerun_experts(T, bufs["record"], bufs["rows"])
+        b.record()
+    torch.cuda.synchronize()
+    k_ms = float(np.mean([a.elapsed_time(b) for a, b in evs]))
+    moe.check()
+    k_bytes = (last_d + 1) * eb
+    peak, peak_kind = peaks()
+    achieved = k_bytes / (k_ms / 1e3) / 1e9
+
+    # end to end through the public API with host buffers
+    host_x = torch.empty((POOL, T, H), dtype=torch.bfloat16).pin_memory()
+    host_x.copy_(xs.cpu())
+    host_out = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
+    xdev = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    e2e_steps = min(args.steps, 1000)
+    barrier()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for i in range(e2e_steps):
+        xdev.copy_(host_x[i % POOL], non_blocking=True)
+        out = step(xdev)
+        host_out.copy_(out, non_blocking=True)
+    e2.record()
+    torch.cuda.synchronize()
+    e2e_ms = s2.elapsed_time(e2)
+    if dist is not None:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = T * e2e_steps / (e2e_ms / 1e3)
+
+    traffic = None
+    tpath = os.path.join(REPO, "profiles", "expert_kernel_traffic.json")
+    if os.path.exists(tpath):
+        try:
+            with open(tpath) as f:
+                tj = json.load(f)
+            if int(tj.get("world", 1)) == world and int(tj.get("tokens", T)) == T:
+                traffic = tj.get("bytes_per_launch")
+        except Exception:
+            traffic = None
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(w, shared, router, bias, xs, T)
+
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_step,
+        "us_per_layer": ms_step * 1e3,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "mxfp4 weights x mxfp8(hi+lo) activations, fp32 accumulate",
+        "data": "synthetic (seeded random MXFP4 weights, bf16 x ~ N(0,1))",
+        "config": {
+            "workload": f"BASELINE config 2: one routed-MoE layer, hidden {H}, {E} routed + 1 shared experts, "
+                        f"intermediate {I}" + (f" (TP{world}: {I // world} per rank)" if world > 1 else "")
+                        + f", sigmoid+bias top-{K}, scale {SCALE}, MXFP4, {T} tokens",
+            "tokens": T,
+            "parallelism": f"tp{world}" if world > 1 else "single",
+            "l2": "inputs larger than L2 (~1.4 GB of expert weights per step, 64 distinct token batches)",
+            "distinct_experts_per_step": d_mean,
+            "layer_weight_bytes": layer_bytes,
+            "layer_roofline_frac": (layer_bytes / (ms_step / 1e3) / 1e9) / peak,
+        },
+        "roofline": {
+            "bound": "hbm",
+            "kernel": "mm::expert_kernel",
+            "achieved": achieved,
+            "peak": peak,
+            "peak_kind": peak_kind,
+            "unit": "GB/s",
+            "frac": achieved / peak,
+            "traffic": traffic,
+            "algorithmic_bytes_per_launch": k_bytes,
+            "launch_ms": k_ms,
+        },
+        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
+                "d2h_bytes_per_step": T * H * 2, "steps": e2e_steps},
+        "gpu_launches": args.steps * (4 if world == 1 else 5),
+        "clocks": clocks.summary(),
+        "cpu_baseline": cpu,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# --------------------------------------------------------------------------- CPU legs
+def _cpu_layer_step(x_bf16, router_bf16, bias, experts_w, shared_w, oracle):
+    logits = oracle.router_gemv(oracle.bf16_bits(x_bf16), oracle.bf16_bits(router_bf16))
+    w, ids = oracle.gate_topk(logits, bias.numpy(), K, scale=SCALE)
+    x = x_bf16.float()
+    out = torch.zeros_like(x)
+    for e in sorted(set(ids.flatten().tolist())):
+        toks = [t for t in range(ids.shape[0]) if e in ids[t]]
+        ws = [float(w[t][list(ids[t]).index(e)]) for t in toks]
+        y = oracle.expert_mlp(x[toks], *experts_w(e), None, "exact")
+        for j, t in enumerate(toks):
+            out[t] += ws[j] * y[j]
+    out += oracle.expert_mlp(x, *shared_w, None, "exact")
+    return out, ids
+
+
+def cpu_baseline(w, shared, router, bias, xs, T):
+    """The oracle port timed on this host's cores: one full layer step of the
+    same workload (all activated experts + shared), after one warm-up step."""
+    from oracle import oracle
+
+    threads = torch.get_num_threads()
+    router_c, bias_c = router.cpu(), bias.cpu()
+    xc = [xs[i].cpu() for i in range(2)]
+    needed = set()
+    for xi in xc:
+        logits = oracle.router_gemv(oracle.bf16_bits(xi), oracle.bf16_bits(router_c))
+        _, ids = oracle.gate_topk(logits, bias_c.numpy(), K, scale=SCALE)
+        needed |= set(ids.flatten().tolist())
+    cache = {e: tuple(t[e].cpu() for t in w) for e in needed}
+    sh = tuple(t[0].cpu() for t in shared)
+    _cpu_layer_step(xc[0], router_c, bias_c, lambda e: cache[e], sh, oracle)  # warm-up
+    t0 = time.perf_counter()
+    _cpu_layer_step(xc[1], router_c, bias_c, lambda e: cache[e], sh, oracle)
+    dt = time.perf_counter() - t0
+    return {"value": T / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"1 full layer step ({T} tokens, every activated expert + shared) after 1 warm-up; "
+                      f"{dt:.1f} s"}
+
+
+def run_reference(args):
+    """The reference path's CPU implementation (the oracle port: the reference
+    itself has no CPU MoE path) on all host threads, on this arm's workload.
+    Each step is a bounded sample: the routing of one token batch plus one of
+    its activated experts' MLP; the layer time is the routing time plus (distinct
+    + 1) times the mean expert time. Steps stop after a ~150 s budget."""
+    from oracle import oracle
+
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    torch.set_num_threads(os.cpu_count() or 1)
+    threads = torch.get_num_threads()
+    T = args.tokens
+    g = torch.Generator().manual_seed(1000)
+
+    def rnd(shape, lo, hi):
+        return torch.randint(lo, hi + 1, shape, dtype=torch.uint8, generator=g)
+
+    gx = torch.Generator().manual_seed(7)
+    router = (torch.randn((E, H), generator=gx) * 0.02).to(torch.bfloat16)
+    bias = (torch.randn((E,), generator=gx) * 0.01).float()
+    x = torch.randn((T, H), generator=gx).to(torch.bfloat16)
+    expert = (rnd((2 * I, H // 2), 0, 255), rnd((2 * I, H // 32), 117, 121), rnd((H, I // 2), 0, 255),
+              rnd((H, I // 32), 117, 121))
+    budget = 150.0
+    route_t, exp_t, distinct = [], [], []
+    t_begin = time.perf_counter()
+    done = 0
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        logits = oracle.router_gemv(oracle.bf16_bits(x), oracle.bf16_bits(router))
+        w, ids = oracle.gate_topk(logits, bias.numpy(), K, scale=SCALE)
+        t1 = time.perf_counter()
+        e = int(ids.flatten()[i % ids.size])
+        toks = [t for t in range(T) if e in ids[t]]
+        oracle.expert_mlp(x[toks].float(), *expert, None, "exact")
+        t2 = time.perf_counter()
+        if i >= args.warmup:
+            route_t.append(t1 - t0)
+            exp_t.append(t2 - t1)
+            distinct.append(len(set(ids.flatten().tolist())))
+            done += 1
+        if time.perf_counter() - t_begin > budget and done >= 3:
+            break
+    layer_s = float(np.mean(route_t)) + (float(np.mean(distinct)) + 1) * float(np.mean(exp_t))
+    value = T / layer_s
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": args.gpus,
+        "steps": done,
+        "warmup": args.warmup,
+        "ms_per_step": layer_s * 1e3,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "fp32 (dequantized MXFP4)",
+        "data": "synthetic (seeded)",
+        "config": {"workload": f"BASELINE config 2 layer (hidden {H}, {E}+1 experts, intermediate {I}, top-{K}, "
+                               f"{T} tokens) on the CPU oracle port",
+                   "tokens": T},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"{done} steps of (routing + 1 activated expert MLP), layer time = routing + "
+                                   f"(distinct + 1) x mean expert time; steps capped by a {budget:.0f} s budget"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_mm(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -470,6 +470,18 @@ static int run_front_and_experts(mm_layer *L, const uint16_t *x, const mm_gate_a
   return MM_OK;
 }
 
+int mm_layer_rerun_experts(mm_layer *L, int32_t tokens, const int32_t *record, uint16_t *rows, void *stream) {
+  if (!L || !record || !rows) return fail(MM_ERR_INVALID, "mm_layer_rerun_experts: null pointer");
+  if (tokens < 1 || tokens > L->Tmax) return fail(MM_ERR_INVALID, "tokens %d outside 1..%d", tokens, L->Tmax);
+  MM_CUDA(cudaSetDevice(L->d.device));
+  ExpertArgs ea = L->ea;
+  ea.rows_out = rows;
+  ea.record = record;
+  ea.token_off = 4 + 2 * route_cta_words(route_max_ctas(tokens, L->K, L->E));
+  MM_CUDA(launch(expert_kernel, dim3(L->num_sms), dim3(kExpertThreads), kSmemAlloc, stream, ea));
+  return MM_OK;
+}
+
 int mm_layer_experts(mm_layer *L, const uint16_t *x, const int32_t *ids, int32_t tokens,
                      int32_t *permuted, int32_t *record, uint16_t *rows, void *stream) {
   if (!L) return fail(MM_ERR_INVALID, "null layer");

@@ -200,6 +200,10 @@ __global__ void __launch_bounds__(kExpertThreads, 1) expert_kernel(const __grid_
       pdl_wait();
       const int nseg = p.ctrl[kCtrlSegments];
       uint32_t stage = 0, phase = 0, ws = 0, wphase = 0, acc = 0, acc_phase = 0;
+      // descriptor words that never change: A/B 128-byte-swizzled K-major with
+      // 1 KB between 8-row groups; scale chunks: 32 rows x 16 B, 128 B apart
+      const uint64_t sw_hi = smem_desc(0, 0, 1024, kLayoutSw128);
+      const uint64_t sf_hi = smem_desc(0, 0, 128, kLayoutNone);
 #pragma unroll 1
       while (true) {
         if (!mbar_wait(bar(kBarWorkFull + ws), wphase, err, kErrTimeoutWork)) break;
@@ -212,10 +216,14 @@ __global__ void __launch_bounds__(kExpertThreads, 1) expert_kernel(const __grid_
         decode_unit(u, nseg, p.m1, p.m2, g2, seg, m);
         const int4 sg = p.segs[seg];
         const uint32_t n = static_cast<uint32_t>((sg.z + 7) & ~7);
+        const uint32_t nmma = n * static_cast<uint32_t>(p.terms);  // hi rows, then lo rows
+        uint32_t idesc[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) idesc[j] = idesc_mxf4_e4m3(nmma, j, j);
         const int ks_n = g2 ? p.ks2 : p.ks1;
         if (!mbar_wait(bar(kBarAccEmpty + acc), acc_phase ^ 1u, err, kErrTimeoutAcc)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tbase + kTmemAcc + acc * kSegRows;
+        const uint32_t d_tmem = tbase + kTmemAcc + acc * kBRows;
         bool ok = true;
 #pragma unroll 1
         for (int ks = 0; ks < ks_n; ++ks) {
@@ -226,29 +234,21 @@ __global__ void __launch_bounds__(kExpertThreads, 1) expert_kernel(const __grid_
           tc_fence_after();
           fence_proxy_async_smem();  // activation rows and B scales arrived via cp.async
           const uint32_t sfa_t = tbase + kTmemSfa + stage * 8;
-          const uint32_t sfb_t = tbase + kTmemSfb + stage * 16;
-          const uint32_t sfa_s = base + kSmemSfa + stage * kSfaStageBytes;
-          const uint32_t sfb_s = base + kSmemSfb + stage * kSfbStageBytes;
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            tc_cp_32x128b_warpx4(sfa_t + 4 * c, smem_desc(sfa_s + 512 * c, 0, 128, kLayoutNone));
-            for (int t = 0; t < p.terms; ++t)
-              tc_cp_32x128b_warpx4(sfb_t + 8 * t + 4 * c,
-                                   smem_desc(sfb_s + kSfbTermBytes * t + 512 * c, 0, 128, kLayoutNone));
-          }
-          const uint32_t sa = base + kSmemA + stage * kAStageBytes;
-          const uint32_t sb = base + kSmemB + stage * kBStageBytes;
+          const uint32_t sfb_t = tbase + kTmemSfb + stage * 8;
+          const uint64_t sfa_d = sf_hi | ((base + kSmemSfa + stage * kSfaStageBytes) >> 4);
+          const uint64_t sfb_d = sf_hi | ((base + kSmemSfb + stage * kSfbStageBytes) >> 4);
+          tc_cp_32x128b_warpx4(sfa_t, sfa_d);
+          tc_cp_32x128b_warpx4(sfa_t + 4, sfa_d + (512 >> 4));
+          tc_cp_32x128b_warpx4(sfb_t, sfb_d);
+          tc_cp_32x128b_warpx4(sfb_t + 4, sfb_d + (512 >> 4));
+          const uint64_t a_d = sw_hi | ((base + kSmemA + stage * kAStageBytes) >> 4);
+          const uint64_t b_d = sw_hi | ((base + kSmemB + stage * kBStageBytes) >> 4);
 #pragma unroll
           for (int kk = 0; kk < kStageK / 32; ++kk) {
             const uint32_t c = kk >> 2, j = kk & 3;
-            const uint64_t adesc = smem_desc(sa + c * kAChunkBytes + j * 32, 0, 1024, kLayoutSw128);
-            const uint32_t idesc = idesc_mxf4_e4m3(n, j, j);
-            for (int t = 0; t < p.terms; ++t) {
-              const uint64_t bdesc =
-                  smem_desc(sb + t * kBTermBytes + c * kBChunkBytes + j * 32, 0, 1024, kLayoutSw128);
-              tc_mma_mxf8f6f4(d_tmem, adesc, bdesc, idesc, sfa_t + 4 * c, sfb_t + 8 * t + 4 * c,
-                              (ks | kk | t) != 0 ? 1u : 0u);
-            }
+            tc_mma_mxf8f6f4(d_tmem, a_d + ((c * kAChunkBytes + j * 32) >> 4),
+                            b_d + ((c * kBChunkBytes + j * 32) >> 4), idesc[j], sfa_t + 4 * c,
+                            sfb_t + 4 * c, (ks | kk) != 0 ? 1u : 0u);
           }
           tc_commit(bar(kBarEmpty + stage));
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
@@ -263,9 +263,15 @@ __global__ void __launch_bounds__(kExpertThreads, 1) expert_kernel(const __grid_
     }
   } else if (warp == 2) {
     // ============================ B loader ===================================
+    // Per unit, every lane fixes its share of the stage once: 16-byte piece
+    // pc = lane % 16 of B rows rr = lane / 16 + 2 i (hi rows [0, n), lo rows
+    // [n, 2n)); per stage it only issues the copies at the stage's K offset.
     pdl_wait();
     const int nseg = p.ctrl[kCtrlSegments];
     uint32_t stage = 0, phase = 0, ws = 0, wphase = 0;
+    const int pc = lane & 15;           // 16-byte piece of the 256-byte stage row
+    const int half = lane >> 4;
+    const int pc_c = pc >> 3, pc_j = pc & 7;
 #pragma unroll 1
     while (true) {
       int u = -1, okw = 1;
@@ -286,6 +292,7 @@ __global__ void __launch_bounds__(kExpertThreads, 1) expert_kernel(const __grid_
       const int4 sg = p.segs[seg];
       const int rows = sg.z;
       const int n = (rows + 7) & ~7;
+      const int nb = n * p.terms;         // B rows of this unit
       if (g2) {
         int okf = 1;
         if (lane == 0) okf = wait_flag(p.flags + seg, 2 * p.m1, err) ? 1 : 0;
@@ -299,13 +306,38 @@ __global__ void __launch_bounds__(kExpertThreads, 1) expert_kernel(const __grid_
         else src = sg.w >= 0 ? sg.w + lane : __ldg(p.record + p.token_off + sg.y + lane);
       }
       const int K = g2 ? p.inter : p.hidden;
-      const int ks_n = g2 ? p.ks2 : p.ks1;
       const uint8_t *dq = g2 ? p.hq : p.xq;
       const uint8_t *dsc = g2 ? p.hs : p.xs;
-      const size_t term_q = static_cast<size_t>(g2 ? p.rows_cap : p.max_tokens) * K;
-      const size_t term_s = term_q >> 5;
-      const int data_pieces = p.terms * n * 16;  // 16-byte pieces per stage (multiple of 32)
-      const int scale_pieces = p.terms * n * 2;  // 4-byte pieces per stage
+      const uint32_t term_q = static_cast<uint32_t>(g2 ? p.rows_cap : p.max_tokens) * static_cast<uint32_t>(K);
+      const uint32_t term_s = term_q >> 5;
+      // data pieces: up to 16 per lane
+      uint32_t soff[kBRows / 2], doff[kBRows / 2], sbytes[kBRows / 2];
+#pragma unroll
+      for (int i = 0; i < kBRows / 2; ++i) {
+        const int rr = half + 2 * i;
+        const int t = rr >= n ? 1 : 0;
+        const int r = rr - t * n;
+        const int sr = __shfl_sync(0xffffffffu, src, r & 31);
+        soff[i] = static_cast<uint32_t>(t) * term_q + static_cast<uint32_t>(sr) * K + pc * 16;
+        doff[i] = pc_c * kBChunkBytes + (rr >> 3) * 1024 + (rr & 7) * 128 + ((pc_j ^ (rr & 7)) << 4);
+        sbytes[i] = (rr < nb && r < rows) ? 16u : 0u;
+      }
+      // scale pieces: B row rr = lane (and lane + 32 never: nb <= 32), chunks 0 and 1
+      uint32_t s_soff[2], s_doff[2], s_bytes[2];
+      {
+        const int rr = lane;
+        const int t = rr >= n ? 1 : 0;
+        const int r = rr - t * n;
+        const int sr = __shfl_sync(0xffffffffu, src, r & 31);
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          s_soff[c] = static_cast<uint32_t>(t) * term_s + static_cast<uint32_t>(sr) * (K >> 5) + c * 4;
+          s_doff[c] = c * 512 + rr * 16;
+          s_bytes[c] = (rr < nb && r < rows) ? 4u : 0u;
+        }
+      }
+      const bool issue_scale = lane < nb;
+      const int ks_n = g2 ? p.ks2 : p.ks1;
 #pragma unroll 1
       for (int ks = 0; ks < ks_n; ++ks) {
         int oke = 1;
@@ -313,32 +345,16 @@ __global__ void __launch_bounds__(kExpertThreads, 1) expert_kernel(const __grid_
         oke = __shfl_sync(0xffffffffu, oke, 0);
         if (!oke) break;
         const uint32_t sb = base + kSmemB + stage * kBStageBytes;
-        const uint32_t ssb = base + kSmemSfb + stage * kSfbStageBytes;
-#pragma unroll 1
-        for (int i0 = 0; i0 < data_pieces; i0 += 32) {
-          const int idx = i0 + lane;
-          const int t = idx / (n * 16);
-          const int rem = idx - t * n * 16;
-          const int r = rem >> 4, pc = rem & 15;
-          const int c = pc >> 3, j = pc & 7;
-          const int sr = __shfl_sync(0xffffffffu, src, r & 31);
-          const uint8_t *g = dq + t * term_q + static_cast<size_t>(sr) * K + ks * kStageK + c * 128 + j * 16;
-          const uint32_t d = sb + t * kBTermBytes + c * kBChunkBytes + (r >> 3) * 1024 + (r & 7) * 128 +
-                             ((j ^ (r & 7)) << 4);
-          cp_async_16(d, g, r < rows ? 16u : 0u);
+        const uint8_t *gq = dq + ks * kStageK;
+#pragma unroll
+        for (int i = 0; i < kBRows / 2; ++i) {
+          if (half + 2 * i < nb) cp_async_16(sb + doff[i], gq + soff[i], sbytes[i]);
         }
-#pragma unroll 1
-        for (int i0 = 0; i0 < scale_pieces; i0 += 32) {
-          const int idx = i0 + lane;
-          const int t = idx / (n * 2);
-          const int rem = idx - t * n * 2;
-          const int r = rem >> 1, c = rem & 1;
-          const int sr = __shfl_sync(0xffffffffu, src, r & 31);
-          if (idx < scale_pieces) {
-            const uint8_t *g = dsc + t * term_s + static_cast<size_t>(sr) * (K >> 5) + ks * 8 + c * 4;
-            const uint32_t d = ssb + t * kSfbTermBytes + c * 512 + r * 16;
-            cp_async_4(d, g, r < rows ? 4u : 0u);
-          }
+        if (issue_scale) {
+          const uint32_t ssb = base + kSmemSfb + stage * kSfbStageBytes;
+          const uint8_t *gs = dsc + ks * 8;
+          cp_async_4(ssb + s_doff[0], gs + s_soff[0], s_bytes[0]);
+          cp_async_4(ssb + s_doff[1], gs + s_soff[1], s_bytes[1]);
         }
         cp_async_arrive_noinc(bar(kBarFull + stage));
         if (++stage == kStages) { stage = 0; phase ^= 1u; }
@@ -375,18 +391,27 @@ __global__ void __launch_bounds__(kExpertThreads, 1) expert_kernel(const __grid_
       decode_unit(u, nseg, p.m1, p.m2, g2, seg, m);
       const int4 sg = p.segs[seg];
       const int rows = sg.z;
+      const int n = (rows + 7) & ~7;
       int ok = 1;
       if (lane == 0) ok = mbar_wait(bar(kBarAccFull + acc), acc_phase, err, kErrTimeoutAcc) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       tc_fence_after();
-      uint32_t v[16];
-      tc_ld_32x32b_x16(tbase + (static_cast<uint32_t>(32 * q) << 16) + kTmemAcc + acc * kSegRows, v);
+      uint32_t raw[kBRows];
+      tc_ld_32x32b_x32(tbase + (static_cast<uint32_t>(32 * q) << 16) + kTmemAcc + acc * kBRows, raw);
       tc_wait_ld();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(kBarAccEmpty + acc));
       if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      // column j holds the hi-term product of segment row j, column n + j the lo term
+      float v[kSegRows];
+#pragma unroll
+      for (int j = 0; j < kSegRows; ++j) {
+        float a = __uint_as_float(raw[j]);
+        if (p.terms > 1) a = __fadd_rn(a, __uint_as_float(n == 8 ? raw[8 + j] : raw[16 + j]));
+        v[j] = a;
+      }
       if (!g2) {
         // rows 0..63: gate of features 64m + row; rows 64..127: up of the same features
         if (q >= 2) {
@@ -394,7 +419,7 @@ __global__ void __launch_bounds__(kExpertThreads, 1) expert_kernel(const __grid_
           ok = __shfl_sync(0xffffffffu, ok, 0);
           if (!ok) break;
 #pragma unroll
-          for (int j = 0; j < kSegRows; ++j) ex[(row - 64) * kSegRows + j] = __uint_as_float(v[j]);
+          for (int j = 0; j < kSegRows; ++j) ex[(row - 64) * kSegRows + j] = v[j];
           __syncwarp();
           if (lane == 0) mbar_arrive(bar(kBarExFull));
         } else {
@@ -414,7 +439,7 @@ __global__ void __launch_bounds__(kExpertThreads, 1) expert_kernel(const __grid_
 #pragma unroll
           for (int j = 0; j < kSegRows; ++j) {
             if (j >= rows) break;
-            float g = __uint_as_float(v[j]);
+            float g = v[j];
             float up = upv[j];
             if (clamped) {
               up = fminf(fmaxf(up, -L), L);
@@ -449,7 +474,7 @@ __global__ void __launch_bounds__(kExpertThreads, 1) expert_kernel(const __grid_
 #pragma unroll
         for (int j = 0; j < kSegRows; ++j) {
           if (j >= rows) break;
-          p.rows_out[static_cast<size_t>(sg.y + j) * p.hidden + col] = float_to_bf16_bits(__uint_as_float(v[j]));
+          p.rows_out[static_cast<size_t>(sg.y + j) * p.hidden + col] = float_to_bf16_bits(v[j]);
         }
       }
     }
@@ -461,6 +486,19 @@ __global__ void __launch_bounds__(kExpertThreads, 1) expert_kernel(const __grid_
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tbase, kTmemCols);
+  }
+  // The last CTA to finish re-arms the work tables (claim counter, mailboxes),
+  // so the kernel can be launched again on the same front-kernel output.
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int done = atomicAdd(&p.ctrl[kCtrlDone], 1);
+    if (done == static_cast<int>(gridDim.x) - 1) {
+      __threadfence();
+      const int nseg = *reinterpret_cast<volatile int *>(&p.ctrl[kCtrlSegments]);
+      for (int s = 0; s < nseg; ++s) p.flags[s] = 0;
+      p.ctrl[kCtrlClaim] = 0;
+      p.ctrl[kCtrlDone] = 0;
+    }
   }
 }
 

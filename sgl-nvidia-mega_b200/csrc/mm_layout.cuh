@@ -51,6 +51,7 @@ constexpr int kCtrlSegments = 0;  // number of segments
 constexpr int kCtrlUnits = 1;     // gate_up units + down units
 constexpr int kCtrlClaim = 2;     // next unit to claim (reset to 0 by the front kernel)
 constexpr int kCtrlTicket = 3;    // front kernel's last-CTA ticket (reset by the last CTA)
+constexpr int kCtrlDone = 4;      // expert kernel's finished CTAs (reset by the last CTA)
 constexpr int kCtrlWords = 8;
 
 // ---- the persistent expert kernel's shared memory -----------------------------------
@@ -58,13 +59,15 @@ constexpr int kStages = 5;
 constexpr int kStageK = 256;                  // K elements per pipeline stage
 constexpr int kAStageBytes = 128 * kStageK;   // 4-bit codes in 8-bit slots: 32 KB
 constexpr int kAChunkBytes = 128 * 128;       // one 128-K chunk of 128 rows
-constexpr int kBTermBytes = kSegRows * kStageK;  // 16 rows x 256 B
-constexpr int kBStageBytes = 2 * kBTermBytes;    // hi + lo
-constexpr int kBChunkBytes = kSegRows * 128;     // one 128-K chunk of the 16 rows
+// B (activation) rows of a stage: the hi terms of the segment's n rows at rows
+// [0, n), the lo terms at [n, 2n) (n = rows rounded up to 8), so one MMA with
+// N = 2n accumulates both terms in separate accumulator columns.
+constexpr int kBRows = 2 * kSegRows;            // 32
+constexpr int kBStageBytes = kBRows * kStageK;  // 8 KB
+constexpr int kBChunkBytes = kBRows * 128;      // one 128-K chunk of the 32 rows
 constexpr int kSfaStageBytes = 1024;          // 2 chunks x 512 B
-constexpr int kSfbTermBytes = 1024;           // 2 chunks x 512 B
-constexpr int kSfbStageBytes = 2 * kSfbTermBytes;
-constexpr int kEpiBytes = 128 * kSegRows * 4; // epilogue exchange / transpose
+constexpr int kSfbStageBytes = 1024;          // 2 chunks x (32 rows x 16 B)
+constexpr int kEpiBytes = 64 * kSegRows * 4;  // gate_up epilogue exchange
 constexpr int kWorkSlots = 4;
 
 constexpr int kSmemA = 0;
@@ -92,13 +95,13 @@ constexpr int kSmemAlloc = kSmemTotal + 1024;  // room to align the base to 1 KB
 static_assert(kSmemAlloc <= 232448, "expert kernel shared memory over the 227 KB limit");
 static_assert(kSmemB % 1024 == 0 && kSmemSfa % 128 == 0 && kSmemSfb % 128 == 0, "alignment");
 
-// TMEM columns: 2 accumulators of kSegRows fp32 columns, then per stage the
-// A scale chunks (8 columns) and the B scale chunks of both terms (16 columns).
+// TMEM columns: 2 accumulators of kBRows fp32 columns, then per stage the A
+// scale chunks (8 columns) and the B scale chunks (8 columns).
 constexpr int kTmemAcc = 0;
-constexpr int kTmemSfa = 2 * kSegRows;
+constexpr int kTmemSfa = 2 * kBRows;
 constexpr int kTmemSfb = kTmemSfa + kStages * 8;
 constexpr int kTmemCols = 256;
-static_assert(kTmemSfb + kStages * 16 <= kTmemCols, "TMEM columns");
+static_assert(kTmemSfb + kStages * 8 <= kTmemCols, "TMEM columns");
 
 constexpr int kExpertThreads = 224;  // 7 warps: producer, MMA, B loader, 4 epilogue
 

@@ -130,6 +130,7 @@ SIGNATURES = {
         c_int32,
         [c_void_p, c_void_p, POINTER(MMGateArgs), c_int32, c_void_p, c_void_p, c_void_p, c_void_p],
     ),
+    "mm_layer_rerun_experts": (c_int32, [c_void_p, c_int32, c_void_p, c_void_p, c_void_p]),
     "mm_layer_forward": (c_int32, [c_void_p, POINTER(MMForwardArgs), c_void_p]),
     "mm_layer_check": (c_int32, [c_void_p]),
 }

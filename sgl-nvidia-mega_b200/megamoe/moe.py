@@ -293,6 +293,12 @@ class RoutedMoE:
         check(lib().mm_layer_forward(self._handle, ctypes.byref(a), _stream(dev)), "mm_layer_forward")
         return part if partial else out
 
+    def rerun_experts(self, tokens: int, record: torch.Tensor, rows: torch.Tensor) -> None:
+        """Launch the expert kernel again on the last front pass's work tables
+        (benchmark hook: times the dominant kernel alone)."""
+        check(lib().mm_layer_rerun_experts(self._handle, tokens, record.data_ptr(), rows.data_ptr(),
+                                            _stream(self.device)), "mm_layer_rerun_experts")
+
     def check(self) -> None:
         """Synchronize and raise if a bounded device wait of this layer timed out."""
         check(lib().mm_layer_check(self._handle), "mm_layer_check")
@@ -382,10 +388,11 @@ def finalize(rows: torch.Tensor, weights: torch.Tensor, permuted: torch.Tensor,
     return part if partial else out
 
 
-def finalize_partial(partial: torch.Tensor) -> torch.Tensor:
+def finalize_partial(partial: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """bf16 output from an all-reduced fp32 [2, T, H] partial."""
     _, tokens, hidden = partial.shape
-    out = torch.empty((tokens, hidden), dtype=torch.bfloat16, device=partial.device)
+    if out is None:
+        out = torch.empty((tokens, hidden), dtype=torch.bfloat16, device=partial.device)
     check(lib().mm_finalize_partial(partial.data_ptr(), out.data_ptr(), tokens, hidden, _stream(partial.device)),
           "mm_finalize_partial")
     return out
