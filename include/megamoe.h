@@ -60,7 +60,7 @@ extern "C" {
  *   w13_scale u8 [n, 2*I, H/32] E8M0 (value 2^(byte-127)) per 32 elements
  *   w2        u8 [n, H, I/2]
  *   w2_scale  u8 [n, H, I/32]
- * w13 and w2 must be 32-byte aligned (TMA unpacking of 4-bit data). */
+ * w13 and w2 must be 16-byte aligned (TMA tensor maps). */
 typedef struct mm_expert_weights {
   const void *w13;
   const void *w13_scale;
@@ -69,7 +69,7 @@ typedef struct mm_expert_weights {
 } mm_expert_weights;
 
 typedef struct mm_layer_desc {
-  int32_t hidden;         /* H: multiple of 1024                                   */
+  int32_t hidden;         /* H: multiple of 256 (router GEMV: multiple of 1024)    */
   int32_t intermediate;   /* I (this rank's slice): multiple of 256                */
   int32_t experts;        /* local routed experts (this rank's window)             */
   int32_t router_experts; /* experts the router scores (>= expert_offset+experts)  */
@@ -77,8 +77,10 @@ typedef struct mm_layer_desc {
   int32_t top_k;          /* 1..16                                                 */
   int32_t max_tokens;     /* largest T a call may pass: 1..256                     */
   int32_t weight_format;  /* MM_WEIGHT_MXFP4                                       */
-  int32_t act_terms;      /* 2: activations as hi+lo MXFP8 (default numerics);
-                             1: single MXFP8 (the reference kernels' numerics)     */
+  int32_t act_terms;      /* MXFP4 terms carrying each activation into the GEMMs:
+                             x ~ t0 + t1 + t2, t_i the MXFP4 quantization of the
+                             residual of the earlier terms. 1..3; 3 is the default
+                             numerics (about 1e-3 relative), 1 is plain MXFP4.      */
   int32_t device;         /* CUDA device ordinal the weights live on               */
   mm_expert_weights routed; /* n = experts                                         */
   mm_expert_weights shared; /* n = 1; shared.w13 == NULL: no shared expert          */

@@ -9,7 +9,7 @@
  *
  * Parity pins: or_route is checked against the reference's own route.cuh /
  * route_wide.cu compiled for the CPU (oracle/ref_route_shim.h, oracle/Makefile,
- * tests/test_oracle_pins.py); the fixtures under tests/golden/ were generated
+ * tests/test_oracle.py); the fixtures under tests/golden/ were generated
  * from it (tests/golden/make_golden.py).
  */
 #include <math.h>
@@ -280,6 +280,72 @@ void or_mxfp8_quant(const float *v, int nblocks, int terms, uint8_t *q_hi, uint8
     const float inv2 = mx_inverse(c2);
     for (int i = 0; i < 32; ++i) q_lo[(size_t)b * 32 + i] = or_e4m3(r[i] * inv2);
     s_lo[b] = (uint8_t)c2;
+  }
+}
+
+/* ---------------------------------------------------------------------------
+ * MXFP4 terms of the activations (the kernels' numerics: E2M1 codes, E8M0 scale
+ * per 32): per block, term t quantizes the residual r left by the earlier terms:
+ * amax of |r| (6 when zero) times fp32(1/6), E8M0 code = that product's
+ * exponent, rounded up when its mantissa is not zero (the MX rule above with
+ * E2M1's largest magnitude 6); codes e2m1(r * 2^(127-code)), round to nearest
+ * even, saturating at 6; r -= value(code) * 2^(code-127). Two codes per byte,
+ * the even element in the low nibble.
+ * ------------------------------------------------------------------------- */
+uint32_t or_mx4_scale_code(float amax) {
+  const float num = amax == 0.0f ? 6.0f : amax;
+  const uint32_t b = f2u(num * 0x1.555556p-3f);
+  const uint32_t ex = (b >> 23) & 0xffu, ma = b & 0x7fffffu;
+  uint32_t code = ex;
+  if (ma != 0u && ex != 254u) {
+    if (ex != 0u) code = ex + 1u;
+    else if (ma > 0x400000u) code = 1u;
+  }
+  if (ex == 255u) code = 255u;
+  return code;
+}
+
+/* E2M1 code (bits 0-3) of v: round to nearest, ties to the even code, |v| > 6 -> 6 */
+uint8_t or_e2m1(float v) {
+  const uint8_t sign = (f2u(v) >> 31) ? 8u : 0u;
+  const float a = fabsf(v);
+  uint8_t m;
+  if (a != a) m = 7;
+  else if (a <= 0.25f) m = 0;
+  else if (a < 0.75f) m = 1;
+  else if (a <= 1.25f) m = 2;
+  else if (a < 1.75f) m = 3;
+  else if (a <= 2.5f) m = 4;
+  else if (a < 3.5f) m = 5;
+  else if (a <= 5.0f) m = 6;
+  else m = 7;
+  return sign | m;
+}
+
+float or_e2m1_value(uint8_t c) {
+  static const float mag[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+  const float v = mag[c & 7u];
+  return (c & 8u) ? -v : v;
+}
+
+/* v: nblocks x 32 values; q: [terms][nblocks * 16] bytes; s: [terms][nblocks] */
+void or_fp4_quant(const float *v, int nblocks, int terms, uint8_t *q, uint8_t *s) {
+  for (int b = 0; b < nblocks; ++b) {
+    float r[32];
+    for (int i = 0; i < 32; ++i) r[i] = v[(size_t)b * 32 + i];
+    for (int t = 0; t < terms; ++t) {
+      float amax = 0.0f;
+      for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(r[i]));
+      const uint32_t c = or_mx4_scale_code(amax);
+      const float inv = mx_inverse(c), sv = mx_scale_value(c);
+      for (int i = 0; i < 32; i += 2) {
+        const uint8_t lo = or_e2m1(r[i] * inv), hi = or_e2m1(r[i + 1] * inv);
+        q[(size_t)t * nblocks * 16 + (size_t)b * 16 + i / 2] = (uint8_t)(lo | (hi << 4));
+        r[i] = r[i] - or_e2m1_value(lo) * sv;
+        r[i + 1] = r[i + 1] - or_e2m1_value(hi) * sv;
+      }
+      s[(size_t)t * nblocks + b] = (uint8_t)c;
+    }
   }
 }
 

@@ -9,7 +9,7 @@ import this module. It restates the reference's algorithm for each step:
   * the dense expert MLP by dequantize -> fp32 matmul (torch on the CPU), in two
     numerics: "exact" (bf16 input, fp32 throughout: BASELINE's tolerance
     reference) and "kernel" (the inputs of both GEMMs passed through the same
-    MXFP8 terms the kernels use, outputs rounded to bf16 rows).
+    MXFP4 activation terms the kernels use).
 
 MXFP4 codec: OCP MX E2M1 (+-{0, .5, 1, 1.5, 2, 3, 4, 6}), byte = element 2j in the
 low nibble and 2j+1 in the high nibble; E8M0 scale 2^(byte - 127) per 32
@@ -139,13 +139,43 @@ def mxfp8_dequant(q: np.ndarray, s: np.ndarray) -> np.ndarray:
     return (vals.reshape(*s.shape, 32) * scale[..., None]).reshape(q.shape)
 
 
-def mxfp8_roundtrip(v: np.ndarray, terms: int = 2) -> np.ndarray:
-    """The value the kernels multiply in place of v: sum of the MXFP8 terms."""
+def mxfp8_roundtrip(v: np.ndarray, terms: int = 1) -> np.ndarray:
+    """v through MXFP8 (the reference kernels' activation numerics; terms 2 adds
+    the MXFP8 residual term)."""
     qh, ql, sh, sl = mxfp8_quant(v, terms)
     out = mxfp8_dequant(qh, sh)
     if terms > 1:
         out = out + mxfp8_dequant(ql, sl)
     return out
+
+
+def fp4_quant(v: np.ndarray, terms: int = 3):
+    """fp32 [..., K] -> (codes u8 [terms, ..., K/2], scales u8 [terms, ..., K/32]):
+    the kernels' MXFP4 activation terms."""
+    v = np.ascontiguousarray(v, dtype=np.float32)
+    nb = v.size // 32
+    q = np.zeros((terms, nb * 16), dtype=np.uint8)
+    s = np.zeros((terms, nb), dtype=np.uint8)
+    lib().or_fp4_quant(_p(v), nb, terms, _p(q), _p(s))
+    lead = v.shape[:-1]
+    return q.reshape(terms, *lead, v.shape[-1] // 2), s.reshape(terms, *lead, v.shape[-1] // 32)
+
+
+def fp4_dequant(q: np.ndarray, s: np.ndarray) -> np.ndarray:
+    """Sum of the MXFP4 terms (exact)."""
+    lo = E2M1[q & 0x0F]
+    hi = E2M1[q >> 4]
+    vals = np.stack([lo, hi], axis=-1).reshape(*q.shape[:-1], q.shape[-1] * 2)
+    scale = np.exp2(s.astype(np.float32) - 127.0).astype(np.float32)
+    out = (vals.reshape(*s.shape, 32) * scale[..., None]).reshape(vals.shape)
+    return out.sum(axis=0)
+
+
+def act_roundtrip(v: np.ndarray, terms: int = 3) -> np.ndarray:
+    """The value the kernels multiply in place of activation v: the sum of its
+    MXFP4 terms."""
+    q, s = fp4_quant(v, terms)
+    return fp4_dequant(q, s).astype(np.float32)
 
 
 def finalize(rows_bf16: np.ndarray, weights: np.ndarray, permuted: np.ndarray,
@@ -188,13 +218,13 @@ def dequant_mxfp4(codes: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
 
 
 def expert_mlp(x: torch.Tensor, w13: torch.Tensor, s13: torch.Tensor, w2: torch.Tensor, s2: torch.Tensor,
-               clamp: Optional[float], numerics: str, terms: int = 2) -> torch.Tensor:
+               clamp: Optional[float], numerics: str, terms: int = 3) -> torch.Tensor:
     """fp32 [n, H] of one expert on fp32 rows x [n, H] (CPU)."""
     inter = w13.shape[0] // 2
     W13 = dequant_mxfp4(w13, s13)
     xin = x
     if numerics == "kernel":
-        xin = torch.from_numpy(mxfp8_roundtrip(x.numpy(), terms))
+        xin = torch.from_numpy(act_roundtrip(x.numpy(), terms))
     gu = xin @ W13.T
     gate, up = gu[:, :inter], gu[:, inter:]
     if clamp is not None:
@@ -202,13 +232,13 @@ def expert_mlp(x: torch.Tensor, w13: torch.Tensor, s13: torch.Tensor, w2: torch.
         gate = gate.clamp(max=clamp)
     h = up * (gate * torch.sigmoid(gate))
     if numerics == "kernel":
-        h = torch.from_numpy(mxfp8_roundtrip(h.numpy(), terms))
+        h = torch.from_numpy(act_roundtrip(h.numpy(), terms))
     W2 = dequant_mxfp4(w2, s2)
     return h @ W2.T
 
 
 def moe_layer(x_bf16: torch.Tensor, ids: np.ndarray, weights: np.ndarray, layer: dict, *, numerics: str = "exact",
-              terms: int = 2, expert_offset: int = 0, local_experts: Optional[int] = None):
+              terms: int = 3, expert_offset: int = 0, local_experts: Optional[int] = None):
     """Oracle of one MoE layer given routing. Returns (out fp32 [T, H] before
     bf16 rounding of the final sum, per-slot rows fp32 {(t, k): [H]}, shared
     fp32 [T, H] or None). Weights are CPU uint8 tensors in the canonical layout."""

@@ -78,20 +78,21 @@ int get_encode(EncodeTiledFn *fn) {
   return MM_OK;
 }
 
-// 3-D map of packed E2M1 codes [n][rows][k/2] u8 as {k, rows, n} 4-bit elements,
-// box {128, box_rows, 1}, unpacked to 8-bit slots, 128-byte swizzle.
+// 3-D map of packed E2M1 codes [n][rows][k/2] u8 as bytes {k/2, rows, n}, box
+// {128 bytes (256 codes), box_rows, 1}, 128-byte swizzle: one box lands a
+// K = 256 slice of box_rows weight rows as the K-major layout tcgen05 reads.
 int encode_fp4_map(CUtensorMap *map, const void *base, int k, int rows, int n, int box_rows) {
   EncodeTiledFn enc;
   int rc = get_encode(&enc);
   if (rc) return rc;
-  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows),
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(k) / 2, static_cast<cuuint64_t>(rows),
                               static_cast<cuuint64_t>(n)};
   const cuuint64_t strides[2] = {static_cast<cuuint64_t>(k) / 2,
                                  static_cast<cuuint64_t>(k) / 2 * static_cast<cuuint64_t>(rows)};
   const cuuint32_t box[3] = {128u, static_cast<cuuint32_t>(box_rows), 1u};
   const cuuint32_t estr[3] = {1u, 1u, 1u};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 3, const_cast<void *>(base), dims,
-                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides, box,
+                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(MM_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
   return MM_OK;
@@ -232,8 +233,8 @@ static void free_layer(mm_layer *L) {
 
 static int check_weights(const mm_expert_weights &w, const char *what) {
   if (!w.w13 || !w.w13_scale || !w.w2 || !w.w2_scale) return fail(MM_ERR_INVALID, "%s: null weight pointer", what);
-  if (!aligned(w.w13, 32) || !aligned(w.w2, 32))
-    return fail(MM_ERR_INVALID, "%s: packed weights must be 32-byte aligned", what);
+  if (!aligned(w.w13, 16) || !aligned(w.w2, 16))
+    return fail(MM_ERR_INVALID, "%s: packed weights must be 16-byte aligned", what);
   return MM_OK;
 }
 
@@ -253,7 +254,8 @@ int mm_layer_create(const mm_layer_desc *desc, mm_layer **out) {
   if (d.top_k < 1 || d.top_k > kMaxTopK) return fail(MM_ERR_INVALID, "top_k %d outside 1..%d", d.top_k, kMaxTopK);
   if (d.max_tokens < 1 || d.max_tokens > kMaxTokens) return fail(MM_ERR_INVALID, "max_tokens %d outside 1..%d", d.max_tokens, kMaxTokens);
   if (d.weight_format != MM_WEIGHT_MXFP4) return fail(MM_ERR_UNSUPPORTED, "weight format %d is not built (MXFP4)", d.weight_format);
-  if (d.act_terms != 1 && d.act_terms != 2) return fail(MM_ERR_INVALID, "act_terms %d must be 1 or 2", d.act_terms);
+  if (d.act_terms < 1 || d.act_terms > kMaxTerms)
+    return fail(MM_ERR_INVALID, "act_terms %d outside 1..%d", d.act_terms, kMaxTerms);
   int rc = check_weights(d.routed, "routed");
   if (rc) return rc;
   const int has_shared = d.shared.w13 != nullptr;
@@ -306,10 +308,12 @@ int mm_layer_create(const mm_layer_desc *desc, mm_layer **out) {
     ALLOC(L->ssfa13, static_cast<size_t>(L->m1) * L->ks1 * 1024);
     ALLOC(L->ssfa2, static_cast<size_t>(L->m2) * L->ks2 * 1024);
   }
-  ALLOC(L->xq, 2 * static_cast<size_t>(L->Tmax) * H);
-  ALLOC(L->xs, 2 * static_cast<size_t>(L->Tmax) * H / 32);
-  ALLOC(L->hq, 2 * static_cast<size_t>(L->rows_cap) * I);
-  ALLOC(L->hs, 2 * static_cast<size_t>(L->rows_cap) * I / 32);
+  const size_t xq_bytes = kMaxTerms * static_cast<size_t>(L->Tmax) * H / 2;
+  const size_t hq_bytes = kMaxTerms * static_cast<size_t>(L->rows_cap) * I / 2;
+  ALLOC(L->xq, xq_bytes);
+  ALLOC(L->xs, xq_bytes / 16);
+  ALLOC(L->hq, hq_bytes);
+  ALLOC(L->hs, hq_bytes / 16);
   ALLOC(L->segs, sizeof(int4) * L->max_segs);
   ALLOC(L->ctrl, sizeof(int) * kCtrlWords);
   ALLOC(L->flags, sizeof(int) * L->max_segs);
@@ -322,10 +326,10 @@ int mm_layer_create(const mm_layer_desc *desc, mm_layer **out) {
 #undef ALLOC
   ce = cudaMemset(L->ctrl, 0, sizeof(int) * kCtrlWords);
   if (ce == cudaSuccess) ce = cudaMemset(L->err, 0, sizeof(uint32_t));
-  if (ce == cudaSuccess) ce = cudaMemset(L->hq, 0, 2 * static_cast<size_t>(L->rows_cap) * I);
-  if (ce == cudaSuccess) ce = cudaMemset(L->hs, 0, 2 * static_cast<size_t>(L->rows_cap) * I / 32);
-  if (ce == cudaSuccess) ce = cudaMemset(L->xq, 0, 2 * static_cast<size_t>(L->Tmax) * H);
-  if (ce == cudaSuccess) ce = cudaMemset(L->xs, 0, 2 * static_cast<size_t>(L->Tmax) * H / 32);
+  if (ce == cudaSuccess) ce = cudaMemset(L->hq, 0, hq_bytes);
+  if (ce == cudaSuccess) ce = cudaMemset(L->hs, 0, hq_bytes / 16);
+  if (ce == cudaSuccess) ce = cudaMemset(L->xq, 0, xq_bytes);
+  if (ce == cudaSuccess) ce = cudaMemset(L->xs, 0, xq_bytes / 16);
   if (ce != cudaSuccess) {
     free_layer(L);
     return fail(MM_ERR_CUDA, "cudaMemset: %s", cudaGetErrorString(ce));

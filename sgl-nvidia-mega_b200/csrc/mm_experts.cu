@@ -1,6 +1,6 @@
 // The persistent expert kernel (K2 + K3): every routed expert's gate_up GEMM
-// with the SwiGLU (+ clamp) and MXFP8 requant epilogue, then every expert's down
-// GEMM, in one launch of one CTA per SM.
+// with the SwiGLU (+ clamp) and MXFP4-terms requant epilogue, then every
+// expert's down GEMM, in one launch of one CTA per SM.
 //
 // Work: a segment is up to 16 consecutive permuted rows of one expert (the
 // shared expert's tokens form segments too). A gate_up unit streams one 128-row
@@ -9,17 +9,23 @@
 // w2 through all of I. Units are claimed from a global counter in the order
 // [all gate_up units][all down units], so every gate_up unit is claimed before
 // any down unit; a down unit's activations wait on its segment's mailbox (the
-// number of finished gate_up tiles), while its weights stream before that wait.
-// Reference semantics: gemm1.cu:6-7 (h = MXFP8(clamped SwiGLU(x W13^T))),
+// number of finished gate_up warps), while its weights stream before that wait.
+// Reference semantics: gemm1.cu:6-7 (h = MX(clamped SwiGLU(x W13^T))),
 // gemm2.cu:6-7 (rows = h W2^T in bf16, deferred-finalize rows).
 //
+// Arithmetic: tcgen05.mma kind::mxf4 block32 (E2M1 x E2M1, an E8M0 scale per 32
+// along K for both operands), M = 128 weight rows, N = terms * n activation
+// rows, K = 64 per instruction, fp32 accumulators in TMEM. The activations are
+// carried as MXFP4 terms (see quantize_block32_fp4), each term in its own
+// accumulator columns; the epilogue adds the terms.
+//
 // Warp roles (224 threads):
-//   warp 0    producer: claims units, TMA-loads w tiles (E2M1 unpacked to 8-bit
-//             slots by the 16U4_ALIGN16B tensor map) and bulk-loads the scale chunks;
+//   warp 0    producer: claims units, TMA-loads packed weight tiles (128-byte rows,
+//             128-byte swizzle) and bulk-loads the pre-laid scale chunks;
 //   warp 1    MMA: TMEM owner; copies scale chunks to TMEM (tcgen05.cp) and issues
-//             tcgen05.mma kind::mxf8f6f4.block_scale, M = 128, N = rows (8/16), K = 32;
-//   warp 2    B loader: gathers the segment's MXFP8 activation rows (hi, lo) with
-//             cp.async into the 128-byte-swizzled K-major layout;
+//             the MMAs, one thread;
+//   warp 2    B loader: gathers the segment's activation terms with cp.async into
+//             the 128-byte-swizzled K-major layout;
 //   warps 3-6 epilogue: TMEM -> registers; SwiGLU + requant (gate_up) or bf16 rows
 //             (down).
 // No TMA multicast is used anywhere (one CTA per cluster).
@@ -35,7 +41,7 @@ namespace mm {
 
 namespace {
 
-constexpr uint32_t kATxBytes = 128 * kStageK / 2;  // packed E2M1 bytes of one stage
+constexpr uint32_t kATxBytes = kAStageBytes;  // packed codes land as they are
 
 __device__ __forceinline__ void decode_unit(int u, int nseg, int m1, int m2, bool &g2, int &seg,
                                             int &m) {
@@ -80,6 +86,32 @@ __device__ bool wait_flag(const int *flag, int target, uint32_t *err) {
   }
 }
 
+// Instruction descriptor of kind::mxf4 block32: A and B E2M1 (format 1), both
+// K-major, E8M0 scales, M = 128, N = n, K = 64; scale-factor byte id 0 or 2
+// (each MMA consumes two consecutive scale bytes per row).
+__device__ __forceinline__ uint32_t idesc_mxf4(uint32_t n, uint32_t sf_id) {
+  uint32_t d = 0;
+  d |= (sf_id & 3u) << 4;   // B scale-factor id
+  d |= 1u << 7;             // A format E2M1
+  d |= 1u << 10;            // B format E2M1
+  d |= ((n >> 3) & 0x3fu) << 17;
+  d |= 1u << 23;            // scale format E8M0
+  d |= (128u >> 4) << 24;   // M = 128
+  d |= (sf_id & 3u) << 29;  // A scale-factor id
+  return d;
+}
+
+__device__ __forceinline__ void mma_mxf4(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%4], [%5], p;\n\t}" ::
+          "r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(sfa_tmem), "r"(sfb_tmem), "r"(accumulate)
+      : "memory");
+}
+
 }  // namespace
 
 __global__ void __launch_bounds__(kExpertThreads, 1) expert_kernel(const __grid_constant__ ExpertArgs p) {
@@ -115,7 +147,7 @@ __global__ void __launch_bounds__(kExpertThreads, 1) expert_kernel(const __grid_
     mbar_init(bar(kBarExFree), 2);  // the two gate-row warps
     fence_barrier_init();
   }
-  {  // zero the activation and B-scale areas once: rows a unit does not load stay finite
+  {  // zero the activation and scale areas once: rows a unit does not load stay finite
     uint4 *z = reinterpret_cast<uint4 *>(sbase + kSmemB);
     const int n16 = (kSmemEpi - kSmemB) / 16;
     for (int i = threadIdx.x; i < n16; i += blockDim.x) z[i] = make_uint4(0u, 0u, 0u, 0u);
@@ -173,15 +205,12 @@ __global__ void __launch_bounds__(kExpertThreads, 1) expert_kernel(const __grid_
           const uint32_t full = bar(kBarFull + stage);
           mbar_expect_tx(full, kATxBytes + kSfaStageBytes);
           const uint32_t sa = base + kSmemA + stage * kAStageBytes;
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            const int x = ks * kStageK + c * 128;
-            if (!g2) {
-              tma_load_3d(sa + c * kAChunkBytes, map, x, 64 * m, e, full, policy);
-              tma_load_3d(sa + c * kAChunkBytes + 64 * 128, map, x, p.inter + 64 * m, e, full, policy);
-            } else {
-              tma_load_3d(sa + c * kAChunkBytes, map, x, 128 * m, e, full, policy);
-            }
+          const int x = ks * kRowBytes;  // byte offset along K
+          if (!g2) {
+            tma_load_3d(sa, map, x, 64 * m, e, full, policy);
+            tma_load_3d(sa + 64 * kRowBytes, map, x, p.inter + 64 * m, e, full, policy);
+          } else {
+            tma_load_3d(sa, map, x, 128 * m, e, full, policy);
           }
           bulk_load(base + kSmemSfa + stage * kSfaStageBytes, sfa + static_cast<size_t>(ks) * 1024u,
                     kSfaStageBytes, full, policy);
@@ -204,6 +233,7 @@ __global__ void __launch_bounds__(kExpertThreads, 1) expert_kernel(const __grid_
       // 1 KB between 8-row groups; scale chunks: 32 rows x 16 B, 128 B apart
       const uint64_t sw_hi = smem_desc(0, 0, 1024, kLayoutSw128);
       const uint64_t sf_hi = smem_desc(0, 0, 128, kLayoutNone);
+      const uint32_t idesc_base = idesc_mxf4(0, 0);
 #pragma unroll 1
       while (true) {
         if (!mbar_wait(bar(kBarWorkFull + ws), wphase, err, kErrTimeoutWork)) break;
@@ -216,10 +246,9 @@ __global__ void __launch_bounds__(kExpertThreads, 1) expert_kernel(const __grid_
         decode_unit(u, nseg, p.m1, p.m2, g2, seg, m);
         const int4 sg = p.segs[seg];
         const uint32_t n = static_cast<uint32_t>((sg.z + 7) & ~7);
-        const uint32_t nmma = n * static_cast<uint32_t>(p.terms);  // hi rows, then lo rows
-        uint32_t idesc[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) idesc[j] = idesc_mxf4_e4m3(nmma, j, j);
+        const uint32_t nmma = n * static_cast<uint32_t>(p.terms);  // term 0 rows, term 1 rows, ...
+        const uint32_t id0 = idesc_base | ((nmma >> 3) << 17);
+        const uint32_t id2 = id0 | (2u << 4) | (2u << 29);
         const int ks_n = g2 ? p.ks2 : p.ks1;
         if (!mbar_wait(bar(kBarAccEmpty + acc), acc_phase ^ 1u, err, kErrTimeoutAcc)) break;
         tc_fence_after();
@@ -243,12 +272,12 @@ __global__ void __launch_bounds__(kExpertThreads, 1) expert_kernel(const __grid_
           tc_cp_32x128b_warpx4(sfb_t + 4, sfb_d + (512 >> 4));
           const uint64_t a_d = sw_hi | ((base + kSmemA + stage * kAStageBytes) >> 4);
           const uint64_t b_d = sw_hi | ((base + kSmemB + stage * kBStageBytes) >> 4);
+          // four K = 64 steps of 32 bytes along the 128-byte swizzled row;
+          // scale chunk c = k / 2 holds k-blocks 2k, 2k + 1 at bytes (k % 2) * 2
 #pragma unroll
-          for (int kk = 0; kk < kStageK / 32; ++kk) {
-            const uint32_t c = kk >> 2, j = kk & 3;
-            tc_mma_mxf8f6f4(d_tmem, a_d + ((c * kAChunkBytes + j * 32) >> 4),
-                            b_d + ((c * kBChunkBytes + j * 32) >> 4), idesc[j], sfa_t + 4 * c,
-                            sfb_t + 4 * c, (ks | kk) != 0 ? 1u : 0u);
+          for (int k = 0; k < 4; ++k) {
+            mma_mxf4(d_tmem, a_d + 2 * k, b_d + 2 * k, (k & 1) ? id2 : id0, sfa_t + 4 * (k >> 1),
+                     sfb_t + 4 * (k >> 1), (ks | k) != 0 ? 1u : 0u);
           }
           tc_commit(bar(kBarEmpty + stage));
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
@@ -263,15 +292,15 @@ __global__ void __launch_bounds__(kExpertThreads, 1) expert_kernel(const __grid_
     }
   } else if (warp == 2) {
     // ============================ B loader ===================================
-    // Per unit, every lane fixes its share of the stage once: 16-byte piece
-    // pc = lane % 16 of B rows rr = lane / 16 + 2 i (hi rows [0, n), lo rows
-    // [n, 2n)); per stage it only issues the copies at the stage's K offset.
+    // Per unit, every lane fixes its share of a stage once: 16-byte piece
+    // pc = lane % 8 of B rows rr = lane / 8 + 4 i (term t rows at [t n, (t+1) n));
+    // per stage it only issues the copies at the stage's K offset.
     pdl_wait();
     const int nseg = p.ctrl[kCtrlSegments];
     uint32_t stage = 0, phase = 0, ws = 0, wphase = 0;
-    const int pc = lane & 15;           // 16-byte piece of the 256-byte stage row
-    const int half = lane >> 4;
-    const int pc_c = pc >> 3, pc_j = pc & 7;
+    const int pc = lane & 7;            // 16-byte piece of the 128-byte stage row
+    const int quarter = lane >> 3;
+    constexpr int kPieces = kBRows / 4;  // rows per lane
 #pragma unroll 1
     while (true) {
       int u = -1, okw = 1;
@@ -292,7 +321,7 @@ __global__ void __launch_bounds__(kExpertThreads, 1) expert_kernel(const __grid_
       const int4 sg = p.segs[seg];
       const int rows = sg.z;
       const int n = (rows + 7) & ~7;
-      const int nb = n * p.terms;         // B rows of this unit
+      const int nb = n * p.terms;  // B rows of this unit
       if (g2) {
         int okf = 1;
         if (lane == 0) okf = wait_flag(p.flags + seg, 2 * p.m1, err) ? 1 : 0;
@@ -308,35 +337,35 @@ __global__ void __launch_bounds__(kExpertThreads, 1) expert_kernel(const __grid_
       const int K = g2 ? p.inter : p.hidden;
       const uint8_t *dq = g2 ? p.hq : p.xq;
       const uint8_t *dsc = g2 ? p.hs : p.xs;
-      const uint32_t term_q = static_cast<uint32_t>(g2 ? p.rows_cap : p.max_tokens) * static_cast<uint32_t>(K);
-      const uint32_t term_s = term_q >> 5;
-      // data pieces: up to 16 per lane
-      uint32_t soff[kBRows / 2], doff[kBRows / 2], sbytes[kBRows / 2];
+      const uint32_t rowb = static_cast<uint32_t>(K) >> 1;  // packed bytes per row
+      const uint32_t term_q = static_cast<uint32_t>(g2 ? p.rows_cap : p.max_tokens) * rowb;
+      const uint32_t term_s = term_q >> 4;
+      uint32_t soff[kPieces], doff[kPieces], sbytes[kPieces];
 #pragma unroll
-      for (int i = 0; i < kBRows / 2; ++i) {
-        const int rr = half + 2 * i;
-        const int t = rr >= n ? 1 : 0;
+      for (int i = 0; i < kPieces; ++i) {
+        const int rr = quarter + 4 * i;
+        const int t = rr / n;
         const int r = rr - t * n;
         const int sr = __shfl_sync(0xffffffffu, src, r & 31);
-        soff[i] = static_cast<uint32_t>(t) * term_q + static_cast<uint32_t>(sr) * K + pc * 16;
-        doff[i] = pc_c * kBChunkBytes + (rr >> 3) * 1024 + (rr & 7) * 128 + ((pc_j ^ (rr & 7)) << 4);
+        soff[i] = static_cast<uint32_t>(t) * term_q + static_cast<uint32_t>(sr) * rowb + pc * 16;
+        doff[i] = (rr >> 3) * 1024 + (rr & 7) * 128 + ((pc ^ (rr & 7)) << 4);
         sbytes[i] = (rr < nb && r < rows) ? 16u : 0u;
       }
-      // scale pieces: B row rr = lane (and lane + 32 never: nb <= 32), chunks 0 and 1
-      uint32_t s_soff[2], s_doff[2], s_bytes[2];
-      {
-        const int rr = lane;
-        const int t = rr >= n ? 1 : 0;
+      // scale pieces: B rows rr = lane and lane + 32, chunks 0 and 1
+      uint32_t s_soff[4], s_doff[4], s_bytes[4];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int rr = lane + 32 * h;
+        const int t = rr / n;
         const int r = rr - t * n;
         const int sr = __shfl_sync(0xffffffffu, src, r & 31);
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
-          s_soff[c] = static_cast<uint32_t>(t) * term_s + static_cast<uint32_t>(sr) * (K >> 5) + c * 4;
-          s_doff[c] = c * 512 + rr * 16;
-          s_bytes[c] = (rr < nb && r < rows) ? 4u : 0u;
+          s_soff[2 * h + c] = static_cast<uint32_t>(t) * term_s + static_cast<uint32_t>(sr) * (K >> 5) + c * 4;
+          s_doff[2 * h + c] = c * 512 + (rr & 31) * 16 + (rr >> 5) * 4;
+          s_bytes[2 * h + c] = (rr < nb && r < rows) ? 4u : 0u;
         }
       }
-      const bool issue_scale = lane < nb;
       const int ks_n = g2 ? p.ks2 : p.ks1;
 #pragma unroll 1
       for (int ks = 0; ks < ks_n; ++ks) {
@@ -345,16 +374,19 @@ __global__ void __launch_bounds__(kExpertThreads, 1) expert_kernel(const __grid_
         oke = __shfl_sync(0xffffffffu, oke, 0);
         if (!oke) break;
         const uint32_t sb = base + kSmemB + stage * kBStageBytes;
-        const uint8_t *gq = dq + ks * kStageK;
+        const uint8_t *gq = dq + ks * kRowBytes;
 #pragma unroll
-        for (int i = 0; i < kBRows / 2; ++i) {
-          if (half + 2 * i < nb) cp_async_16(sb + doff[i], gq + soff[i], sbytes[i]);
+        for (int i = 0; i < kPieces; ++i) {
+          if (quarter + 4 * i < nb) cp_async_16(sb + doff[i], gq + soff[i], sbytes[i]);
         }
-        if (issue_scale) {
-          const uint32_t ssb = base + kSmemSfb + stage * kSfbStageBytes;
-          const uint8_t *gs = dsc + ks * 8;
-          cp_async_4(ssb + s_doff[0], gs + s_soff[0], s_bytes[0]);
-          cp_async_4(ssb + s_doff[1], gs + s_soff[1], s_bytes[1]);
+        const uint32_t ssb = base + kSmemSfb + stage * kSfbStageBytes;
+        const uint8_t *gs = dsc + ks * 8;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          if (lane + 32 * h < nb) {
+            cp_async_4(ssb + s_doff[2 * h], gs + s_soff[2 * h], s_bytes[2 * h]);
+            cp_async_4(ssb + s_doff[2 * h + 1], gs + s_soff[2 * h + 1], s_bytes[2 * h + 1]);
+          }
         }
         cp_async_arrive_noinc(bar(kBarFull + stage));
         if (++stage == kStages) { stage = 0; phase ^= 1u; }
@@ -397,19 +429,22 @@ __global__ void __launch_bounds__(kExpertThreads, 1) expert_kernel(const __grid_
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       tc_fence_after();
-      uint32_t raw[kBRows];
-      tc_ld_32x32b_x32(tbase + (static_cast<uint32_t>(32 * q) << 16) + kTmemAcc + acc * kBRows, raw);
+      uint32_t ra[32], rb[16];
+      const uint32_t taddr = tbase + (static_cast<uint32_t>(32 * q) << 16) + kTmemAcc + acc * kBRows;
+      tc_ld_32x32b_x32(taddr, ra);
+      tc_ld_32x32b_x16(taddr + 32, rb);
       tc_wait_ld();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(kBarAccEmpty + acc));
       if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
-      // column j holds the hi-term product of segment row j, column n + j the lo term
+      // columns [t n, (t+1) n) hold term t's products; row j's value = sum of terms
       float v[kSegRows];
 #pragma unroll
       for (int j = 0; j < kSegRows; ++j) {
-        float a = __uint_as_float(raw[j]);
-        if (p.terms > 1) a = __fadd_rn(a, __uint_as_float(n == 8 ? raw[8 + j] : raw[16 + j]));
+        float a = __uint_as_float(ra[j]);
+        if (p.terms > 1) a = __fadd_rn(a, __uint_as_float(n == 8 ? ra[8 + j] : ra[16 + j]));
+        if (p.terms > 2) a = __fadd_rn(a, __uint_as_float(n == 8 ? ra[16 + j] : rb[j]));
         v[j] = a;
       }
       if (!g2) {
@@ -435,7 +470,9 @@ __global__ void __launch_bounds__(kExpertThreads, 1) expert_kernel(const __grid_
           const bool clamped = lim != nullptr;
           const float L = clamped ? lim[sg.x < 0 ? 0 : sg.x] : 0.0f;
           const int f = 64 * m + 32 * q + lane;  // feature (column of h)
-          const size_t lo_q = static_cast<size_t>(p.rows_cap) * p.inter;
+          const size_t rowb = static_cast<size_t>(p.inter) >> 1;
+          const size_t tq = static_cast<size_t>(p.rows_cap) * rowb;  // term stride of hq
+          const size_t ts = tq >> 4;                                  // term stride of hs
 #pragma unroll
           for (int j = 0; j < kSegRows; ++j) {
             if (j >= rows) break;
@@ -445,21 +482,17 @@ __global__ void __launch_bounds__(kExpertThreads, 1) expert_kernel(const __grid_
               up = fminf(fmaxf(up, -L), L);
               g = fminf(g, L);
             }
-            const float h = __fmul_rn(up, __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
-            // MXFP8 hi / lo of the 32 features of this warp for token row j
-            const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(h))));
-            const uint32_t code = mx_scale_code(amax);
-            const uint8_t qh = static_cast<uint8_t>(e4m3x2(__fmul_rn(h, mx_inverse(code)), 0.0f) & 0xffu);
+            float r = __fmul_rn(up, __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
             const size_t prow = static_cast<size_t>(sg.y + j);
-            p.hq[prow * p.inter + f] = qh;
-            if (lane == 0) p.hs[prow * (p.inter >> 5) + (f >> 5)] = static_cast<uint8_t>(code);
-            if (p.terms > 1) {
-              const float r = __fsub_rn(h, __fmul_rn(e4m3_value(qh), mx_scale_value(code)));
-              const float amax2 = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(r))));
-              const uint32_t code2 = mx_scale_code(amax2);
-              const uint8_t ql = static_cast<uint8_t>(e4m3x2(__fmul_rn(r, mx_inverse(code2)), 0.0f) & 0xffu);
-              p.hq[lo_q + prow * p.inter + f] = ql;
-              if (lane == 0) p.hs[(lo_q >> 5) + prow * (p.inter >> 5) + (f >> 5)] = static_cast<uint8_t>(code2);
+            // MXFP4 terms of the 32 features of this warp for token row j
+            for (int t = 0; t < p.terms; ++t) {
+              const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(r))));
+              const uint32_t code = mx4_scale_code(amax);
+              const uint32_t nib = e2m1x2(__fmul_rn(r, mx_inverse(code)), 0.0f) & 15u;
+              r = __fsub_rn(r, __fmul_rn(e2m1_value(nib), mx_scale_value(code)));
+              const uint32_t up_nib = __shfl_down_sync(0xffffffffu, nib, 1);
+              if ((lane & 1) == 0) p.hq[t * tq + prow * rowb + (f >> 1)] = static_cast<uint8_t>(nib | (up_nib << 4));
+              if (lane == 0) p.hs[t * ts + prow * (p.inter >> 5) + (f >> 5)] = static_cast<uint8_t>(code);
             }
           }
           // publish this warp's 32 features of every row: two increments per unit
@@ -510,7 +543,7 @@ __global__ void __launch_bounds__(kExpertThreads, 1) expert_kernel(const __grid_
 __global__ void repack_scales_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst,
                                      int n, int rows, int k, int gate_up, int inter) {
   const int ks_n = k / kStageK;
-  const int tiles = gate_up ? rows / 128 : rows / 128;
+  const int tiles = rows / 128;
   const size_t total = static_cast<size_t>(n) * tiles * ks_n * 1024;
   for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
        idx += static_cast<size_t>(gridDim.x) * blockDim.x) {

@@ -40,26 +40,26 @@ struct FrontArgs {
   GateArgs gate;             // gate.logits null: ids are given in route.ids
   RouteArgs route;
   const uint16_t *x;         // bf16 [T, H]
-  uint8_t *xq;               // [2][max_tokens][H]
-  uint8_t *xs;               // [2][max_tokens][H/32]
+  uint8_t *xq;               // [kMaxTerms][max_tokens][H/2] packed E2M1
+  uint8_t *xs;               // [kMaxTerms][max_tokens][H/32] E8M0
   int hidden;
   int max_tokens;
   int terms;
 };
 
 struct alignas(64) ExpertArgs {
-  CUtensorMap w13_map;       // routed gate_up codes, 3-D {H, 2I, E}, 16U4_ALIGN16B
-  CUtensorMap w2_map;        // routed down codes, {I, H, E}
+  CUtensorMap w13_map;       // routed gate_up codes, u8 3-D {H/2, 2I, E}, box {128, 64, 1}
+  CUtensorMap w2_map;        // routed down codes, u8 {I/2, H, E}, box {128, 128, 1}
   CUtensorMap sw13_map;      // shared expert (same shapes, E = 1)
   CUtensorMap sw2_map;
   const uint8_t *sfa13;      // [E][I/64][H/256][1024] scale chunks
   const uint8_t *sfa2;       // [E][H/128][I/256][1024]
   const uint8_t *ssfa13;
   const uint8_t *ssfa2;
-  const uint8_t *xq;         // [2][max_tokens][H]
-  const uint8_t *xs;         // [2][max_tokens][H/32]
-  uint8_t *hq;               // [2][rows_cap][I]
-  uint8_t *hs;               // [2][rows_cap][I/32]
+  const uint8_t *xq;         // [kMaxTerms][max_tokens][H/2]
+  const uint8_t *xs;         // [kMaxTerms][max_tokens][H/32]
+  uint8_t *hq;               // [kMaxTerms][rows_cap][I/2]
+  uint8_t *hs;               // [kMaxTerms][rows_cap][I/32]
   uint16_t *rows_out;        // [rows_cap][H] bf16
   const int *record;
   const int4 *segs;
@@ -82,46 +82,34 @@ struct FinalizeArgs {
   int tokens, top_k, hidden;
 };
 
-// Two-term MXFP8 quantization of 32 fp32 values (see quantize_row).
-__device__ __forceinline__ void quantize_block32(const float (&v)[32], uint8_t *q_hi,
-                                                 uint8_t *q_lo, uint8_t *s_hi, uint8_t *s_lo,
-                                                 int terms) {
-  float amax = 0.0f;
-#pragma unroll
-  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
-  const uint32_t c = mx_scale_code(amax);
-  const float inv = mx_inverse(c);
-  const float sv = mx_scale_value(c);
-  uint32_t packed[8];
+// MXFP4 terms of 32 fp32 values (one block): term t is the MXFP4 quantization
+// of the residual left by terms 0..t-1 (E8M0 code by mx4_scale_code, codes
+// e2m1(r * 2^(127-code)) RN saturating, residual r -= e2m1 * 2^(code-127)).
+// Writes 16 bytes of codes per term at q + t * q_stride and the code at
+// s + t * s_stride.
+__device__ __forceinline__ void quantize_block32_fp4(const float (&v)[32], int terms, uint8_t *q,
+                                                     size_t q_stride, uint8_t *s, size_t s_stride) {
   float r[32];
-  float amax2 = 0.0f;
 #pragma unroll
-  for (int i = 0; i < 32; i += 2) {
-    const uint16_t q2 = e4m3x2(__fmul_rn(v[i], inv), __fmul_rn(v[i + 1], inv));
-    const uint8_t c0 = static_cast<uint8_t>(q2 & 0xffu), c1 = static_cast<uint8_t>(q2 >> 8);
-    if ((i & 2) == 0) packed[i >> 2] = q2;
-    else packed[i >> 2] |= static_cast<uint32_t>(q2) << 16;
-    r[i] = __fsub_rn(v[i], __fmul_rn(e4m3_value(c0), sv));
-    r[i + 1] = __fsub_rn(v[i + 1], __fmul_rn(e4m3_value(c1), sv));
-    amax2 = fmaxf(amax2, fmaxf(fabsf(r[i]), fabsf(r[i + 1])));
-  }
-  uint4 *dh = reinterpret_cast<uint4 *>(q_hi);
-  dh[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-  dh[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
-  *s_hi = static_cast<uint8_t>(c);
-  if (terms < 2) return;
-  const uint32_t c2 = mx_scale_code(amax2);
-  const float inv2 = mx_inverse(c2);
+  for (int i = 0; i < 32; ++i) r[i] = v[i];
+  for (int t = 0; t < terms; ++t) {
+    float amax = 0.0f;
 #pragma unroll
-  for (int i = 0; i < 32; i += 2) {
-    const uint16_t q2 = e4m3x2(__fmul_rn(r[i], inv2), __fmul_rn(r[i + 1], inv2));
-    if ((i & 2) == 0) packed[i >> 2] = q2;
-    else packed[i >> 2] |= static_cast<uint32_t>(q2) << 16;
+    for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(r[i]));
+    const uint32_t c = mx4_scale_code(amax);
+    const float inv = mx_inverse(c);
+    const float sv = mx_scale_value(c);
+    uint32_t packed[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) {
+      const uint32_t b = e2m1x2(__fmul_rn(r[i], inv), __fmul_rn(r[i + 1], inv));
+      packed[i >> 3] |= b << (8 * ((i >> 1) & 3));
+      r[i] = __fsub_rn(r[i], __fmul_rn(e2m1_value(b & 15u), sv));
+      r[i + 1] = __fsub_rn(r[i + 1], __fmul_rn(e2m1_value(b >> 4), sv));
+    }
+    *reinterpret_cast<uint4 *>(q + t * q_stride) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    s[t * s_stride] = static_cast<uint8_t>(c);
   }
-  uint4 *dl = reinterpret_cast<uint4 *>(q_lo);
-  dl[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-  dl[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
-  *s_lo = static_cast<uint8_t>(c2);
 }
 
 // kernels (definitions in mm_route.cu, mm_experts.cu, mm_finalize.cu)

@@ -2,13 +2,13 @@
 //
 // HBM, per layer (all device memory, allocated once at layer creation):
 //   weights     caller-owned canonical MXFP4 (E2M1 codes, [n, rows, K/2] u8) read
-//               in place by TMA with on-the-fly 4-bit -> 8-bit-slot unpacking;
+//               in place by TMA (128-byte rows, 128-byte swizzle);
 //   sfa13/sfa2  the E8M0 weight scales re-laid once as UMMA scale chunks:
 //               [n][m_tile][k_stage][2 chunks][32 m0][4 m1][4 kk] bytes, so one
 //               1 KB bulk copy per pipeline stage lands them ready for tcgen05.cp;
-//   xq/xs       the routed input, two MXFP8 terms (hi, lo): [term][T][H] E4M3 and
+//   xq/xs       the routed input as MXFP4 terms: [term][T][H/2] packed E2M1 and
 //               [term][T][H/32] E8M0, written by the front kernel;
-//   hq/hs       the SwiGLU output of gate_up, [term][rows][I] and [term][rows][I/32],
+//   hq/hs       the SwiGLU output of gate_up, [term][rows][I/2] and [term][rows][I/32],
 //               rows in the reference's padded permuted order;
 //   segs/ctrl   work tables built by the front kernel (below);
 //   err         the device error word.
@@ -55,19 +55,23 @@ constexpr int kCtrlDone = 4;      // expert kernel's finished CTAs (reset by the
 constexpr int kCtrlWords = 8;
 
 // ---- the persistent expert kernel's shared memory -----------------------------------
-constexpr int kStages = 5;
-constexpr int kStageK = 256;                  // K elements per pipeline stage
-constexpr int kAStageBytes = 128 * kStageK;   // 4-bit codes in 8-bit slots: 32 KB
-constexpr int kAChunkBytes = 128 * 128;       // one 128-K chunk of 128 rows
-// B (activation) rows of a stage: the hi terms of the segment's n rows at rows
-// [0, n), the lo terms at [n, 2n) (n = rows rounded up to 8), so one MMA with
-// N = 2n accumulates both terms in separate accumulator columns.
-constexpr int kBRows = 2 * kSegRows;            // 32
-constexpr int kBStageBytes = kBRows * kStageK;  // 8 KB
-constexpr int kBChunkBytes = kBRows * 128;      // one 128-K chunk of the 32 rows
-constexpr int kSfaStageBytes = 1024;          // 2 chunks x 512 B
-constexpr int kSfbStageBytes = 1024;          // 2 chunks x (32 rows x 16 B)
-constexpr int kEpiBytes = 64 * kSegRows * 4;  // gate_up epilogue exchange
+// Weights and activations are both packed E2M1 (two codes per byte) with an E8M0
+// scale per 32 along K, multiplied by tcgen05.mma kind::mxf4 (block32, K = 64).
+// The activations are carried as up to kMaxTerms MXFP4 terms (x ~ t0 + t1 + t2,
+// each term the MXFP4 quantization of the previous residual); a stage's B rows
+// hold term 0 of the segment's n rows at [0, n), term 1 at [n, 2n), term 2 at
+// [2n, 3n) (n = rows rounded up to 8), so one MMA with N = terms * n multiplies
+// every term, each into its own accumulator columns.
+constexpr int kMaxTerms = 3;
+constexpr int kStages = 9;
+constexpr int kStageK = 256;                    // K elements per pipeline stage
+constexpr int kRowBytes = kStageK / 2;          // 128: one 128-byte swizzle row
+constexpr int kAStageBytes = 128 * kRowBytes;   // 16 KB: 128 weight rows
+constexpr int kBRows = kMaxTerms * kSegRows;    // 48
+constexpr int kBStageBytes = kBRows * kRowBytes;  // 6 KB
+constexpr int kSfaStageBytes = 1024;            // 2 chunks x (32 m0 x 4 m1 x 4 kk)
+constexpr int kSfbStageBytes = 1024;            // 2 chunks x (32 x 4 x 4), rows < 64
+constexpr int kEpiBytes = 64 * kSegRows * 4;    // gate_up epilogue exchange
 constexpr int kWorkSlots = 4;
 
 constexpr int kSmemA = 0;
@@ -93,7 +97,9 @@ constexpr int kSmemTmemBase = kSmemWorkIds + 4 * kWorkSlots;
 constexpr int kSmemTotal = kSmemTmemBase + 16;
 constexpr int kSmemAlloc = kSmemTotal + 1024;  // room to align the base to 1 KB
 static_assert(kSmemAlloc <= 232448, "expert kernel shared memory over the 227 KB limit");
-static_assert(kSmemB % 1024 == 0 && kSmemSfa % 128 == 0 && kSmemSfb % 128 == 0, "alignment");
+static_assert(kSmemB % 1024 == 0 && kBStageBytes % 1024 == 0 && kSmemSfa % 128 == 0 &&
+                  kSmemSfb % 128 == 0,
+              "alignment");
 
 // TMEM columns: 2 accumulators of kBRows fp32 columns, then per stage the A
 // scale chunks (8 columns) and the B scale chunks (8 columns).

@@ -13,9 +13,11 @@
 //    the lowest expert id wins a tie (gate_topk.cuh:211-290, routing.py:32-70).
 //  * weights: gate_topk.cuh:187-198 (score / (sum + eps) or the guarded sum, then
 //    the routed scale); glm5_3/sm103/moe/routing.py:3-11 (sigmoid + bias, renorm).
-//  * MXFP8 quantization: deepseek_v41/sm103/moe/src/route_quant.cuh:1-15 and
+//  * MX quantization: deepseek_v41/sm103/moe/src/route_quant.cuh:1-15 and
 //    gemm1.cu:905-1000 (block-32 amax, times fp32(1/448), E8M0 rounded up,
-//    multiply by the exact inverse power of two, e4m3 RN satfinite).
+//    multiply by the exact inverse power of two, e4m3 RN satfinite); the same
+//    rule with E2M1 codes (largest magnitude 6, fp32(1/6)) for the MXFP4 terms
+//    of the activations.
 // The sigmoid uses this file's own exp (Cody-Waite reduction + Taylor
 // polynomial) instead of the reference's tanh.approx, whose bits no CPU code
 // can reproduce; everything else is the reference's rule.
@@ -84,6 +86,22 @@ __device__ __forceinline__ uint32_t mx_scale_code(float amax) {
   if (exponent == 255u) code = 255u;
   return code;
 }
+// E8M0 code of an MXFP4 block (E2M1 codes, largest magnitude 6): the exponent of
+// amax * fp32(1/6), rounded up when the mantissa is non-zero (a zero block gets
+// scale 1), so amax / scale never exceeds 6 by more than the rounding of 1/6.
+__device__ __forceinline__ uint32_t mx4_scale_code(float amax) {
+  const float numerator = amax == 0.0f ? 6.0f : amax;
+  const uint32_t bits = __float_as_uint(__fmul_rn(numerator, 0x1.555556p-3f));
+  const uint32_t exponent = (bits >> 23) & 0xffu;
+  const uint32_t mantissa = bits & 0x7fffffu;
+  uint32_t code = exponent;
+  if (mantissa != 0u && exponent != 254u) {
+    if (exponent != 0u) code = exponent + 1u;
+    else if (mantissa > 0x400000u) code = 1u;
+  }
+  if (exponent == 255u) code = 255u;
+  return code;
+}
 // 2^(127 - code): the exact multiplier that maps the block into E4M3 range.
 __device__ __forceinline__ float mx_inverse(uint32_t code) {
   return code == 254u ? __uint_as_float(0x400000u) : __uint_as_float((254u - code) << 23);
@@ -106,6 +124,23 @@ __device__ __forceinline__ float e4m3_value(uint8_t code) {
   else if (e == 15u && m == 7u) v = __uint_as_float(0x7fc00000u);
   else v = __uint_as_float(((e + 120u) << 23) | (m << 20));
   return s ? -v : v;
+}
+
+// Two floats -> one byte of two E2M1 codes (RN, saturating to +-6); lo in bits 0-3.
+__device__ __forceinline__ uint32_t e2m1x2(float lo, float hi) {
+  uint32_t r;
+  asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\tcvt.u32.u8 %0, t;\n\t}"
+      : "=r"(r)
+      : "f"(hi), "f"(lo));
+  return r & 0xffu;
+}
+// exact value of an E2M1 code (bits 0-3)
+__device__ __forceinline__ float e2m1_value(uint32_t code) {
+  const uint32_t mag = code & 7u;
+  // 0, 0.5, 1, 1.5, 2, 3, 4, 6
+  const float v = mag < 4u ? 0.5f * static_cast<float>(mag)
+                           : (mag < 6u ? static_cast<float>(mag - 2u) : static_cast<float>(2u * mag - 8u));
+  return (code & 8u) ? -v : v;
 }
 
 __device__ __forceinline__ float bf16_bits_to_float(uint16_t b) {

@@ -1,6 +1,6 @@
 // Front of the routed-MoE chain: router GEMV (K0), top-k with bias (K1a), the
-// route record and slot -> row map (K1b), the two-term MXFP8 quantization of
-// the routed input, and the segment / work tables of the expert kernel.
+// route record and slot -> row map (K1b), the MXFP4-terms quantization of the
+// routed input, and the segment / work tables of the expert kernel.
 //
 // The route record is bit for bit the reference's (route.cuh:6-46,94-161 for
 // up to 8 rows, route_wide.cu:1-14,62-163 beyond): local experts in ascending
@@ -203,13 +203,12 @@ __global__ void __launch_bounds__(512) gate_topk_kernel(GateArgs g) {
 }
 
 // ============================================================================
-// Two-term MXFP8 quantization of one bf16 row (block of 512 threads).
-// term 0: q = e4m3(v * 2^(127-c)) with c the E8M0 code of the block's amax;
-// term 1: the same rule applied to the residual v - q * 2^(c-127).
+// MXFP4 terms of one bf16 row (block of 512 threads, one 32-element block per
+// thread): q [term][.][H/2] at stride q_stride, s [term][.][H/32] at s_stride.
 // ============================================================================
-__device__ void quantize_row(const uint16_t *__restrict__ xrow, uint8_t *__restrict__ q_hi,
-                             uint8_t *__restrict__ q_lo, uint8_t *__restrict__ s_hi,
-                             uint8_t *__restrict__ s_lo, int hidden, int terms) {
+__device__ void quantize_row(const uint16_t *__restrict__ xrow, uint8_t *__restrict__ q,
+                             size_t q_stride, uint8_t *__restrict__ s, size_t s_stride, int hidden,
+                             int terms) {
   const int blocks = hidden >> 5;
   for (int b = threadIdx.x; b < blocks; b += blockDim.x) {
     const uint4 *src = reinterpret_cast<const uint4 *>(xrow + 32 * b);
@@ -217,14 +216,14 @@ __device__ void quantize_row(const uint16_t *__restrict__ xrow, uint8_t *__restr
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const uint4 u = src[i];
-      const uint32_t q[4] = {u.x, u.y, u.z, u.w};
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        v[8 * i + 2 * j] = __uint_as_float(q[j] << 16);
-        v[8 * i + 2 * j + 1] = __uint_as_float(q[j] & 0xffff0000u);
+        v[8 * i + 2 * j] = __uint_as_float(w[j] << 16);
+        v[8 * i + 2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
       }
     }
-    quantize_block32(v, q_hi + 32 * b, q_lo + 32 * b, s_hi + b, s_lo + b, terms);
+    quantize_block32_fp4(v, terms, q + 16 * b, q_stride, s + b, s_stride);
   }
 }
 
@@ -371,11 +370,10 @@ __global__ void __launch_bounds__(512) front_kernel(FrontArgs f) {
     const int valid = f.gate.num_valid != nullptr ? *f.gate.num_valid : f.route.tokens;
     gate_row(f.gate, row, valid, gsm);
   }
-  const size_t th = static_cast<size_t>(f.max_tokens) * f.hidden;
-  const size_t ts = th >> 5;
-  quantize_row(f.x + static_cast<size_t>(row) * f.hidden, f.xq + static_cast<size_t>(row) * f.hidden,
-               f.xq + th + static_cast<size_t>(row) * f.hidden, f.xs + static_cast<size_t>(row) * (f.hidden >> 5),
-               f.xs + ts + static_cast<size_t>(row) * (f.hidden >> 5), f.hidden, f.terms);
+  const size_t q_stride = static_cast<size_t>(f.max_tokens) * (f.hidden >> 1);
+  const size_t s_stride = static_cast<size_t>(f.max_tokens) * (f.hidden >> 5);
+  quantize_row(f.x + static_cast<size_t>(row) * f.hidden, f.xq + static_cast<size_t>(row) * (f.hidden >> 1),
+               q_stride, f.xs + static_cast<size_t>(row) * (f.hidden >> 5), s_stride, f.hidden, f.terms);
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {

@@ -59,8 +59,8 @@ class RoutedMoE:
     ``router_experts``: the router's expert count (default: the local ones);
     ``expert_offset``: router id of local expert 0 (expert parallelism);
     ``clamp``: fp32 [E] SwiGLU clamp limits or None;
-    ``act_terms``: 2 (hi + lo MXFP8 activations, default) or 1 (single MXFP8,
-    the reference kernels' numerics).
+    ``act_terms``: MXFP4 terms per activation (1..3, default 3: each term
+    quantizes the residual of the previous ones; about 1e-3 relative).
     """
 
     def __init__(
@@ -77,7 +77,7 @@ class RoutedMoE:
         expert_offset: int = 0,
         shared: Optional[Sequence[torch.Tensor]] = None,
         shared_clamp: Optional[torch.Tensor] = None,
-        act_terms: int = 2,
+        act_terms: int = 3,
     ):
         w13, w13_scale, w2, w2_scale = (_u8(t) for t in (w13, w13_scale, w2, w2_scale))
         if w13.dim() != 3:

@@ -4,8 +4,8 @@ the C ABI via megamoe's ctypes binding).
 Bit-exact: router GEMV logits, top-k ids and weights, the route record and
 slot -> row map, the combine. Tolerance: the MoE output against the oracle's
 dequantize-then-fp32 path (max|got - ref| / max|ref| <= 2e-2, BASELINE's bar),
-and the deferred rows against the oracle fed the kernels' own MXFP8 terms
-(<= 1e-2: only the fp32 accumulation order differs)."""
+and the deferred rows against the oracle fed the kernels' own MXFP4 activation
+terms (<= 1e-2: only the fp32 accumulation order differs)."""
 
 import numpy as np
 import pytest
@@ -25,7 +25,7 @@ def _mm():
     return megamoe
 
 
-def to_gpu_layer(layer, top_k, max_rows, act_terms=2, router_experts=None, expert_offset=0, window=None):
+def to_gpu_layer(layer, top_k, max_rows, act_terms=3, router_experts=None, expert_offset=0, window=None):
     mm = _mm()
     dev = torch.device("cuda", 0)
     sel = (lambda t: t[window]) if window is not None else (lambda t: t)
@@ -130,7 +130,7 @@ def test_finalize_bitexact():
 
 
 # ----------------------------------------------------------------------------- experts
-def _run_and_check(layer, x, ids, weights, K, max_rows, act_terms=2, expert_offset=0, local=None,
+def _run_and_check(layer, x, ids, weights, K, max_rows, act_terms=3, expert_offset=0, local=None,
                    router_experts=None, window=None):
     moe = to_gpu_layer(layer, K, max_rows, act_terms=act_terms, router_experts=router_experts,
                        expert_offset=expert_offset, window=window)
@@ -155,7 +155,7 @@ def _run_and_check(layer, x, ids, weights, K, max_rows, act_terms=2, expert_offs
     if kn_shared is not None:
         sh = rows_c[moe.shared_row_base: moe.shared_row_base + x.shape[0]].numpy()
         assert O.max_abs_rel(sh, kn_shared.numpy()) <= ROWS_TOL
-    tol = OUT_TOL if act_terms == 2 else 1e-1
+    tol = OUT_TOL if act_terms == 3 else 1e-1
     err = O.max_abs_rel(out.float().cpu().numpy(), ex_out.numpy())
     assert err <= tol, err
     return moe, out
@@ -194,7 +194,7 @@ def test_experts_clamp_and_single_term():
     ids = _random_ids(T, K, E, g)
     w = torch.rand((T, K), generator=g)
     _run_and_check(layer, x, ids, w, K, max_rows=8)
-    _run_and_check(layer, x, ids, w, K, max_rows=8, act_terms=1)
+    _run_and_check(layer, x, ids, w, K, max_rows=8, act_terms=2)
 
 
 def test_experts_expert_parallel_window():

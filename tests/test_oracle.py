@@ -162,12 +162,36 @@ def test_e4m3_matches_torch_in_range():
     assert L.or_e4m3(float("nan")) == 0x7F
 
 
-def test_two_term_mxfp8_is_near_exact():
+def test_mxfp4_terms_converge():
     v = np.random.default_rng(3).standard_normal((8, 1024)).astype(np.float32)
-    one = O.mxfp8_roundtrip(v, terms=1)
-    two = O.mxfp8_roundtrip(v, terms=2)
-    assert np.abs(one - v).max() / np.abs(v).max() < 2 ** -4
-    assert np.abs(two - v).max() / np.abs(v).max() < 2 ** -8
+    errs = [np.abs(O.act_roundtrip(v, t) - v).max() / np.abs(v).max() for t in (1, 2, 3)]
+    assert errs[0] < 0.2 and errs[1] < 0.03 and errs[2] < 4e-3
+    assert errs[0] > errs[1] > errs[2]
+
+
+def test_e2m1_rounding_is_nearest_even():
+    L = O.lib()
+    L.or_e2m1.restype = ctypes.c_uint8
+    L.or_e2m1.argtypes = [ctypes.c_float]
+    grid = np.array([0, 0.5, 1, 1.5, 2, 3, 4, 6], dtype=np.float64)
+    xs = np.concatenate([np.linspace(0, 7, 2801), [0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, 100.0]])
+    for x in xs:
+        code = L.or_e2m1(float(x))
+        d = np.abs(grid - min(x, 6.0))
+        best = np.flatnonzero(d == d.min())
+        want = best[0] if len(best) == 1 else [b for b in best if b % 2 == 0][0]
+        assert code == want, (x, code, want)
+        assert L.or_e2m1(float(-x)) == (want | 8 if x > 0 else L.or_e2m1(float(-x)))
+
+
+def test_mx4_scale_code_known_answers():
+    L = O.lib()
+    L.or_mx4_scale_code.restype = ctypes.c_uint32
+    L.or_mx4_scale_code.argtypes = [ctypes.c_float]
+    assert L.or_mx4_scale_code(0.0) == 127   # zero block: scale 1
+    assert L.or_mx4_scale_code(6.0) == 127   # exactly E2M1's largest magnitude
+    assert L.or_mx4_scale_code(6.5) == 128   # rounded up, never saturating
+    assert L.or_mx4_scale_code(3.0) == 126
 
 
 # ------------------------------------------------------------------ GEMV order, combine
