@@ -470,7 +470,7 @@ static int run_front_and_experts(mm_layer *L, const uint16_t *x, const mm_gate_a
   ea.rows_out = rows;
   ea.record = record;
   ea.token_off = 4 + 2 * route_cta_words(route_max_ctas(tokens, L->K, L->E));
-  MM_CUDA(launch(expert_kernel, dim3(L->num_sms), dim3(kExpertThreads), kSmemAlloc, stream, ea));
+  MM_CUDA(launch(expert_kernel, dim3(kCtasPerSm * L->num_sms), dim3(kExpertThreads), kSmemAlloc, stream, ea));
   return MM_OK;
 }
 
@@ -482,7 +482,7 @@ int mm_layer_rerun_experts(mm_layer *L, int32_t tokens, const int32_t *record, u
   ea.rows_out = rows;
   ea.record = record;
   ea.token_off = 4 + 2 * route_cta_words(route_max_ctas(tokens, L->K, L->E));
-  MM_CUDA(launch(expert_kernel, dim3(L->num_sms), dim3(kExpertThreads), kSmemAlloc, stream, ea));
+  MM_CUDA(launch(expert_kernel, dim3(kCtasPerSm * L->num_sms), dim3(kExpertThreads), kSmemAlloc, stream, ea));
   return MM_OK;
 }
 

@@ -1,6 +1,6 @@
 // The persistent expert kernel (K2 + K3): every routed expert's gate_up GEMM
 // with the SwiGLU (+ clamp) and MXFP4-terms requant epilogue, then every
-// expert's down GEMM, in one launch of one CTA per SM.
+// expert's down GEMM, in one launch of two CTAs per SM (kCtasPerSm).
 //
 // Work: a segment is up to 16 consecutive permuted rows of one expert (the
 // shared expert's tokens form segments too). A gate_up unit streams one 128-row
@@ -114,7 +114,7 @@ __device__ __forceinline__ void mma_mxf4(uint32_t d_tmem, uint64_t adesc, uint64
 
 }  // namespace
 
-__global__ void __launch_bounds__(kExpertThreads, 1) expert_kernel(const __grid_constant__ ExpertArgs p) {
+__global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(const __grid_constant__ ExpertArgs p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;

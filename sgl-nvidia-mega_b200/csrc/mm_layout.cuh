@@ -63,7 +63,11 @@ constexpr int kCtrlWords = 8;
 // [2n, 3n) (n = rows rounded up to 8), so one MMA with N = terms * n multiplies
 // every term, each into its own accumulator columns.
 constexpr int kMaxTerms = 3;
-constexpr int kStages = 9;
+// Two CTAs share each SM (kCtasPerSm), each with its own 4-stage ring: two
+// independent producer -> MMA -> release loops per SM hide each other's
+// per-stage hand-off latency, which one deeper ring cannot.
+constexpr int kCtasPerSm = 2;
+constexpr int kStages = 4;
 constexpr int kStageK = 256;                    // K elements per pipeline stage
 constexpr int kRowBytes = kStageK / 2;          // 128: one 128-byte swizzle row
 constexpr int kAStageBytes = 128 * kRowBytes;   // 16 KB: 128 weight rows
@@ -97,6 +101,7 @@ constexpr int kSmemTmemBase = kSmemWorkIds + 4 * kWorkSlots;
 constexpr int kSmemTotal = kSmemTmemBase + 16;
 constexpr int kSmemAlloc = kSmemTotal + 1024;  // room to align the base to 1 KB
 static_assert(kSmemAlloc <= 232448, "expert kernel shared memory over the 227 KB limit");
+static_assert(kCtasPerSm * (kSmemAlloc + 1024) <= 233472, "two CTAs must fit one SM's 228 KB");
 static_assert(kSmemB % 1024 == 0 && kBStageBytes % 1024 == 0 && kSmemSfa % 128 == 0 &&
                   kSmemSfb % 128 == 0,
               "alignment");
@@ -106,8 +111,9 @@ static_assert(kSmemB % 1024 == 0 && kBStageBytes % 1024 == 0 && kSmemSfa % 128 =
 constexpr int kTmemAcc = 0;
 constexpr int kTmemSfa = 2 * kBRows;
 constexpr int kTmemSfb = kTmemSfa + kStages * 8;
-constexpr int kTmemCols = 256;
+constexpr int kTmemCols = 256;  // x kCtasPerSm = the SM's 512 columns
 static_assert(kTmemSfb + kStages * 8 <= kTmemCols, "TMEM columns");
+static_assert(kCtasPerSm * kTmemCols <= 512, "TMEM columns per SM");
 
 constexpr int kExpertThreads = 224;  // 7 warps: producer, MMA, B loader, 4 epilogue
 
