@@ -28,24 +28,25 @@ static inline uint16_t f_to_bf16(float f) {
 }
 
 /* ---------------------------------------------------------------------------
- * Router GEMV in the kernel's fixed order: 4 parts of H/4; in part p, lane l
- * (0..31) accumulates h = p*H/4 + 8*(l + 32 j) + i, j ascending, i = 0..7, with
- * acc = fma(x, w, acc); lanes combine by the xor butterfly 16, 8, 4, 2, 1; parts
- * as (p0 + p1) + (p2 + p3). Reference operation: router_mma.cu:101 (logits =
- * x . W^T in fp32 from bf16 operands); its summation order is the kernel's own.
+ * Router GEMV in the kernel's fixed order: H in parts of 1024; in part p, lane l
+ * (0..31) accumulates h = 1024 p + 8 (l + 32 j) + i for j = 0..3, i = 0..7, with
+ * acc = fma(x, w, acc) from 0; lanes combine by the xor butterfly 16, 8, 4, 2, 1;
+ * parts in order, s = ((p0 + p1) + p2) + ... Reference operation:
+ * router_mma.cu:101 (logits = x . W^T in fp32 from bf16 operands); the
+ * summation order is the kernel's own.
  * ------------------------------------------------------------------------- */
 void or_router_gemv(const uint16_t *x, const uint16_t *w, float *logits, int T, int E, int H) {
-  const int kp = H / 4, nvec = kp / 256;
+  const int parts = H / 1024;
   for (int t = 0; t < T; ++t)
     for (int e = 0; e < E; ++e) {
-      float part[4];
-      for (int p = 0; p < 4; ++p) {
+      float s = 0.0f;
+      for (int p = 0; p < parts; ++p) {
         float lane[32];
         for (int l = 0; l < 32; ++l) {
           float acc = 0.0f;
-          for (int j = 0; j < nvec; ++j)
+          for (int j = 0; j < 4; ++j)
             for (int i = 0; i < 8; ++i) {
-              const int h = p * kp + 8 * (l + 32 * j) + i;
+              const int h = 1024 * p + 8 * (l + 32 * j) + i;
               acc = fmaf(bf16_to_f(x[(size_t)t * H + h]), bf16_to_f(w[(size_t)e * H + h]), acc);
             }
           lane[l] = acc;
@@ -55,9 +56,9 @@ void or_router_gemv(const uint16_t *x, const uint16_t *w, float *logits, int T, 
           for (int l = 0; l < 32; ++l) nxt[l] = lane[l] + lane[l ^ off];
           memcpy(lane, nxt, sizeof(lane));
         }
-        part[p] = lane[0];
+        s = p == 0 ? lane[0] : s + lane[0];
       }
-      logits[(size_t)t * E + e] = (part[0] + part[1]) + (part[2] + part[3]);
+      logits[(size_t)t * E + e] = s;
     }
 }
 

@@ -130,12 +130,20 @@ int64_t mm_route_words(int32_t tokens, int32_t top_k, int32_t experts) {
 int mm_router_gemv(const uint16_t *x, const uint16_t *w, float *logits, int32_t tokens,
                    int32_t experts, int32_t hidden, void *stream) {
   if (!x || !w || !logits) return fail(MM_ERR_INVALID, "mm_router_gemv: null pointer");
-  if (tokens < 1 || experts < 1 || hidden < 1024 || hidden % 1024)
-    return fail(MM_ERR_INVALID, "mm_router_gemv: tokens %d experts %d hidden %d (hidden %% 1024 == 0)",
-                tokens, experts, hidden);
+  if (tokens < 1 || experts < 1 || hidden < 1024 || hidden % 1024 || hidden > 1024 * kMaxRouterParts)
+    return fail(MM_ERR_INVALID, "mm_router_gemv: tokens %d experts %d hidden %d (hidden %% 1024 == 0, <= %d)",
+                tokens, experts, hidden, 1024 * kMaxRouterParts);
   if (!aligned(x, 16) || !aligned(w, 16)) return fail(MM_ERR_INVALID, "mm_router_gemv: x and w must be 16-byte aligned");
+  RouterArgs a = {};
+  a.x = x;
+  a.w = w;
+  a.logits = logits;
+  a.tokens = tokens;
+  a.experts = experts;
+  a.hidden = hidden;
+  a.gemv_ctas = experts;
   dim3 grid(experts, (tokens + 7) / 8);
-  MM_CUDA(launch(router_gemv_kernel, grid, dim3(128), 0, stream, x, w, logits, tokens, experts, hidden));
+  MM_CUDA(launch(router_quant_kernel, grid, dim3(256), 0, stream, a));
   return MM_OK;
 }
 
@@ -427,10 +435,35 @@ int mm_layer_get_info(const mm_layer *L, mm_layer_info *info) {
   return MM_OK;
 }
 
-// front (gate or given ids) + experts
+// One launch of the router GEMV (w non-null) and the MXFP4-terms quantization
+// of x into the layer's scratch (extra CTAs of the same grid).
+static int launch_router_quant(mm_layer *L, const uint16_t *x, const uint16_t *w, float *logits, int tokens,
+                               void *stream) {
+  if (w && (L->H % 1024 || L->H > 1024 * kMaxRouterParts))
+    return fail(MM_ERR_INVALID, "router GEMV: hidden %d must be a multiple of 1024, <= %d", L->H, 1024 * kMaxRouterParts);
+  if (w && !aligned(w, 16)) return fail(MM_ERR_INVALID, "router weight must be 16-byte aligned");
+  RouterArgs a = {};
+  a.x = x;
+  a.w = w;
+  a.logits = logits;
+  a.tokens = tokens;
+  a.experts = L->R;
+  a.hidden = L->H;
+  a.gemv_ctas = w ? L->R : 0;
+  a.xq = L->xq;
+  a.xs = L->xs;
+  a.max_tokens = L->Tmax;
+  a.terms = L->terms;
+  const int quant_ctas = (tokens * (L->H / 32) + 255) / 256;
+  dim3 grid(a.gemv_ctas + quant_ctas, w ? (tokens + 7) / 8 : 1);
+  MM_CUDA(launch(router_quant_kernel, grid, dim3(256), 0, stream, a));
+  return MM_OK;
+}
+
+// [quantization] + front (gate or given ids) + experts
 static int run_front_and_experts(mm_layer *L, const uint16_t *x, const mm_gate_args *gate,
                                  const int32_t *ids, int tokens, int32_t *permuted, int32_t *record,
-                                 uint16_t *rows, void *stream) {
+                                 uint16_t *rows, void *stream, bool quant_done = false) {
   if (!x || !permuted || !record || !rows) return fail(MM_ERR_INVALID, "layer call: null pointer");
   if (tokens < 1 || tokens > L->Tmax) return fail(MM_ERR_INVALID, "tokens %d outside 1..%d", tokens, L->Tmax);
   if (!aligned(x, 16) || !aligned(rows, 16)) return fail(MM_ERR_INVALID, "x and rows must be 16-byte aligned");
@@ -458,13 +491,11 @@ static int run_front_and_experts(mm_layer *L, const uint16_t *x, const mm_gate_a
   f.route.shared_row_base = L->shared_row_base;
   f.route.m1 = L->m1;
   f.route.m2 = L->m2;
-  f.x = x;
-  f.xq = L->xq;
-  f.xs = L->xs;
-  f.hidden = L->H;
-  f.max_tokens = L->Tmax;
-  f.terms = L->terms;
   MM_CUDA(cudaSetDevice(L->d.device));
+  if (!quant_done) {
+    int rc = launch_router_quant(L, x, nullptr, nullptr, tokens, stream);
+    if (rc) return rc;
+  }
   MM_CUDA(launch(front_kernel, dim3(tokens), dim3(512), route_smem_bytes(tokens, L->E), stream, f));
   ExpertArgs ea = L->ea;
   ea.rows_out = rows;
@@ -503,11 +534,13 @@ int mm_layer_forward(mm_layer *L, const mm_forward_args *a, void *stream) {
   const int T = a->tokens;
   if (T < 1 || T > L->Tmax) return fail(MM_ERR_INVALID, "tokens %d outside 1..%d", T, L->Tmax);
   const float *logits = a->logits;
-  if (a->router_w) {
-    float *lo = a->logits_out ? a->logits_out : L->logits;
-    int rc = mm_router_gemv(a->x, a->router_w, lo, T, L->R, L->H, stream);
+  if (!a->x || !aligned(a->x, 16)) return fail(MM_ERR_INVALID, "mm_layer_forward: x must be a 16-byte aligned pointer");
+  MM_CUDA(cudaSetDevice(L->d.device));
+  {
+    float *lo = a->router_w ? (a->logits_out ? a->logits_out : L->logits) : nullptr;
+    int rc = launch_router_quant(L, a->x, a->router_w, lo, T, stream);
     if (rc) return rc;
-    logits = lo;
+    if (a->router_w) logits = lo;
   }
   if (!logits) return fail(MM_ERR_INVALID, "mm_layer_forward: neither router_w nor logits");
   mm_gate_args g = {};
@@ -523,7 +556,7 @@ int mm_layer_forward(mm_layer *L, const mm_forward_args *a, void *stream) {
   int32_t *perm = a->permuted ? a->permuted : L->permuted;
   int32_t *rec = a->record ? a->record : L->record;
   if (!a->rows) return fail(MM_ERR_INVALID, "mm_layer_forward: null rows buffer");
-  int rc = run_front_and_experts(L, a->x, &g, nullptr, T, perm, rec, a->rows, stream);
+  int rc = run_front_and_experts(L, a->x, &g, nullptr, T, perm, rec, a->rows, stream, true);
   if (rc) return rc;
   if (a->out || a->partial) {
     const uint16_t *shared = L->has_shared ? a->rows + static_cast<size_t>(L->shared_row_base) * L->H : nullptr;

@@ -10,6 +10,7 @@
 #include <cuda_runtime.h>
 
 #include "mm_kernels.cuh"
+#include "mm_layout.cuh"
 #include "mm_numerics.cuh"
 #include "mm_ptx.cuh"
 
@@ -22,19 +23,31 @@ __global__ void __launch_bounds__(256) finalize_kernel(FinalizeArgs a) {
   const int t = blockIdx.x;
   const int h0 = (blockIdx.y * 256 + threadIdx.x) * 8;
   if (h0 >= a.hidden) return;
+  // every slot's row index and weight first, then every row load, then the
+  // slot-order accumulation (the loads are independent; the order is not)
+  int perm[kMaxTopK];
+  float wt[kMaxTopK];
+#pragma unroll
+  for (int k = 0; k < kMaxTopK; ++k) {
+    perm[k] = k < a.top_k ? a.permuted[t * a.top_k + k] : -1;
+    wt[k] = k < a.top_k ? a.weights[t * a.top_k + k] : 0.0f;
+  }
+  uint4 row[kMaxTopK];
+#pragma unroll
+  for (int k = 0; k < kMaxTopK; ++k)
+    row[k] = perm[k] >= 0 ? *reinterpret_cast<const uint4 *>(a.rows + static_cast<size_t>(perm[k]) * a.hidden + h0)
+                          : make_uint4(0u, 0u, 0u, 0u);
   float acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
-  for (int k = 0; k < a.top_k; ++k) {
-    const int p = a.permuted[t * a.top_k + k];
-    if (p < 0) continue;
-    const float w = a.weights[t * a.top_k + k];
-    const uint4 v = *reinterpret_cast<const uint4 *>(a.rows + static_cast<size_t>(p) * a.hidden + h0);
-    const uint32_t q[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int k = 0; k < kMaxTopK; ++k) {
+    if (perm[k] < 0) continue;
+    const uint32_t q[4] = {row[k].x, row[k].y, row[k].z, row[k].w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      acc[2 * j] = __fmaf_rn(w, __uint_as_float(q[j] << 16), acc[2 * j]);
-      acc[2 * j + 1] = __fmaf_rn(w, __uint_as_float(q[j] & 0xffff0000u), acc[2 * j + 1]);
+      acc[2 * j] = __fmaf_rn(wt[k], __uint_as_float(q[j] << 16), acc[2 * j]);
+      acc[2 * j + 1] = __fmaf_rn(wt[k], __uint_as_float(q[j] & 0xffff0000u), acc[2 * j + 1]);
     }
   }
   float sh[8];

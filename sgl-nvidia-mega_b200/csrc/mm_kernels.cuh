@@ -39,10 +39,18 @@ struct RouteArgs {
 struct FrontArgs {
   GateArgs gate;             // gate.logits null: ids are given in route.ids
   RouteArgs route;
+};
+
+constexpr int kMaxRouterParts = 16;  // H <= 16384 for the router GEMV
+
+struct RouterArgs {
   const uint16_t *x;         // bf16 [T, H]
-  uint8_t *xq;               // [kMaxTerms][max_tokens][H/2] packed E2M1
+  const uint16_t *w;         // bf16 [E, H] (null when gemv_ctas == 0)
+  float *logits;             // [T, E]
+  int tokens, experts, hidden;
+  int gemv_ctas;             // E, or 0 for quantization only
+  uint8_t *xq;               // [kMaxTerms][max_tokens][H/2] packed E2M1, or null
   uint8_t *xs;               // [kMaxTerms][max_tokens][H/32] E8M0
-  int hidden;
   int max_tokens;
   int terms;
 };
@@ -113,8 +121,7 @@ __device__ __forceinline__ void quantize_block32_fp4(const float (&v)[32], int t
 }
 
 // kernels (definitions in mm_route.cu, mm_experts.cu, mm_finalize.cu)
-__global__ void router_gemv_kernel(const uint16_t *__restrict__ x, const uint16_t *__restrict__ w,
-                                   float *__restrict__ logits, int tokens, int experts, int hidden);
+__global__ void router_quant_kernel(RouterArgs a);
 __global__ void gate_topk_kernel(GateArgs g);
 __global__ void route_kernel(RouteArgs r);
 __global__ void front_kernel(FrontArgs f);

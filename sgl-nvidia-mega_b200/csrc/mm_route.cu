@@ -19,71 +19,114 @@
 namespace mm {
 
 // ============================================================================
-// K0: router GEMV. logits[t, e] = sum_h x[t, h] w[e, h], fp32.
+// K0: router GEMV + routed-input quantization in one launch.
 //
-// Summation order (the CPU oracle replays it): the hidden dimension is cut in
-// four parts of H/4 (one warp each); lane l of a part accumulates, for
-// j = 0, 1, ..., the eight elements h = part*H/4 + 8*(l + 32 j) + i (i = 0..7)
-// with acc = fma(x, w, acc) from acc = 0; the 32 lane sums are combined by the
-// butterfly acc += shfl_xor(acc, 16, 8, 4, 2, 1); the part sums as
-// (p0 + p1) + (p2 + p3). bf16 x bf16 products are exact in fp32.
-// grid (E, ceil(T/8)), block 128.
+// CTAs [0, gemv_ctas) x grid.y: logits[t, e] = sum_h x[t, h] w[e, h] (fp32) for
+// expert e = blockIdx.x and the 8 tokens of chunk blockIdx.y. Summation order
+// (the CPU oracle replays it): H is cut in parts of 1024; part p belongs to warp
+// p % 8; lane l of a part accumulates, for j = 0..3 and i = 0..7, the element
+// h = 1024 p + 8 (l + 32 j) + i with acc = fma(x, w, acc) from acc = 0; the 32
+// lane sums are combined by the butterfly acc += shfl_xor(acc, 16, 8, 4, 2, 1);
+// the part sums in part order, s = ((p0 + p1) + p2) + ... bf16 x bf16 products
+// are exact in fp32. The weight row is static, so its loads are issued before
+// the grid-dependency wait.
+//
+// CTAs [gemv_ctas, ...) (blockIdx.y == 0): the MXFP4 terms of x, one 32-element
+// block of one token per thread (independent of the routing).
 // ============================================================================
-__global__ void __launch_bounds__(128) router_gemv_kernel(const uint16_t *__restrict__ x,
-                                                          const uint16_t *__restrict__ w,
-                                                          float *__restrict__ logits, int tokens,
-                                                          int experts, int hidden) {
+__global__ void __launch_bounds__(256) router_quant_kernel(RouterArgs a) {
   pdl_launch_dependents();
-  const int e = blockIdx.x;
-  const int t0 = blockIdx.y * 8;
-  const int nt = min(8, tokens - t0);
-  const int part = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kp = hidden >> 2;
-  const int nvec = kp >> 8;  // 16-byte vectors per lane
-  __shared__ float part_sum[4][8];
-  // The weights are static: stream them before waiting for the producer of x.
-  const uint4 *wrow = reinterpret_cast<const uint4 *>(w + static_cast<size_t>(e) * hidden + part * kp);
-  pdl_wait();
-  float acc[8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (static_cast<int>(blockIdx.x) >= a.gemv_ctas) {
+    pdl_wait();
+    if (blockIdx.y != 0 || a.xq == nullptr) return;
+    const int blocks = a.hidden >> 5;
+    const int idx = (blockIdx.x - a.gemv_ctas) * blockDim.x + threadIdx.x;
+    if (idx >= a.tokens * blocks) return;
+    const int t = idx / blocks, b = idx - t * blocks;
+    const uint4 *src = reinterpret_cast<const uint4 *>(a.x + static_cast<size_t>(t) * a.hidden + 32 * b);
+    float v[32];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
-#pragma unroll 1
-  for (int j = 0; j < nvec; ++j) {
-    const int v = lane + 32 * j;
-    const uint4 wv = __ldg(wrow + v);
-    const uint32_t wq[4] = {wv.x, wv.y, wv.z, wv.w};
+    for (int i = 0; i < 4; ++i) {
+      const uint4 u = src[i];
+      const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-    for (int tt = 0; tt < 8; ++tt) {
-      if (tt < nt) {
-        const uint4 xv = __ldg(reinterpret_cast<const uint4 *>(
-                                   x + static_cast<size_t>(t0 + tt) * hidden + part * kp) +
-                               v);
-        const uint32_t xq[4] = {xv.x, xv.y, xv.z, xv.w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          acc[tt] = __fmaf_rn(__uint_as_float(xq[q] << 16), __uint_as_float(wq[q] << 16), acc[tt]);
-          acc[tt] = __fmaf_rn(__uint_as_float(xq[q] & 0xffff0000u),
-                              __uint_as_float(wq[q] & 0xffff0000u), acc[tt]);
-        }
+      for (int j = 0; j < 4; ++j) {
+        v[8 * i + 2 * j] = __uint_as_float(w4[j] << 16);
+        v[8 * i + 2 * j + 1] = __uint_as_float(w4[j] & 0xffff0000u);
       }
     }
+    const size_t q_stride = static_cast<size_t>(a.max_tokens) * (a.hidden >> 1);
+    const size_t s_stride = static_cast<size_t>(a.max_tokens) * blocks;
+    quantize_block32_fp4(v, a.terms, a.xq + static_cast<size_t>(t) * (a.hidden >> 1) + 16 * b, q_stride,
+                         a.xs + static_cast<size_t>(t) * blocks + b, s_stride);
+    return;
   }
+  __shared__ float part_sum[kMaxRouterParts][8];
+  const int e = blockIdx.x;
+  const int t0 = blockIdx.y * 8;
+  const int nt = min(8, a.tokens - t0);
+  const int parts = a.hidden >> 10;
+  // the weight row first (static): four 16-byte vectors per lane and part
+  uint4 wv[kMaxRouterParts / 8][4];
 #pragma unroll
-  for (int tt = 0; tt < 8; ++tt) {
+  for (int pi = 0; pi < kMaxRouterParts / 8; ++pi) {
+    const int part = warp + 8 * pi;
 #pragma unroll
-    for (int off = 16; off >= 1; off >>= 1)
-      acc[tt] = __fadd_rn(acc[tt], __shfl_xor_sync(0xffffffffu, acc[tt], off));
+    for (int j = 0; j < 4; ++j)
+      wv[pi][j] = part < parts ? __ldg(reinterpret_cast<const uint4 *>(a.w + static_cast<size_t>(e) * a.hidden +
+                                                                       1024 * part) + lane + 32 * j)
+                               : make_uint4(0u, 0u, 0u, 0u);
   }
-  if (lane == 0) {
+  pdl_wait();
 #pragma unroll
-    for (int tt = 0; tt < 8; ++tt) part_sum[part][tt] = acc[tt];
+  for (int pi = 0; pi < kMaxRouterParts / 8; ++pi) {
+    const int part = warp + 8 * pi;
+    if (part >= parts) break;
+    float acc[8];
+#pragma unroll
+    for (int tt = 0; tt < 8; tt += 2) {
+      uint4 xv[2][4];
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          xv[u][j] = (tt + u < nt) ? __ldg(reinterpret_cast<const uint4 *>(a.x + static_cast<size_t>(t0 + tt + u) * a.hidden +
+                                                                           1024 * part) + lane + 32 * j)
+                                   : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        float s = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t xq[4] = {xv[u][j].x, xv[u][j].y, xv[u][j].z, xv[u][j].w};
+          const uint32_t wq[4] = {wv[pi][j].x, wv[pi][j].y, wv[pi][j].z, wv[pi][j].w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            s = __fmaf_rn(__uint_as_float(xq[q] << 16), __uint_as_float(wq[q] << 16), s);
+            s = __fmaf_rn(__uint_as_float(xq[q] & 0xffff0000u), __uint_as_float(wq[q] & 0xffff0000u), s);
+          }
+        }
+        acc[tt + u] = s;
+      }
+    }
+#pragma unroll
+    for (int tt = 0; tt < 8; ++tt) {
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1)
+        acc[tt] = __fadd_rn(acc[tt], __shfl_xor_sync(0xffffffffu, acc[tt], off));
+    }
+    if (lane == 0) {
+#pragma unroll
+      for (int tt = 0; tt < 8; ++tt) part_sum[part][tt] = acc[tt];
+    }
   }
   __syncthreads();
-  if (threadIdx.x < nt) {
+  if (static_cast<int>(threadIdx.x) < nt) {
     const int tt = threadIdx.x;
-    const float s = __fadd_rn(__fadd_rn(part_sum[0][tt], part_sum[1][tt]),
-                              __fadd_rn(part_sum[2][tt], part_sum[3][tt]));
-    logits[static_cast<size_t>(t0 + tt) * experts + e] = s;
+    float s = part_sum[0][tt];
+    for (int p = 1; p < parts; ++p) s = __fadd_rn(s, part_sum[p][tt]);
+    a.logits[static_cast<size_t>(t0 + tt) * a.experts + e] = s;
   }
 }
 
@@ -200,31 +243,6 @@ __global__ void __launch_bounds__(512) gate_topk_kernel(GateArgs g) {
   pdl_wait();
   const int valid = g.num_valid != nullptr ? *g.num_valid : static_cast<int>(gridDim.x);
   gate_row(g, blockIdx.x, valid, sm);
-}
-
-// ============================================================================
-// MXFP4 terms of one bf16 row (block of 512 threads, one 32-element block per
-// thread): q [term][.][H/2] at stride q_stride, s [term][.][H/32] at s_stride.
-// ============================================================================
-__device__ void quantize_row(const uint16_t *__restrict__ xrow, uint8_t *__restrict__ q,
-                             size_t q_stride, uint8_t *__restrict__ s, size_t s_stride, int hidden,
-                             int terms) {
-  const int blocks = hidden >> 5;
-  for (int b = threadIdx.x; b < blocks; b += blockDim.x) {
-    const uint4 *src = reinterpret_cast<const uint4 *>(xrow + 32 * b);
-    float v[32];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint4 u = src[i];
-      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        v[8 * i + 2 * j] = __uint_as_float(w[j] << 16);
-        v[8 * i + 2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
-      }
-    }
-    quantize_block32_fp4(v, terms, q + 16 * b, q_stride, s + b, s_stride);
-  }
 }
 
 // ============================================================================
@@ -355,9 +373,9 @@ __global__ void __launch_bounds__(512) route_kernel(RouteArgs r) {
 }
 
 // ============================================================================
-// The fused front kernel: grid = T rows, block 512. Each CTA ranks its row
-// (or takes given ids) and quantizes its token; the last CTA to finish builds
-// the route record and the work tables.
+// The front kernel: grid = T rows, block 512. Each CTA ranks its row (or takes
+// given ids); the last CTA to finish builds the route record and the work
+// tables.
 // ============================================================================
 __global__ void __launch_bounds__(512) front_kernel(FrontArgs f) {
   pdl_launch_dependents();
@@ -370,10 +388,6 @@ __global__ void __launch_bounds__(512) front_kernel(FrontArgs f) {
     const int valid = f.gate.num_valid != nullptr ? *f.gate.num_valid : f.route.tokens;
     gate_row(f.gate, row, valid, gsm);
   }
-  const size_t q_stride = static_cast<size_t>(f.max_tokens) * (f.hidden >> 1);
-  const size_t s_stride = static_cast<size_t>(f.max_tokens) * (f.hidden >> 5);
-  quantize_row(f.x + static_cast<size_t>(row) * f.hidden, f.xq + static_cast<size_t>(row) * (f.hidden >> 1),
-               q_stride, f.xs + static_cast<size_t>(row) * (f.hidden >> 5), s_stride, f.hidden, f.terms);
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
