@@ -300,7 +300,7 @@ __device__ void build_route(const RouteArgs &r, unsigned char *smem_raw) {
   __syncthreads();
   for (int s = tid; s < slots; s += blockDim.x) {
     const int t = s / K;
-    const int e = r.ids[s] - r.expert_offset;
+    const int e = __ldcg(r.ids + s) - r.expert_offset;  // written by other CTAs: L2
     if (e >= 0 && e < E) atomicOr(&rowmask[e * words + (t >> 5)], 1u << (t & 31));
   }
   __syncthreads();
@@ -321,7 +321,7 @@ __device__ void build_route(const RouteArgs &r, unsigned char *smem_raw) {
   }
   for (int s = tid; s < slots; s += blockDim.x) {
     const int t = s / K;
-    const int e = r.ids[s] - r.expert_offset;
+    const int e = __ldcg(r.ids + s) - r.expert_offset;  // written by other CTAs: L2
     if (e < 0 || e >= E) {
       r.permuted[s] = -1;
       continue;
