@@ -158,6 +158,22 @@ int64_t mm_route_words(int32_t tokens, int32_t top_k, int32_t experts);
 int mm_route(const int32_t *ids, int32_t *permuted, int32_t *record, int32_t tokens,
              int32_t top_k, int32_t experts, int32_t expert_offset, void *stream);
 
+/* The router top-k and the route record in ONE launch that allocates nothing.
+ * No counterpart in the reference. For callers that cannot call cudaMalloc: code
+ * running while a CUDA graph is captured, or inside a runtime whose memory pool
+ * owns the device, with only its input and output buffers at hand (the same fused
+ * launch inside mm_layer_* uses scratch that mm_layer_create allocates).
+ * Outputs equal mm_gate_topk followed by mm_route. gate->ids may be NULL (ids
+ * not returned). Scratch: 8.25 KB of the library's static device memory per
+ * GPU, held until exit; tokens * top_k <= 2048, larger requests are rejected
+ * with MM_ERR_INVALID. The first call on a device sets the scratch up (symbol lookup,
+ * a cudaMemset of its counter) and should come before any stream capture. All
+ * calls on a device share the scratch: calls that overlap on the GPU (other
+ * streams) race; consecutive calls on one stream do not. */
+int mm_gate_route_noalloc(const mm_gate_args *gate, int32_t tokens, int32_t router_experts,
+                          int32_t top_k, int32_t experts, int32_t expert_offset,
+                          int32_t *permuted, int32_t *record, void *stream);
+
 /* out[t] = bf16(bf16(sum_k w[t,k] * rows[perm[t,k]]) + shared[t]) in slot order
  * (rows with perm -1 are skipped); shared_rows may be NULL. partial (fp32
  * [2, T, H]) receives the un-rounded routed sum and the shared row instead

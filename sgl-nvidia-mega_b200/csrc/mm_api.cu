@@ -100,6 +100,18 @@ int encode_fp4_map(CUtensorMap *map, const void *base, int k, int rows, int n, i
 
 }  // namespace
 
+namespace mm {
+int set_error(int code, const char *fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_error = buf;
+  return code;
+}
+}  // namespace mm
+
 struct mm_layer {
   mm_layer_desc d;
   int H, I, E, R, offset, K, Tmax, terms;

@@ -120,6 +120,14 @@ __device__ __forceinline__ void quantize_block32_fp4(const float (&v)[32], int t
   }
 }
 
+// Host helpers shared by the .cu files (mm_api.cu defines them).
+int set_error(int code, const char *fmt, ...);
+// dynamic shared memory of the route build for (tokens, local experts)
+inline size_t route_smem_size(int tokens, int experts) {
+  const int words = (tokens + 31) / 32;
+  return static_cast<size_t>(experts) * words * 4 + static_cast<size_t>(experts) * 4 * 3 + 32 * 4;
+}
+
 // kernels (definitions in mm_route.cu, mm_experts.cu, mm_finalize.cu)
 __global__ void router_quant_kernel(RouterArgs a);
 __global__ void gate_topk_kernel(GateArgs g);

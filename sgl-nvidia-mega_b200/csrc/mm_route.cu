@@ -9,8 +9,10 @@
 // consecutive tiles. The construction here is our own (multi-word row masks in
 // shared memory and one block scan, for up to 256 rows).
 #include <cstdint>
+#include <mutex>
 #include <cuda_runtime.h>
 
+#include "megamoe.h"
 #include "mm_kernels.cuh"
 #include "mm_layout.cuh"
 #include "mm_numerics.cuh"
@@ -401,4 +403,140 @@ __global__ void __launch_bounds__(512) front_kernel(FrontArgs f) {
   if (threadIdx.x == 0) f.route.ctrl[kCtrlTicket] = 0;
 }
 
+// ============================================================================
+// Router top-k + route record in one launch that allocates nothing.
+//
+// For callers that cannot call cudaMalloc: code that runs while a CUDA graph is
+// being captured or inside a serving runtime that owns all device memory through
+// its own pool, and that has only its input and output buffers at hand. The
+// fused launch (one CTA per row, the last CTA builds the record) needs scratch
+// that outlives a CTA (the last-CTA ticket and the top-k ids of every row);
+// mm_layer_create provides it with cudaMalloc, this variant keeps it in the
+// file-scope array below instead: 8.25 KB of static device memory that every
+// GPU which loads libmegamoe holds until the process exits.
+//   words [0, kNoAllocIdsWord): the ticket (word 0; zero between launches)
+//   words [kNoAllocIdsWord, + kNoAllocMaxSlots): the staged top-k ids
+// ============================================================================
+constexpr int kNoAllocMaxSlots = 2048;  // tokens * top_k
+constexpr int kNoAllocIdsWord = 64;
+constexpr int kNoAllocWords = kNoAllocIdsWord + kNoAllocMaxSlots;
+static __device__ __align__(256) int g_noalloc_scratch[kNoAllocWords];
+
+__global__ void __launch_bounds__(512) gate_route_noalloc_kernel(GateArgs g, RouteArgs r, int *scratch,
+                                                                  int *ids_out) {
+  pdl_launch_dependents();
+  extern __shared__ __align__(16) unsigned char na_smem[];
+  __shared__ GateSmem gsm;
+  __shared__ int is_last;
+  pdl_wait();  // the previous launch on this stream (same scratch) has completed
+  const int valid = g.num_valid != nullptr ? *g.num_valid : r.tokens;
+  gate_row(g, blockIdx.x, valid, gsm);  // g.ids_out points into the scratch
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int ticket = atomicAdd(&scratch[0], 1);
+    is_last = ticket == static_cast<int>(gridDim.x) - 1;
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  build_route(r, na_smem);
+  if (ids_out != nullptr) {
+    const int slots = r.tokens * r.top_k;
+    for (int i = threadIdx.x; i < slots; i += blockDim.x) ids_out[i] = __ldcg(r.ids + i);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) scratch[0] = 0;  // re-arm the ticket for the next launch
+}
+
+namespace {
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+int *g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Once per device, with that device current: the device address of the scratch
+// array (in host code its name is only a stand-in), its ticket cleared, and the
+// kernel's shared-memory limit raised. Runs on the first call on a device.
+int noalloc_setup(int device, int **out) {
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_ptr[device] == nullptr) {
+    int *ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void **>(&ptr), g_noalloc_scratch);
+    if (e != cudaSuccess)
+      return set_error(MM_ERR_CUDA, "mm_gate_route_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+    e = cudaMemset(ptr, 0, sizeof(int) * kNoAllocIdsWord);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gate_route_noalloc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(route_smem_size(kMaxTokens, kMaxRouterExperts)));
+    if (e != cudaSuccess)
+      return set_error(MM_ERR_CUDA, "mm_gate_route_noalloc: set-up failed: %s", cudaGetErrorString(e));
+    g_noalloc_ptr[device] = ptr;
+  }
+  *out = g_noalloc_ptr[device];
+  return MM_OK;
+}
+}  // namespace
+
 }  // namespace mm
+
+extern "C" int mm_gate_route_noalloc(const mm_gate_args *gate, int32_t tokens, int32_t router_experts,
+                                     int32_t top_k, int32_t experts, int32_t expert_offset, int32_t *permuted,
+                                     int32_t *record, void *stream) {
+  using namespace mm;
+  if (!gate || !gate->logits || !gate->weights || !permuted || !record)
+    return set_error(MM_ERR_INVALID, "mm_gate_route_noalloc: null pointer");
+  if (tokens < 1 || tokens > kMaxTokens || router_experts < 1 || router_experts > kMaxRouterExperts ||
+      top_k < 1 || top_k > kMaxTopK || top_k > router_experts)
+    return set_error(MM_ERR_INVALID, "mm_gate_route_noalloc: tokens %d, router_experts %d, top_k %d out of range",
+                     tokens, router_experts, top_k);
+  if (tokens * top_k > kNoAllocMaxSlots)
+    return set_error(MM_ERR_INVALID,
+                     "mm_gate_route_noalloc: tokens * top_k = %d exceeds the static scratch (%d slots)",
+                     tokens * top_k, kNoAllocMaxSlots);
+  if (experts < 1 || experts > kMaxRouterExperts || expert_offset < 0 || expert_offset + experts > router_experts)
+    return set_error(MM_ERR_INVALID, "mm_gate_route_noalloc: local experts [%d, %d) outside the router's %d",
+                     expert_offset, expert_offset + experts, router_experts);
+  if (gate->score_func != MM_SCORE_SIGMOID && gate->score_func != MM_SCORE_SOFTMAX)
+    return set_error(MM_ERR_UNSUPPORTED, "mm_gate_route_noalloc: score function %d is not built", gate->score_func);
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess || device < 0 || device >= kNoAllocMaxDevices)
+    return set_error(MM_ERR_CUDA, "mm_gate_route_noalloc: no usable current device");
+  int *scratch = nullptr;
+  int rc = noalloc_setup(device, &scratch);
+  if (rc) return rc;
+  GateArgs g;
+  g.logits = gate->logits;
+  g.bias = gate->bias;
+  g.num_valid = gate->num_valid;
+  g.score_func = gate->score_func;
+  g.renormalize = gate->renormalize;
+  g.routed_scaling = gate->routed_scaling;
+  g.renorm_eps = gate->renorm_eps;
+  g.router_experts = router_experts;
+  g.top_k = top_k;
+  g.weights_out = gate->weights;
+  g.ids_out = scratch + kNoAllocIdsWord;
+  RouteArgs r = {};
+  r.ids = scratch + kNoAllocIdsWord;
+  r.permuted = permuted;
+  r.record = record;
+  r.tokens = tokens;
+  r.top_k = top_k;
+  r.experts = experts;
+  r.expert_offset = expert_offset;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(tokens);
+  cfg.blockDim = dim3(512);
+  cfg.dynamicSmemBytes = route_smem_size(tokens, experts);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, gate_route_noalloc_kernel, g, r, scratch, gate->ids);
+  if (e != cudaSuccess)
+    return set_error(MM_ERR_CUDA, "mm_gate_route_noalloc: launch failed: %s", cudaGetErrorString(e));
+  return MM_OK;
+}

@@ -114,6 +114,10 @@ SIGNATURES = {
     "mm_gate_topk": (c_int32, [POINTER(MMGateArgs), c_int32, c_int32, c_int32, c_void_p]),
     "mm_route_words": (c_int64, [c_int32, c_int32, c_int32]),
     "mm_route": (c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_void_p]),
+    "mm_gate_route_noalloc": (
+        c_int32,
+        [POINTER(MMGateArgs), c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p],
+    ),
     "mm_finalize": (
         c_int32,
         [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p],
