@@ -256,14 +256,17 @@ def run_mm(args):
         e2e_ms = float(t.item())
     e2e_value = T * e2e_steps / (e2e_ms / 1e3)
 
+    # DRAM bytes of the dominant kernel: measured per streamed expert in one ncu
+    # capture of a smaller case (profiles/expert_kernel_traffic.json), scaled by
+    # the experts this launch streams; only where the capture's shape applies
     traffic = None
     tpath = os.path.join(REPO, "profiles", "expert_kernel_traffic.json")
     if os.path.exists(tpath):
         try:
             with open(tpath) as f:
                 tj = json.load(f)
-            if int(tj.get("world", 1)) == world and int(tj.get("tokens", T)) == T:
-                traffic = tj.get("bytes_per_launch")
+            if int(tj["world"]) == world and int(tj["hidden"]) == H and int(tj["intermediate"]) == I:
+                traffic = float(tj["traffic_bytes_per_expert"]) * (last_d + 1)
         except Exception:
             traffic = None
 
