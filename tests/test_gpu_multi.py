@@ -1,0 +1,92 @@
+"""Two-GPU parity (NCCL): the layer split tensor-parallel on the intermediate, or
+expert-parallel by expert windows, over two ranks; each rank runs the chain on its
+part (forward(partial=True)), the fp32 partial sums meet in an NCCL all-reduce and
+finalize_partial rounds them. The result must match the fp32 oracle of the whole
+layer within BASELINE's bar. Skipped with fewer than two GPUs."""
+
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                                 reason="needs two GPUs")]
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, mode, queue):
+    import sys
+
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [repo, os.path.join(repo, "sgl-nvidia-mega_b200")]
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        import megamoe
+        from megamoe import shard
+        from oracle import oracle as O
+
+        H, I, E, K, T = 1024, 512, 32, 8, 8
+        layer = O.make_layer(H, I, E, shared=True, seed=9)
+        x, wr, bias = O.make_inputs(T, H, E, seed=9)
+        if mode == "tp":
+            w = shard.tp_slice(layer["w13"], layer["w13_scale"], layer["w2"], layer["w2_scale"], rank, world)
+            sh = shard.tp_slice(*layer["shared"], rank, world)
+            moe = megamoe.RoutedMoE(*(t.to(dev) for t in w), K, 16, shared=[t.to(dev) for t in sh])
+        else:
+            offset, local = shard.ep_window(E, rank, world)
+            w = shard.ep_slice([layer["w13"], layer["w13_scale"], layer["w2"], layer["w2_scale"]], rank, world)
+            sh = [t.to(dev) for t in layer["shared"]] if rank == 0 else None
+            moe = megamoe.RoutedMoE(*(t.to(dev) for t in w), K, 16, router_experts=E, expert_offset=offset,
+                                    shared=sh)
+        bufs = {}
+        part = moe.forward(x.to(dev), router_weight=wr.to(dev), bias=bias.to(dev), routed_scaling_factor=2.5,
+                           partial=True, buffers=bufs)
+        dist.all_reduce(part)
+        out = megamoe.finalize_partial(part)
+        torch.cuda.synchronize()
+        moe.check()
+        if rank == 0:
+            logits = O.router_gemv(O.bf16_bits(x), O.bf16_bits(wr))
+            ow, oids = O.gate_topk(logits, bias.numpy(), K, scale=2.5)
+            same_ids = bool(np.array_equal(bufs["ids"].cpu().numpy(), oids))
+            ref, _, _ = O.moe_layer(x, oids, ow, layer)
+            queue.put((same_ids, O.max_abs_rel(out.float().cpu().numpy(), ref.numpy())))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("mode", ["tp", "ep"])
+def test_two_gpu_partitions_match_the_oracle(mode):
+    from oracle import oracle as O
+
+    O.build()
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, queue)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    same_ids, err = queue.get(timeout=5)
+    assert same_ids
+    assert err <= 2e-2, err
