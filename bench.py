@@ -14,6 +14,7 @@ A step is one MoE layer over one batch: router GEMV -> top-k -> route ->
 gate_up -> SwiGLU + requant -> down -> combine (-> all-reduce). Each step takes
 the next of 64 resident token batches (distinct routings); one step streams
 ~1.4 GB of expert weights, far above the 126 MB L2, so no flush is needed.
+The e2e figure goes through the public API call with host buffers.
 
 Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mm|reference]
 Under torchrun each rank drives one GPU; rank 0 prints one JSON line.
@@ -295,6 +296,7 @@ def run_mm(args):
             "tokens": T,
             "parallelism": f"tp{world}" if world > 1 else "single",
             "l2": "inputs larger than L2 (~1.4 GB of expert weights per step, 64 distinct token batches)",
+            "launch": "eager, PDL-chained launches",
             "distinct_experts_per_step": d_mean,
             "layer_weight_bytes": layer_bytes,
             "layer_roofline_frac": (layer_bytes / (ms_step / 1e3) / 1e9) / peak,
