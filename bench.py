@@ -7,9 +7,11 @@ Workload (all synthetic, seeded; random-init MXFP4 weights of the named shape):
          2.5, MXFP4 weights (E2M1 codes uniform over 16 nibbles, E8M0 exponents
          uniform in [-10, -6]), 8 tokens of bf16 x ~ N(0, 1).
   N > 1: the same layer tensor-parallel on the expert intermediate (2048 / N per
-         rank, shared expert split alike), routing replicated on every rank, the
-         fp32 partial sums combined by an NCCL all-reduce; total work fixed
-         ("scaling": "strong").
+         rank, shared expert split alike), routing replicated on every rank; the
+         combine fused with the all-reduce over NVLink peer memory (one launch:
+         each rank pushes its combined rows to every peer by P2P stores, waits on
+         per-tile flags, sums in rank order), or with --combine nccl the fp32
+         partial sums all-reduced by NCCL; total work fixed ("scaling": "strong").
 A step is one MoE layer over one batch: router GEMV -> top-k -> route ->
 gate_up -> SwiGLU + requant -> down -> combine (-> all-reduce). Each step takes
 the next of 64 resident token batches (distinct routings); one step streams
@@ -52,6 +54,8 @@ def parse_args():
     ap.add_argument("--experts", type=int, default=384,
                     help="routed experts (384 = config 2; fewer only for small profiling cases)")
     ap.add_argument("--impl", choices=["mm", "reference"], default="mm")
+    ap.add_argument("--combine", choices=["peer", "nccl"], default="peer",
+                    help="N > 1: fused combine + peer all-reduce (default) or NCCL all-reduce of fp32 partials")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -171,10 +175,13 @@ def run_mm(args):
     moe, w, shared, router, bias, xs = build_layer(rank, world, T, dev)
     bufs = {}
     out_buf = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    peer = world > 1 and args.combine == "peer"
+    comm = megamoe.PeerAllReduce(T, H) if peer else None
 
     def step(x):
-        if world == 1:
-            return moe.forward(x, router_weight=router, bias=bias, routed_scaling_factor=SCALE, buffers=bufs)
+        if world == 1 or peer:
+            return moe.forward(x, router_weight=router, bias=bias, routed_scaling_factor=SCALE, buffers=bufs,
+                               comm=comm)
         part = moe.forward(x, router_weight=router, bias=bias, routed_scaling_factor=SCALE, partial=True,
                            buffers=bufs)
         dist.all_reduce(part)
@@ -187,9 +194,14 @@ def run_mm(args):
             dist.barrier()
         torch.cuda.synchronize()
 
+    def check():
+        moe.check()
+        if comm is not None:
+            comm.check()
+
     for i in range(max(args.warmup, 3)):
         step(xs[i % POOL])
-    moe.check()
+    check()
     barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
@@ -204,7 +216,7 @@ def run_mm(args):
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    moe.check()
+    check()
     ms_step = ms / args.steps
     value = T * args.steps / (ms / 1e3)
 
@@ -297,6 +309,8 @@ def run_mm(args):
             "parallelism": f"tp{world}" if world > 1 else "single",
             "l2": "inputs larger than L2 (~1.4 GB of expert weights per step, 64 distinct token batches)",
             "launch": "eager, PDL-chained launches",
+            "combine": ("fused combine + all-reduce over NVLink peer memory" if peer else
+                        "NCCL all-reduce of fp32 partials + round" if world > 1 else "combine"),
             "distinct_experts_per_step": d_mean,
             "layer_weight_bytes": layer_bytes,
             "layer_roofline_frac": (layer_bytes / (ms_step / 1e3) / 1e9) / peak,
@@ -315,13 +329,17 @@ def run_mm(args):
         },
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
                 "d2h_bytes_per_step": T * H * 2, "steps": e2e_steps},
-        "gpu_launches": args.steps * (4 if world == 1 else 5),
+        "gpu_launches": args.steps * (4 if world == 1 or peer else 5),
         "clocks": clocks.summary(),
         "cpu_baseline": cpu,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
+    check()
     if dist is not None:
+        dist.barrier()
+        if comm is not None:
+            comm.close()
         dist.barrier()
         dist.destroy_process_group()
 

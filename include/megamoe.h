@@ -27,6 +27,9 @@
  *   mm_finalize          deepseek_v41/sm103/all_reduce_mhc.py:402-662 (finalize arithmetic);
  *                        glm5_3/sm103/moe/finalize.py:1-27
  *   mm_layer_forward     deepseek_v41/moe/step.py:101 (one MoE step: router -> combine)
+ *   mm_comm_*, mm_finalize_allreduce
+ *                        deepseek_v41/sm103/all_reduce_mhc.py:402-662 (per-rank publish)
+ *                        and :665-1190 (rank-order reduce); AllReduceMHC.finalize :1484
  */
 #ifndef MEGAMOE_H
 #define MEGAMOE_H
@@ -116,6 +119,8 @@ typedef struct mm_layer_info {
 } mm_layer_info;
 
 /* Whole-step arguments (mm_layer_forward). */
+typedef struct mm_comm mm_comm; /* opaque handle: see mm_comm_create */
+
 typedef struct mm_forward_args {
   const uint16_t *x;        /* bf16 [T, H]                                       */
   const uint16_t *router_w; /* bf16 [router_experts, H] or NULL (then logits)    */
@@ -134,6 +139,15 @@ typedef struct mm_forward_args {
   uint16_t *out;            /* out bf16 [T, H] combined, or NULL                 */
   float *partial;           /* out fp32 [2, T, H] (routed, shared) un-rounded
                                partial sums for a cross-rank all-reduce, or NULL */
+  mm_comm *comm;            /* non-NULL: out receives the group's all-reduced
+                               output (mm_finalize_allreduce) instead of this
+                               rank's own combine; partial must then be NULL   */
+  const uint16_t *residual; /* non-NULL (needs comm): the hop epilogue of
+                               mm_finalize_allreduce_norm; out receives the
+                               normalized output (NULL: none)                  */
+  const uint16_t *gamma;    /* bf16 [H] RMSNorm weight (with out)              */
+  float norm_eps;
+  uint16_t *residual_out;   /* bf16 [T, H] new residual (may alias residual)   */
 } mm_forward_args;
 
 /* ---- library ------------------------------------------------------------ */
@@ -186,6 +200,51 @@ int mm_finalize(const uint16_t *rows, const float *weights, const int32_t *permu
 int mm_finalize_partial(const float *partial, uint16_t *out, int32_t tokens,
                         int32_t hidden, void *stream);
 
+/* ---- combine + all-reduce over NVLink peer memory ------------------------ */
+/* One rank's view of a TP/EP group whose ranks exchange their partial outputs
+ * by plain P2P stores into each other's buffers (CUDA IPC; no multicast). */
+#define MM_IPC_HANDLE_BYTES 64
+
+/* Allocates this rank's tile counters and mailbox (2 generations x world x
+ * max_tokens x hidden bf16, every value the empty sentinel -0) on `device`. */
+int mm_comm_create(int32_t rank, int32_t world, int32_t max_tokens, int32_t hidden,
+                   int32_t device, mm_comm **out);
+/* Writes this rank's IPC handle (MM_IPC_HANDLE_BYTES bytes) to `handle`. */
+int mm_comm_handle(const mm_comm *comm, void *handle);
+/* Opens the peers' buffers from all ranks' handles (world x MM_IPC_HANDLE_BYTES,
+ * rank order; this rank's own entry is ignored). Once per comm. */
+int mm_comm_open(mm_comm *comm, const void *handles);
+int mm_comm_destroy(mm_comm *comm);
+/* Synchronizes and reads (then clears) the comm's device error word:
+ * MM_OK or MM_ERR_DEVICE_TIMEOUT (a peer's partial never arrived within 1.5 s;
+ * the group's comms must then be rebuilt). */
+int mm_comm_check(mm_comm *comm);
+
+/* out[t] = bf16( sum_{r = 0..world-1} y_r[t] ) in fp32, rank order, where
+ * y_r = bf16(bf16(sum_k w * rows_r[perm_r]) + shared_r) is rank r's partial
+ * (mm_finalize's arithmetic on rank r's rows). One launch per rank; every rank
+ * of the group must call it with the same tokens, in the same order. */
+int mm_finalize_allreduce(mm_comm *comm, const uint16_t *rows, const float *weights,
+                          const int32_t *permuted, const uint16_t *shared_rows,
+                          uint16_t *out, int32_t tokens, int32_t top_k, int32_t hidden,
+                          void *stream);
+
+/* The same combine + all-reduce with the residual + RMSNorm epilogue of a
+ * decoder hop (qwen3_5/sm103/hop/__init__.py:431 moe_finalize_all_reduce_rms_norm;
+ * arithmetic hop.cu:119-139, q35_hop.cuh:258-336): per token,
+ *   pre = bf16(sum_r y_r + residual)   (fp32 rank-order sum, one rounding)
+ *   residual_out = pre
+ *   norm_out = bf16((pre * inv) * gamma), inv = 1 / sqrt(sum(pre^2) / H + eps)
+ * with sqrt and divisions IEEE-rounded and the sum of squares in a fixed fold
+ * (8 features per thread in order, warp xor butterfly 16..1, 8 warps in order,
+ * the row's ceil(H / 2048) CTAs in order). norm_out may be NULL (then gamma
+ * too). H <= 16384. residual may alias residual_out. */
+int mm_finalize_allreduce_norm(mm_comm *comm, const uint16_t *rows, const float *weights,
+                               const int32_t *permuted, const uint16_t *shared_rows,
+                               const uint16_t *residual, const uint16_t *gamma, float eps,
+                               uint16_t *residual_out, uint16_t *norm_out, int32_t tokens,
+                               int32_t top_k, int32_t hidden, void *stream);
+
 /* ---- layer ---------------------------------------------------------------- */
 int mm_layer_create(const mm_layer_desc *desc, mm_layer **out);
 int mm_layer_destroy(mm_layer *layer);
@@ -217,6 +276,20 @@ int mm_layer_forward(mm_layer *layer, const mm_forward_args *args, void *stream)
 /* Synchronizes the layer's device and reads (then clears) its device error
  * word: MM_OK, MM_ERR_DEVICE_TIMEOUT or MM_ERR_DEVICE. */
 int mm_layer_check(mm_layer *layer);
+
+/* ---- stack ------------------------------------------------------------------ */
+/* One step of n MoE layers: mm_layer_forward(layers[i].layer, &layers[i].args)
+ * for i = 0..n-1 on one stream, with no host synchronization, so the launches
+ * of all layers chain by PDL (a layer's hop output is the next layer's input).
+ * The host side of the reference's layer loop (deepseek_v41/moe/step.py:101,
+ * called once per MoE layer by the megakernel's forward); stops at the first
+ * failing layer and returns its status. */
+typedef struct mm_stack_layer {
+  mm_layer *layer;
+  mm_forward_args args;
+} mm_stack_layer;
+
+int mm_stack_forward(const mm_stack_layer *layers, int32_t n, void *stream);
 
 #ifdef __cplusplus
 }

@@ -13,6 +13,7 @@
  * from it (tests/golden/make_golden.py).
  */
 #include <math.h>
+#include <stdlib.h>
 #include <stdint.h>
 #include <string.h>
 
@@ -369,4 +370,72 @@ void or_finalize(const uint16_t *rows, const float *w, const int *perm, const ui
       const float s = shared ? bf16_to_f(shared[(size_t)t * H + h]) : 0.0f;
       out[(size_t)t * H + h] = f_to_bf16(routed + s);
     }
+}
+
+/* ---------------------------------------------------------------------------
+ * Cross-rank sum of the ranks' finalized partials (all_reduce_mhc.py:955-977,
+ * rank_lanes = 1): acc = 0; acc += bf16 partial of rank r for r = 0..world-1
+ * in fp32; out = bf16(acc). y holds world arrays of n values, rank-major.
+ * ------------------------------------------------------------------------- */
+void or_allreduce_ranks(const uint16_t *y, uint16_t *out, int world, size_t n) {
+  for (size_t i = 0; i < n; ++i) {
+    float acc = 0.0f;
+    for (int r = 0; r < world; ++r) acc += bf16_to_f(y[(size_t)r * n + i]);
+    out[i] = f_to_bf16(acc);
+  }
+}
+
+/* ---------------------------------------------------------------------------
+ * All-reduce + residual + RMSNorm epilogue of the combine (the hop of
+ * qwen3_5/sm103/hop/src/hop.cu:119-139, q35_hop.cuh:258-336: pre =
+ * bf16(rank-order fp32 sum + residual); inv = 1/sqrt(sum(pre^2)/H + eps);
+ * norm = bf16((pre * inv) * gamma)). The sum of squares follows the kernel's
+ * fixed fold: a thread owns 8 consecutive features (feature 8 * (256 * c + 32 *
+ * w + l) for CTA c, warp w, lane l), sums x*x over them in order from 0; a
+ * warp folds its lanes by xor butterfly 16, 8, 4, 2, 1; a CTA adds its 8 warp
+ * sums in order from 0; the row adds its CTA sums in order from 0. sqrt and
+ * the divisions are IEEE (correctly rounded). y: world arrays of T x H bf16,
+ * rank-major. gamma NULL: norm_out is not written.
+ * ------------------------------------------------------------------------- */
+void or_allreduce_norm(const uint16_t *y, const uint16_t *residual, const uint16_t *gamma, float eps,
+                       uint16_t *residual_out, uint16_t *norm_out, int world, int T, int H) {
+  const size_t n = (size_t)T * H;
+  const int ctas = (H + 2047) / 2048;
+  float *pre = (float *)malloc(sizeof(float) * (size_t)H);
+  for (int t = 0; t < T; ++t) {
+    for (int h = 0; h < H; ++h) {
+      const size_t i = (size_t)t * H + h;
+      float acc = 0.0f;
+      for (int r = 0; r < world; ++r) acc += bf16_to_f(y[(size_t)r * n + i]);
+      const uint16_t p = f_to_bf16(acc + bf16_to_f(residual[i]));
+      residual_out[i] = p;
+      pre[h] = bf16_to_f(p);
+    }
+    float total = 0.0f;
+    for (int c = 0; c < ctas; ++c) {
+      float cta = 0.0f;
+      for (int w = 0; w < 8; ++w) {
+        float lane[32];
+        for (int l = 0; l < 32; ++l) {
+          const int h0 = 8 * (256 * c + 32 * w + l);
+          float s = 0.0f;
+          if (h0 < H)
+            for (int e = 0; e < 8; ++e) s += pre[h0 + e] * pre[h0 + e];
+          lane[l] = s;
+        }
+        for (int off = 16; off >= 1; off >>= 1) {
+          float nxt[32];
+          for (int l = 0; l < 32; ++l) nxt[l] = lane[l] + lane[l ^ off];
+          memcpy(lane, nxt, sizeof(lane));
+        }
+        cta += lane[0];
+      }
+      total += cta;
+    }
+    const float inv = 1.0f / sqrtf(total / (float)H + eps);
+    if (gamma && norm_out)
+      for (int h = 0; h < H; ++h)
+        norm_out[(size_t)t * H + h] = f_to_bf16((pre[h] * inv) * bf16_to_f(gamma[h]));
+  }
+  free(pre);
 }

@@ -16,7 +16,7 @@ low nibble and 2j+1 in the high nibble; E8M0 scale 2^(byte - 127) per 32
 elements along K (glm5_3/sm103/moe/api.py:39-53, route_quant.cuh:1-15).
 Expert MLP: gemm1.cu:6-7 + epilogue :656-1000 (clamped SwiGLU: up in [-L, L],
 gate <= L, h = up * gate * sigmoid(gate)), gemm2.cu:6-7. Combine:
-all_reduce_mhc.py:528-640.
+all_reduce_mhc.py:528-640; cross-rank sum: all_reduce_mhc.py:955-977.
 """
 
 from __future__ import annotations
@@ -189,6 +189,27 @@ def finalize(rows_bf16: np.ndarray, weights: np.ndarray, permuted: np.ndarray,
     out = np.empty((T, H), dtype=np.uint16)
     lib().or_finalize(_p(rows), _p(w), _p(perm), _p(sh), _p(out), T, K, H)
     return out
+
+
+def allreduce_ranks(partials) -> np.ndarray:
+    """bf16 bits of the rank-order fp32 sum of the ranks' bf16 partials."""
+    y = np.ascontiguousarray(np.stack([np.asarray(p, dtype=np.uint16) for p in partials]))
+    out = np.empty(y.shape[1:], dtype=np.uint16)
+    lib().or_allreduce_ranks(_p(y), _p(out), y.shape[0], ctypes.c_size_t(out.size))
+    return out
+
+
+def allreduce_norm(partials, residual: np.ndarray, gamma: Optional[np.ndarray], eps: float):
+    """(residual_out, norm_out) bf16 bits of the all-reduce + residual + RMSNorm
+    epilogue over the ranks' bf16 partials (norm_out None without gamma)."""
+    y = np.ascontiguousarray(np.stack([np.asarray(p, dtype=np.uint16) for p in partials]))
+    world, T, H = y.shape
+    res = np.ascontiguousarray(residual, dtype=np.uint16)
+    gam = None if gamma is None else np.ascontiguousarray(gamma, dtype=np.uint16)
+    r_out = np.empty((T, H), dtype=np.uint16)
+    n_out = None if gam is None else np.empty((T, H), dtype=np.uint16)
+    lib().or_allreduce_norm(_p(y), _p(res), _p(gam), c_float(eps), _p(r_out), _p(n_out), world, T, H)
+    return r_out, n_out
 
 
 def ref_route_lib() -> Optional[ctypes.CDLL]:

@@ -570,9 +570,27 @@ int mm_layer_forward(mm_layer *L, const mm_forward_args *a, void *stream) {
   if (!a->rows) return fail(MM_ERR_INVALID, "mm_layer_forward: null rows buffer");
   int rc = run_front_and_experts(L, a->x, &g, nullptr, T, perm, rec, a->rows, stream, true);
   if (rc) return rc;
+  const uint16_t *shared = L->has_shared ? a->rows + static_cast<size_t>(L->shared_row_base) * L->H : nullptr;
+  if (a->residual) {
+    if (!a->comm || a->partial) return fail(MM_ERR_INVALID, "mm_layer_forward: residual needs comm and no partial");
+    return mm_finalize_allreduce_norm(a->comm, a->rows, g.weights, perm, shared, a->residual, a->gamma, a->norm_eps,
+                                      a->residual_out, a->out, T, L->K, L->H, stream);
+  }
+  if (a->comm) {
+    if (!a->out || a->partial) return fail(MM_ERR_INVALID, "mm_layer_forward: comm needs out and no partial");
+    return mm_finalize_allreduce(a->comm, a->rows, g.weights, perm, shared, a->out, T, L->K, L->H, stream);
+  }
   if (a->out || a->partial) {
-    const uint16_t *shared = L->has_shared ? a->rows + static_cast<size_t>(L->shared_row_base) * L->H : nullptr;
     rc = mm_finalize(a->rows, g.weights, perm, shared, a->out, a->partial, T, L->K, L->H, stream);
+    if (rc) return rc;
+  }
+  return MM_OK;
+}
+
+int mm_stack_forward(const mm_stack_layer *layers, int32_t n, void *stream) {
+  if (!layers || n < 0) return fail(MM_ERR_INVALID, "mm_stack_forward: %d layers", n);
+  for (int i = 0; i < n; ++i) {
+    const int rc = mm_layer_forward(layers[i].layer, &layers[i].args, stream);
     if (rc) return rc;
   }
   return MM_OK;

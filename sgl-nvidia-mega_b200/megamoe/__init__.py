@@ -15,5 +15,7 @@ from .moe import (  # noqa: F401
     route_words,
     router_gemv,
 )
+from .comm import PeerAllReduce  # noqa: F401
+from .stack import MoEStack  # noqa: F401
 
-__all__ = ["RoutedMoE", "finalize", "finalize_partial", "gate_topk", "route", "route_words", "router_gemv"]
+__all__ = ["MoEStack", "PeerAllReduce", "RoutedMoE", "finalize", "finalize_partial", "gate_topk", "route", "route_words", "router_gemv"]

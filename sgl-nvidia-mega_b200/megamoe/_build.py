@@ -10,7 +10,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.dirname(HERE)
 REPO = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
-SOURCES = ["mm_api.cu", "mm_route.cu", "mm_experts.cu", "mm_finalize.cu"]
+SOURCES = ["mm_api.cu", "mm_route.cu", "mm_experts.cu", "mm_finalize.cu", "mm_comm.cu"]
 HEADERS = ["mm_kernels.cuh", "mm_layout.cuh", "mm_numerics.cuh", "mm_ptx.cuh"]
 OUTPUT = os.path.join(HERE, "libmegamoe.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")

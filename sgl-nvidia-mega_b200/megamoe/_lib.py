@@ -20,6 +20,7 @@ MM_ERR_UNSUPPORTED = 2
 MM_ERR_CUDA = 3
 MM_ERR_DEVICE_TIMEOUT = 4
 MM_ERR_DEVICE = 5
+MM_IPC_HANDLE_BYTES = 64
 
 MM_SCORE_SIGMOID = 0
 MM_SCORE_SOFTMAX = 1
@@ -103,7 +104,16 @@ class MMForwardArgs(ctypes.Structure):
         ("rows", c_void_p),
         ("out", c_void_p),
         ("partial", c_void_p),
+        ("comm", c_void_p),
+        ("residual", c_void_p),
+        ("gamma", c_void_p),
+        ("norm_eps", c_float),
+        ("residual_out", c_void_p),
     ]
+
+
+class MMStackLayer(ctypes.Structure):
+    _fields_ = [("layer", c_void_p), ("args", MMForwardArgs)]
 
 
 # name -> (restype, argtypes); every extern "C" symbol of include/megamoe.h
@@ -137,6 +147,21 @@ SIGNATURES = {
     "mm_layer_rerun_experts": (c_int32, [c_void_p, c_int32, c_void_p, c_void_p, c_void_p]),
     "mm_layer_forward": (c_int32, [c_void_p, POINTER(MMForwardArgs), c_void_p]),
     "mm_layer_check": (c_int32, [c_void_p]),
+    "mm_stack_forward": (c_int32, [POINTER(MMStackLayer), c_int32, c_void_p]),
+    "mm_comm_create": (c_int32, [c_int32, c_int32, c_int32, c_int32, c_int32, POINTER(c_void_p)]),
+    "mm_comm_handle": (c_int32, [c_void_p, c_void_p]),
+    "mm_comm_open": (c_int32, [c_void_p, c_void_p]),
+    "mm_comm_destroy": (c_int32, [c_void_p]),
+    "mm_comm_check": (c_int32, [c_void_p]),
+    "mm_finalize_allreduce_norm": (
+        c_int32,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_void_p,
+         c_int32, c_int32, c_int32, c_void_p],
+    ),
+    "mm_finalize_allreduce": (
+        c_int32,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p],
+    ),
 }
 
 _lib = None

@@ -243,13 +243,32 @@ class RoutedMoE:
         renormalize_epsilon: float = 0.0,
         partial: bool = False,
         buffers: Optional[dict] = None,
+        comm=None,
+        residual: Optional[torch.Tensor] = None,
+        gamma: Optional[torch.Tensor] = None,
     ):
         """One whole MoE step on the current stream. Returns the bf16 [T, H]
-        output (or the fp32 [2, T, H] partial sums with ``partial``). ``buffers``
+        output (or the fp32 [2, T, H] partial sums with ``partial``; with
+        ``comm``, a ``megamoe.PeerAllReduce`` of this rank's group, the output
+        all-reduced over the group in the same launch as the combine; with
+        ``comm`` and ``residual`` (bf16 [T, H]), the decoder hop's epilogue too:
+        returns (norm_out, residual_out) as ``comm.moe_finalize_all_reduce_rms_norm``
+        does, norm_out None without ``gamma``; residual_out may be ``residual``
+        itself via buffers["residual_out"]). ``buffers``
         (optional dict) receives the intermediate tensors and may carry
         preallocated ones (keys: logits, weights, ids, permuted, record, rows,
         out, partial) so repeated calls allocate nothing."""
         tokens = self._check_x(x)
+        if comm is not None and partial:
+            raise ValueError("forward: comm and partial are exclusive")
+        if residual is not None:
+            if comm is None:
+                raise ValueError("forward: residual needs comm (a PeerAllReduce, a group of one on one GPU)")
+            if residual.dtype != torch.bfloat16 or tuple(residual.shape) != (tokens, self.hidden) \
+                    or not residual.is_contiguous():
+                raise ValueError("residual must be contiguous bf16 [T, H]")
+            if gamma is not None and (gamma.dtype != torch.bfloat16 or tuple(gamma.shape) != (self.hidden,)):
+                raise ValueError("gamma must be bf16 [H]")
         b = {} if buffers is None else buffers
         dev = self.device
         if router_weight is not None:
@@ -272,7 +291,9 @@ class RoutedMoE:
         permuted = buf("permuted", (tokens, self.top_k), torch.int32)
         record = buf("record", (route_words(tokens, self.top_k, self.experts),), torch.int32)
         rows = buf("rows", (self.rows_capacity, self.hidden), torch.bfloat16)
-        out = None if partial else buf("out", (tokens, self.hidden), torch.bfloat16)
+        out = None if partial or (residual is not None and gamma is None) else \
+            buf("out", (tokens, self.hidden), torch.bfloat16)
+        res_out = buf("residual_out", (tokens, self.hidden), torch.bfloat16) if residual is not None else None
         part = buf("partial", (2, tokens, self.hidden), torch.float32) if partial else None
         a = _lib.MMForwardArgs()
         a.x = x.data_ptr()
@@ -290,7 +311,14 @@ class RoutedMoE:
         a.rows = rows.data_ptr()
         a.out = _ptr(out)
         a.partial = _ptr(part)
+        a.comm = None if comm is None else comm.handle
+        a.residual = _ptr(residual)
+        a.gamma = _ptr(gamma)
+        a.norm_eps = 0.0 if comm is None else comm.eps
+        a.residual_out = _ptr(res_out)
         check(lib().mm_layer_forward(self._handle, ctypes.byref(a), _stream(dev)), "mm_layer_forward")
+        if residual is not None:
+            return out, res_out
         return part if partial else out
 
     def rerun_experts(self, tokens: int, record: torch.Tensor, rows: torch.Tensor) -> None:

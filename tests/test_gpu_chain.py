@@ -237,3 +237,182 @@ def test_forward_matches_steps_and_graph():
     torch.cuda.synchronize()
     assert torch.equal(bufs["out"], out)
     moe.check()
+
+
+# ----------------------------------------------------------------------------- peer combine
+def test_peer_allreduce_group_of_one_matches_finalize():
+    """The combine fused with the all-reduce, in a group of one: each call's
+    output is bit-exact the oracle's combine, across calls whose token counts
+    change (the per-slot flags, counters and parity must stay consistent) and
+    across CUDA-graph replays (the state lives on the device)."""
+    mm = _mm()
+    g = torch.Generator().manual_seed(5)
+    K, H, P, TMAX = 8, 7168, 160, 16
+    comm = mm.PeerAllReduce(TMAX, H)
+    rows = torch.randn((P, H), generator=g).to(torch.bfloat16)
+    rg = rows.cuda()
+    for T in (8, 3, 8, 16, 1, 5, 16, 16, 2):
+        shared = torch.randn((T, H), generator=g).to(torch.bfloat16)
+        w = torch.rand((T, K), generator=g)
+        perm = torch.randint(-1, P, (T, K), generator=g).int()
+        out = comm.finalize(rg, w.cuda(), perm.cuda(), shared.cuda())
+        want = O.allreduce_ranks([O.finalize(O.bf16_bits(rows), w.numpy(), perm.numpy(), O.bf16_bits(shared))])
+        assert np.array_equal(O.bf16_bits(out.cpu()), want), T
+    comm.check()
+    T = 8
+    shared = torch.randn((T, H), generator=g).to(torch.bfloat16).cuda()
+    w = torch.rand((T, K), generator=g).cuda()
+    perm = torch.randint(-1, P, (T, K), generator=g).int().cuda()
+    out = torch.empty((T, H), dtype=torch.bfloat16, device="cuda")
+    eager = comm.finalize(rg, w, perm, shared).clone()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        comm.finalize(rg, w, perm, shared, out=out)
+    for _ in range(5):
+        out.zero_()
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, eager)
+    comm.check()
+    comm.close()
+
+
+def test_forward_with_peer_group_of_one():
+    """forward(comm=...) runs the whole step with the fused combine and equals forward()."""
+    mm = _mm()
+    H, I, E, K, T = 2048, 256, 64, 8, 8
+    layer = O.make_layer(H, I, E, shared=True, seed=23)
+    x, wr, bias = O.make_inputs(T, H, E, seed=23)
+    moe = to_gpu_layer(layer, K, 16)
+    comm = mm.PeerAllReduce(16, H)
+    xg, wg, bg = x.cuda(), wr.cuda(), bias.cuda()
+    want = moe.forward(xg, router_weight=wg, bias=bg, routed_scaling_factor=2.5).clone()
+    for _ in range(3):
+        got = moe.forward(xg, router_weight=wg, bias=bg, routed_scaling_factor=2.5, comm=comm)
+        assert torch.equal(got, want)
+    with pytest.raises(ValueError):
+        moe.forward(xg, router_weight=wg, bias=bg, partial=True, comm=comm)
+    comm.check()
+    moe.check()
+    comm.close()
+
+
+@pytest.mark.parametrize("H", [1024, 6144, 7168])
+def test_peer_allreduce_norm_group_of_one(H):
+    """The combine + all-reduce with the decoder hop's residual + RMSNorm
+    epilogue (one cluster per token row): residual_out and norm_out bit-exact
+    the oracle's fold, across calls of changing token counts, with residual
+    updated in place, and without gamma."""
+    mm = _mm()
+    g = torch.Generator().manual_seed(H)
+    K, P, TMAX, EPS = 8, 96, 16, 1e-6
+    comm = mm.PeerAllReduce(TMAX, H, eps=EPS)
+    rows = torch.randn((P, H), generator=g).to(torch.bfloat16)
+    gamma = (1 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16)
+    rg, gg = rows.cuda(), gamma.cuda()
+    for T in (8, 3, 16, 1, 8):
+        shared = torch.randn((T, H), generator=g).to(torch.bfloat16)
+        w = torch.rand((T, K), generator=g)
+        perm = torch.randint(-1, P, (T, K), generator=g).int()
+        res = torch.randn((T, H), generator=g).to(torch.bfloat16)
+        y = O.finalize(O.bf16_bits(rows), w.numpy(), perm.numpy(), O.bf16_bits(shared))
+        want_r, want_n = O.allreduce_norm([y], O.bf16_bits(res), O.bf16_bits(gamma), EPS)
+        args = dict(routed_output=rg, expert_weights=w.cuda(), permuted_indices=perm.cuda(),
+                    gated_shared_output=shared.cuda())
+        norm, r_out = comm.moe_finalize_all_reduce_rms_norm(**args, residual=res.cuda(), gamma=gg)
+        assert np.array_equal(O.bf16_bits(r_out.cpu()), want_r), T
+        assert np.array_equal(O.bf16_bits(norm.cpu()), want_n), T
+        inplace = res.cuda()
+        none, r2 = comm.moe_finalize_all_reduce_rms_norm(**args, residual=inplace, gamma=None, residual_out=inplace)
+        assert none is None and r2.data_ptr() == inplace.data_ptr()
+        assert np.array_equal(O.bf16_bits(inplace.cpu()), want_r), T
+    comm.check()
+    comm.close()
+
+
+def test_forward_hop_group_of_one():
+    """forward(comm, residual, gamma): the whole step ending in the hop equals
+    forward() followed by the oracle's residual + RMSNorm of its output."""
+    mm = _mm()
+    H, I, E, K, T = 2048, 256, 64, 8, 8
+    layer = O.make_layer(H, I, E, shared=True, seed=29)
+    x, wr, bias = O.make_inputs(T, H, E, seed=29)
+    moe = to_gpu_layer(layer, K, 16)
+    comm = mm.PeerAllReduce(16, H, eps=1e-5)
+    g = torch.Generator().manual_seed(29)
+    res = torch.randn((T, H), generator=g).to(torch.bfloat16)
+    gamma = (1 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16)
+    xg, wg, bg = x.cuda(), wr.cuda(), bias.cuda()
+    bufs = {}
+    moe.forward(xg, router_weight=wg, bias=bg, routed_scaling_factor=2.5, buffers=bufs)
+    shared = moe.shared_rows(bufs["rows"], T)
+    y = O.finalize(O.bf16_bits(bufs["rows"].cpu()), bufs["weights"].cpu().numpy(), bufs["permuted"].cpu().numpy(),
+                   O.bf16_bits(shared.cpu()))
+    want_r, want_n = O.allreduce_norm([y], O.bf16_bits(res), O.bf16_bits(gamma), 1e-5)
+    norm, r_out = moe.forward(xg, router_weight=wg, bias=bg, routed_scaling_factor=2.5, comm=comm,
+                              residual=res.cuda(), gamma=gamma.cuda())
+    assert np.array_equal(O.bf16_bits(r_out.cpu()), want_r)
+    assert np.array_equal(O.bf16_bits(norm.cpu()), want_n)
+    with pytest.raises(ValueError):
+        moe.forward(xg, router_weight=wg, bias=bg, residual=res.cuda())
+    comm.check()
+    moe.check()
+    comm.close()
+
+
+# ----------------------------------------------------------------------------- stack
+def _stack_parts(n, H, I, E, K, T, seed, window=None):
+    g = torch.Generator().manual_seed(seed)
+    layers = [O.make_layer(H, I, E, shared=False, seed=seed + 1 + i) for i in range(n)]
+    routers = [(torch.randn((E, H), generator=g) * 0.02).to(torch.bfloat16) for _ in range(n)]
+    biases = [(torch.randn((E,), generator=g) * 0.01).float() for _ in range(n)]
+    gammas = [(1 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16) for _ in range(n)]
+    x = torch.randn((T, H), generator=g).to(torch.bfloat16)
+    res = torch.randn((T, H), generator=g).to(torch.bfloat16)
+    return layers, routers, biases, gammas, x, res
+
+
+def test_stack_matches_layer_loop_oracle_and_graph():
+    """mm_stack_forward over 3 layers equals the per-layer forward loop bit for
+    bit; each layer's ids and hop outputs equal the oracle's on the GPU's own
+    layer inputs; a CUDA-graph replay of the step equals eager."""
+    mm = _mm()
+    n, H, I, E, K, T = 3, 1024, 256, 32, 8, 8
+    layers, routers, biases, gammas, x, res = _stack_parts(n, H, I, E, K, T, seed=40)
+    moes = [to_gpu_layer(L, K, 16) for L in layers]
+    comm = mm.PeerAllReduce(16, H, eps=1e-6)
+    rg, bg, gg = [t.cuda() for t in routers], [t.cuda() for t in biases], [t.cuda() for t in gammas]
+    stack = mm.MoEStack(moes, rg, gg, comm, biases=bg, routed_scaling_factor=2.5)
+    xs, r_stack = x.cuda(), res.cuda()
+    out = stack.forward(xs, r_stack).clone()
+    # the loop, checked layer by layer against the oracle on its own inputs
+    cur, r = xs, res.cuda()
+    for i, m in enumerate(moes):
+        bufs = {}
+        norm, r_new = m.forward(cur, router_weight=rg[i], bias=bg[i], routed_scaling_factor=2.5, buffers=bufs,
+                                comm=comm, residual=r, gamma=gg[i])
+        ow, oids = O.gate_topk(O.router_gemv(O.bf16_bits(cur.cpu()), O.bf16_bits(routers[i])), biases[i].numpy(),
+                               K, scale=2.5)
+        assert np.array_equal(bufs["ids"].cpu().numpy(), oids), i
+        y = O.finalize(O.bf16_bits(bufs["rows"].cpu()), bufs["weights"].cpu().numpy(),
+                       bufs["permuted"].cpu().numpy(), None)
+        want_r, want_n = O.allreduce_norm([y], O.bf16_bits(r.cpu()), O.bf16_bits(gammas[i]), 1e-6)
+        assert np.array_equal(O.bf16_bits(r_new.cpu()), want_r), i
+        assert np.array_equal(O.bf16_bits(norm.cpu()), want_n), i
+        cur, r = norm.clone(), r_new.clone()
+    assert torch.equal(out, cur)
+    assert torch.equal(r_stack, r)
+    # graph replay of the whole step (residual restored before each replay)
+    r_graph = res.cuda()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        stack.forward(xs, r_graph)
+    for _ in range(3):
+        r_graph.copy_(res.cuda())
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(r_graph, r)
+        assert torch.equal(stack.norm[(n - 1) & 1][:T], out)
+    stack.check()
+    del graph
+    comm.close()

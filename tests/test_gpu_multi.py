@@ -1,8 +1,11 @@
-"""Two-GPU parity (NCCL): the layer split tensor-parallel on the intermediate, or
+"""Two-GPU parity: the layer split tensor-parallel on the intermediate, or
 expert-parallel by expert windows, over two ranks; each rank runs the chain on its
-part (forward(partial=True)), the fp32 partial sums meet in an NCCL all-reduce and
-finalize_partial rounds them. The result must match the fp32 oracle of the whole
-layer within BASELINE's bar. Skipped with fewer than two GPUs."""
+part. Two combines: (1) forward(partial=True), the fp32 partial sums meet in an
+NCCL all-reduce and finalize_partial rounds them; (2) forward(comm=PeerAllReduce),
+the combine fused with the all-reduce over NVLink peer memory, which must equal
+bit for bit the oracle's rank-order sum of every rank's combine of its own rows.
+Both must match the fp32 oracle of the whole layer within BASELINE's bar.
+Skipped with fewer than two GPUs."""
 
 import datetime
 import os
@@ -25,7 +28,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, mode, queue):
+def _worker(rank, world, port, mode, peer, queue):
     import sys
 
     repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -56,10 +59,48 @@ def _worker(rank, world, port, mode, queue):
             moe = megamoe.RoutedMoE(*(t.to(dev) for t in w), K, 16, router_experts=E, expert_offset=offset,
                                     shared=sh)
         bufs = {}
-        part = moe.forward(x.to(dev), router_weight=wr.to(dev), bias=bias.to(dev), routed_scaling_factor=2.5,
-                           partial=True, buffers=bufs)
-        dist.all_reduce(part)
-        out = megamoe.finalize_partial(part)
+        xg, wg, bg = x.to(dev), wr.to(dev), bias.to(dev)
+        exact = True
+        if not peer:
+            part = moe.forward(xg, router_weight=wg, bias=bg, routed_scaling_factor=2.5, partial=True, buffers=bufs)
+            dist.all_reduce(part)
+            out = megamoe.finalize_partial(part)
+        else:
+            comm = megamoe.PeerAllReduce(16, H)
+            for _ in range(3):
+                out = moe.forward(xg, router_weight=wg, bias=bg, routed_scaling_factor=2.5, buffers=bufs, comm=comm)
+            torch.cuda.synchronize()
+            shared = moe.shared_rows(bufs["rows"], T)
+            mine = (O.bf16_bits(bufs["rows"].cpu()), bufs["weights"].cpu().numpy(), bufs["permuted"].cpu().numpy(),
+                    None if shared is None else O.bf16_bits(shared.cpu()))
+            every = [None] * world
+            dist.all_gather_object(every, mine)
+            want = O.allreduce_ranks([O.finalize(*r) for r in every])
+            exact = bool(np.array_equal(O.bf16_bits(out.cpu()), want))
+            # the decoder hop: residual + RMSNorm of the group sum, same launch
+            gr = torch.Generator().manual_seed(31)
+            res = torch.randn((T, H), generator=gr).to(torch.bfloat16)
+            gamma = (1 + 0.1 * torch.randn(H, generator=gr)).to(torch.bfloat16)
+            want_r, want_n = O.allreduce_norm([O.finalize(*r) for r in every], O.bf16_bits(res),
+                                              O.bf16_bits(gamma), comm.eps)
+            norm, r_out = moe.forward(xg, router_weight=wg, bias=bg, routed_scaling_factor=2.5, buffers=bufs,
+                                      comm=comm, residual=res.to(dev), gamma=gamma.to(dev))
+            exact = exact and bool(np.array_equal(O.bf16_bits(r_out.cpu()), want_r))
+            exact = exact and bool(np.array_equal(O.bf16_bits(norm.cpu()), want_n))
+            out = moe.forward(xg, router_weight=wg, bias=bg, routed_scaling_factor=2.5, buffers=bufs, comm=comm)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                moe.forward(xg, router_weight=wg, bias=bg, routed_scaling_factor=2.5, buffers=bufs, comm=comm)
+            first = out.clone()
+            for _ in range(3):
+                bufs["out"].zero_()
+                graph.replay()
+                torch.cuda.synchronize()
+                exact = exact and torch.equal(bufs["out"], first)
+            comm.check()
+            del graph
+            dist.barrier()
+            comm.close()
         torch.cuda.synchronize()
         moe.check()
         if rank == 0:
@@ -67,26 +108,31 @@ def _worker(rank, world, port, mode, queue):
             ow, oids = O.gate_topk(logits, bias.numpy(), K, scale=2.5)
             same_ids = bool(np.array_equal(bufs["ids"].cpu().numpy(), oids))
             ref, _, _ = O.moe_layer(x, oids, ow, layer)
-            queue.put((same_ids, O.max_abs_rel(out.float().cpu().numpy(), ref.numpy())))
+            queue.put((same_ids, exact, O.max_abs_rel(out.float().cpu().numpy(), ref.numpy())))
         dist.barrier()
     finally:
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("peer", [False, True], ids=["nccl", "peer"])
 @pytest.mark.parametrize("mode", ["tp", "ep"])
-def test_two_gpu_partitions_match_the_oracle(mode):
+def test_two_gpu_partitions_match_the_oracle(mode, peer):
     from oracle import oracle as O
 
     O.build()
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, queue)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, peer, queue)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
         p.join(timeout=240)
+    for p in procs:
+        if p.exitcode is None:
+            p.kill()
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-    same_ids, err = queue.get(timeout=5)
+    same_ids, exact, err = queue.get(timeout=5)
     assert same_ids
+    assert exact
     assert err <= 2e-2, err

@@ -217,6 +217,53 @@ def test_finalize_known_answer():
     assert vals.tolist() == [[0.5 + 0.75 + 1.0, 1.0 - 1.0 + 1.0]]
 
 
+def test_allreduce_ranks_sums_in_rank_order():
+    def bf(a):
+        return O.bf16_bits(torch.tensor(a, dtype=torch.float32).to(torch.bfloat16))
+
+    big = 2.0 ** 30
+    # fp32 absorbs 1 into 2^30, so only the order (2^30, -2^30, 1) keeps it
+    assert O.bits_to_f32(O.allreduce_ranks([bf([big]), bf([1.0]), bf([-big])])).tolist() == [0.0]
+    assert O.bits_to_f32(O.allreduce_ranks([bf([big]), bf([-big]), bf([1.0])])).tolist() == [1.0]
+    # the fp32 sum is rounded to bf16 once, at the end (nearest even)
+    ys = [bf([1.0]), bf([2.0 ** -8]), bf([2.0 ** -9])]
+    assert O.bits_to_f32(O.allreduce_ranks(ys)).tolist() == [1.0 + 2.0 ** -7]
+    one = O.allreduce_ranks([bf([[1.5, -2.0], [0.0, 3.0]])])
+    assert np.array_equal(one, bf([[1.5, -2.0], [0.0, 3.0]]))
+
+
+def test_allreduce_norm_known_answers():
+    def bf(a):
+        return O.bf16_bits(torch.tensor(a, dtype=torch.float32).to(torch.bfloat16))
+
+    H = 7168
+    gamma = bf(np.linspace(-2, 2, H, dtype=np.float32))
+    # every pre value 2: sum of squares 4 H, inv = 1 / sqrt(4) = 1/2, norm = gamma
+    res_out, norm = O.allreduce_norm([bf(np.zeros((2, H), np.float32))], bf(np.full((2, H), 2.0, np.float32)),
+                                     gamma, 0.0)
+    assert np.array_equal(res_out, bf(np.full((2, H), 2.0, np.float32)))
+    assert np.array_equal(norm, np.stack([gamma, gamma]))
+    # two ranks + residual: pre is one rounding of the fp32 sum (1 + 2^-8 + 2^-9 -> 1 + 2^-7)
+    y0, y1 = bf(np.full((1, H), 1.0, np.float32)), bf(np.full((1, H), 2.0 ** -8, np.float32))
+    res_out, none = O.allreduce_norm([y0, y1], bf(np.full((1, H), 2.0 ** -9, np.float32)), None, 1e-6)
+    assert none is None
+    assert np.all(O.bits_to_f32(res_out) == 1.0 + 2.0 ** -7)
+
+
+def test_allreduce_norm_matches_float64():
+    g = torch.Generator().manual_seed(4)
+    for H in (1024, 6144, 7168):
+        ys = [O.bf16_bits(torch.randn(5, H, generator=g).to(torch.bfloat16)) for _ in range(3)]
+        res = O.bf16_bits(torch.randn(5, H, generator=g).to(torch.bfloat16))
+        gam = O.bf16_bits((1 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16))
+        r, n = O.allreduce_norm(ys, res, gam, 1e-6)
+        pre = sum(O.bits_to_f32(y).astype(np.float64) for y in ys) + O.bits_to_f32(res)
+        assert np.abs(O.bits_to_f32(r) - pre).max() <= 2.0 ** -8 * np.abs(pre).max()
+        p = O.bits_to_f32(r).astype(np.float64)
+        ref = p / np.sqrt((p * p).mean(1, keepdims=True) + 1e-6) * O.bits_to_f32(gam)
+        assert np.abs(O.bits_to_f32(n) - ref).max() <= 2.0 ** -7 * np.abs(ref).max()
+
+
 def test_moe_layer_oracle_shapes_and_linearity():
     H, I, E, K, T = 256, 256, 4, 2, 3
     layer = O.make_layer(H, I, E, shared=True, seed=1)
