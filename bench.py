@@ -57,6 +57,9 @@ def parse_args():
     ap.add_argument("--combine", choices=["peer", "nccl"], default="peer",
                     help="N > 1: fused combine + peer all-reduce (default) or NCCL all-reduce of fp32 partials")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--stack", action="store_true",
+                    help="BASELINE config 5: a step of --layers EP8 MoE layers chained through the fused hop")
+    ap.add_argument("--layers", type=int, default=60)
     return ap.parse_args()
 
 
@@ -344,6 +347,204 @@ def run_mm(args):
         dist.destroy_process_group()
 
 
+# --------------------------------------------------------------------------- config 5
+def run_stack(args):
+    """a step of `layers` routed-MoE layers (hidden 7168, 384
+    experts, top-8, intermediate 2048, MXFP4, no shared expert) at EP8: rank r
+    holds the EP8 window r (48 experts per layer per GPU); routing is replicated;
+    each layer's combine is all-reduced over the ranks and followed by the
+    residual + RMSNorm hop in the same launch, whose output is the next layer's
+    input (bf16 residual stream carried through the step). With fewer than 8
+    ranks each rank still holds one EP8 window, so its per-layer work is that of
+    an EP8 rank (routes to absent windows are skipped)."""
+    import megamoe
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    ep = 8
+    if world > ep:
+        raise SystemExit("--stack runs at most 8 ranks (EP8)")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    T, L = args.tokens, args.layers
+    per = E // ep
+    offset = rank * per
+    moes, routers, biases, gammas = [], [], [], []
+    for layer in range(L):
+        g = torch.Generator(device=dev).manual_seed(1000 + 97 * layer + rank)
+
+        def rnd(shape, lo, hi):
+            return torch.randint(lo, hi + 1, shape, dtype=torch.uint8, device=dev, generator=g)
+
+        w = [rnd((per, 2 * I, H // 2), 0, 255), rnd((per, 2 * I, H // 32), 117, 121),
+             rnd((per, H, I // 2), 0, 255), rnd((per, H, I // 32), 117, 121)]
+        moes.append(megamoe.RoutedMoE(*w, K, max(T, 8), router_experts=E, expert_offset=offset))
+        gx = torch.Generator(device=dev).manual_seed(7 + layer)  # replicated on every rank
+        routers.append((torch.randn((E, H), device=dev, generator=gx) * 0.02).to(torch.bfloat16))
+        biases.append((torch.randn((E,), device=dev, generator=gx) * 0.01).float())
+        gammas.append((1 + 0.1 * torch.randn((H,), device=dev, generator=gx)).to(torch.bfloat16))
+    comm = megamoe.PeerAllReduce(max(T, 8), H)
+    stack = megamoe.MoEStack(moes, routers, gammas, comm, biases=biases, routed_scaling_factor=SCALE)
+    gx = torch.Generator(device=dev).manual_seed(5)
+    xs = torch.randn((POOL, T, H), device=dev, generator=gx).to(torch.bfloat16)
+    res_pool = torch.randn((POOL, T, H), device=dev, generator=gx).to(torch.bfloat16)
+    residual = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+
+    def step(i, x=None):
+        residual.copy_(res_pool[i % POOL])
+        return stack.forward(xs[i % POOL] if x is None else x, residual)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if dist is None:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    stack.check()
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record()
+        for i in range(args.steps):
+            step(i)
+        end.record()
+        torch.cuda.synchronize()
+    ms = max_over_ranks(start.elapsed_time(end))
+    barrier()
+    stack.check()
+    ms_step = ms / args.steps
+    value = T * args.steps / (ms / 1e3)
+
+    # local distinct experts per layer (layer by layer through the same hop, 4 pool entries)
+    d_local = []
+    for i in range(4):
+        cur = xs[i]
+        residual.copy_(res_pool[i])
+        for li, m in enumerate(moes):
+            bufs = {}
+            cur, _ = m.forward(cur, router_weight=routers[li], bias=biases[li], routed_scaling_factor=SCALE,
+                               buffers=bufs, comm=comm, residual=residual, gamma=gammas[li])
+            ids = bufs["ids"]
+            d_local.append(int(torch.unique(ids[(ids >= offset) & (ids < offset + per)]).numel()))
+            residual.copy_(bufs["residual_out"])
+    torch.cuda.synchronize()
+    stack.check()
+    eb = expert_bytes(H, I)
+    d_mean = float(np.mean(d_local))
+    step_bytes = L * (d_mean * eb + E * H * 2)
+    step_bytes_max = max_over_ranks(step_bytes)
+
+    # the dominant kernel alone: layer 0's expert kernel relaunched on its last tables
+    bufs = {}
+    moes[0].forward(xs[0], router_weight=routers[0], bias=biases[0], routed_scaling_factor=SCALE, buffers=bufs,
+                    comm=comm, residual=residual, gamma=gammas[0])
+    ids = bufs["ids"]
+    k_d = int(torch.unique(ids[(ids >= offset) & (ids < offset + per)]).numel())
+    reps = 200
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    for a, b in evs:
+        a.record()
+        moes[0].rerun_experts(T, bufs["record"], bufs["rows"])
+        b.record()
+    torch.cuda.synchronize()
+    k_ms = float(np.mean([a.elapsed_time(b) for a, b in evs]))
+    stack.check()
+    peak, peak_kind = peaks()
+    k_bytes = k_d * eb
+    achieved = k_bytes / (k_ms / 1e3) / 1e9 if k_d else 0.0
+
+    # end to end: the step's x and residual from pinned host memory, output read back
+    host_x = torch.empty((POOL, T, H), dtype=torch.bfloat16).pin_memory()
+    host_x.copy_(xs.cpu())
+    host_r = torch.empty((POOL, T, H), dtype=torch.bfloat16).pin_memory()
+    host_r.copy_(res_pool.cpu())
+    host_out = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
+    xdev = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    e2e_steps = min(args.steps, 200)
+    barrier()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for i in range(e2e_steps):
+        xdev.copy_(host_x[i % POOL], non_blocking=True)
+        residual.copy_(host_r[i % POOL], non_blocking=True)
+        out = stack.forward(xdev, residual)
+        host_out.copy_(out, non_blocking=True)
+    e2.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(s2.elapsed_time(e2))
+    stack.check()
+
+    line = {
+        "metric": f"{L}-layer routed-MoE stack tokens/s per step (us/layer = 1e3 * ms_per_step / {L})",
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_step,
+        "us_per_layer": ms_step * 1e3 / L,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "mxfp4 weights x mxfp4(3-term) activations, fp32 accumulate",
+        "data": "synthetic (seeded random MXFP4 weights, bf16 x and residual ~ N(0,1))",
+        "config": {
+            "workload": f"BASELINE config 5: {L} routed-MoE layers, hidden {H}, {E} experts (EP8: {per} per GPU, "
+                        f"window {rank}), intermediate {I}, sigmoid+bias top-{K}, scale {SCALE}, MXFP4, "
+                        f"{T} tokens, bf16 residual + RMSNorm hop between layers",
+            "tokens": T,
+            "layers": L,
+            "parallelism": f"ep8 windows on {world} GPU(s)",
+            "l2": f"inputs larger than L2 (~{step_bytes / 1e9:.1f} GB of expert weights per step)",
+            "launch": "one mm_stack_forward call per step (eager, PDL-chained across layers)",
+            "local_distinct_experts_per_layer": d_mean,
+            "step_weight_bytes_max_rank": step_bytes_max,
+            "step_roofline_frac": (step_bytes_max / (ms_step / 1e3) / 1e9) / peak,
+        },
+        "roofline": {
+            "bound": "hbm",
+            "kernel": "mm::expert_kernel (layer 0)",
+            "achieved": achieved,
+            "peak": peak,
+            "peak_kind": peak_kind,
+            "unit": "GB/s",
+            "frac": achieved / peak,
+            "traffic": None,
+            "algorithmic_bytes_per_launch": k_bytes,
+            "launch_ms": k_ms,
+        },
+        "e2e": {"value": T * e2e_steps / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": 2 * T * H * 2,
+                "d2h_bytes_per_step": T * H * 2, "steps": e2e_steps},
+        "gpu_launches": args.steps * L * 4,
+        "clocks": clocks.summary(),
+        "cpu_baseline": None,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        comm.close()
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 # --------------------------------------------------------------------------- CPU legs
 def _cpu_layer_step(x_bf16, router_bf16, bias, experts_w, shared_w, oracle):
     logits = oracle.router_gemv(oracle.bf16_bits(x_bf16), oracle.bf16_bits(router_bf16))
@@ -460,6 +661,8 @@ def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.stack:
+        run_stack(args)
     else:
         run_mm(args)
 

@@ -136,3 +136,80 @@ def test_two_gpu_partitions_match_the_oracle(mode, peer):
     assert same_ids
     assert exact
     assert err <= 2e-2, err
+
+
+def _stack_worker(rank, world, port, queue):
+    import sys
+
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [repo, os.path.join(repo, "sgl-nvidia-mega_b200")]
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        import megamoe
+        from megamoe import shard
+        from oracle import oracle as O
+
+        n, H, I, E, K, T = 3, 1024, 256, 32, 8, 8
+        g = torch.Generator().manual_seed(50)
+        offset, local = shard.ep_window(E, rank, world)
+        moes, routers, biases, gammas = [], [], [], []
+        for i in range(n):
+            L = O.make_layer(H, I, E, shared=False, seed=51 + i)
+            w = shard.ep_slice([L["w13"], L["w13_scale"], L["w2"], L["w2_scale"]], rank, world)
+            moes.append(megamoe.RoutedMoE(*(t.to(dev) for t in w), K, 16, router_experts=E, expert_offset=offset))
+            routers.append(((torch.randn((E, H), generator=g) * 0.02).to(torch.bfloat16)).to(dev))
+            biases.append(((torch.randn((E,), generator=g) * 0.01).float()).to(dev))
+            gammas.append(((1 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16)).to(dev))
+        x = torch.randn((T, H), generator=g).to(torch.bfloat16).to(dev)
+        res0 = torch.randn((T, H), generator=g).to(torch.bfloat16).to(dev)
+        comm = megamoe.PeerAllReduce(16, H)
+        stack = megamoe.MoEStack(moes, routers, gammas, comm, biases=biases, routed_scaling_factor=2.5)
+        r = res0.clone()
+        out = stack.forward(x, r).clone()
+        cur, rl = x, res0.clone()
+        for i, m in enumerate(moes):
+            cur, rl = m.forward(cur, router_weight=routers[i], bias=biases[i], routed_scaling_factor=2.5,
+                                buffers={}, comm=comm, residual=rl, gamma=gammas[i])
+            cur, rl = cur.clone(), rl.clone()
+        torch.cuda.synchronize()
+        stack.check()
+        same_loop = bool(torch.equal(out, cur) and torch.equal(r, rl))
+        every = [None] * world
+        dist.all_gather_object(every, (O.bf16_bits(out.cpu()), O.bf16_bits(r.cpu())))
+        same_ranks = all(np.array_equal(e[0], every[0][0]) and np.array_equal(e[1], every[0][1]) for e in every)
+        finite = bool(torch.isfinite(out.float()).all())
+        if rank == 0:
+            queue.put((same_loop, same_ranks, finite))
+        dist.barrier()
+        comm.close()
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gpu_expert_parallel_stack():
+    """Three MoE layers, EP2, chained through the fused hop: every rank's output
+    and residual equal its own per-layer loop and are identical across ranks."""
+    from oracle import oracle as O
+
+    O.build()
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_stack_worker, args=(r, 2, port, queue)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    for p in procs:
+        if p.exitcode is None:
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    same_loop, same_ranks, finite = queue.get(timeout=5)
+    assert same_loop and same_ranks and finite
