@@ -6,10 +6,11 @@
 // shared expert's tokens form segments too). A gate_up unit streams one 128-row
 // tile of w13 (64 gate rows + the 64 matching up rows) through all of H and
 // multiplies it with the segment's rows; a down unit streams one 128-row tile of
-// w2 through all of I. Units are claimed from a global counter in the order
-// [all gate_up units][all down units], so every gate_up unit is claimed before
-// any down unit; a down unit's activations wait on its segment's mailbox (the
-// number of finished gate_up warps), while its weights stream before that wait.
+// w2 through all of I. Units are numbered [all gate_up units][all down units];
+// CTA b runs unit b first and then claims units from a global counter, so
+// every gate_up unit is taken before any later down unit; a down unit's
+// activations wait on its segment's mailbox (the number of finished gate_up
+// warps), while its weights stream before that wait.
 // Reference semantics: gemm1.cu:6-7 (h = MX(clamped SwiGLU(x W13^T))),
 // gemm2.cu:6-7 (rows = h W2^T in bf16, deferred-finalize rows).
 //
@@ -174,13 +175,19 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
       const int total = p.ctrl[kCtrlUnits];
       const uint64_t policy = policy_evict_first();
       uint32_t stage = 0, phase = 0, ws = 0, wphase = 0;
-      int next = atomicAdd(&p.ctrl[kCtrlClaim], 1);
+      // CTA b's first unit is unit b, unclaimed: the first wave gives every CTA
+      // exactly one unit (with claims, a CTA could take two long gate_up units
+      // while another took two short down units). Later units come from the
+      // counter, offset by the grid, and are claimed three stages before the
+      // current unit's last load: the claim's round trip hides behind the
+      // stages in flight, and a CTA takes a unit only when it is about to run it.
+      int next = static_cast<int>(blockIdx.x);
       bool ok = true;
 #pragma unroll 1
       while (ok) {
         const int u = next;
         const bool have = u < total;
-        if (have) next = atomicAdd(&p.ctrl[kCtrlClaim], 1);  // claim ahead
+        next = total;
         if (!mbar_wait(bar(kBarWorkEmpty + ws), wphase ^ 1u, err, kErrTimeoutWork)) break;
         work_ids[ws] = have ? u : -1;
         mbar_arrive(bar(kBarWorkFull + ws));
@@ -196,8 +203,10 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
         const int ks_n = g2 ? p.ks2 : p.ks1;
         const uint8_t *sfa = g2 ? (sh ? p.ssfa2 : p.sfa2) : (sh ? p.ssfa13 : p.sfa13);
         sfa += (static_cast<size_t>(e) * (g2 ? p.m2 : p.m1) + m) * static_cast<size_t>(ks_n) * 1024u;
+        const int claim_at = ks_n > 3 ? ks_n - 3 : 0;
 #pragma unroll 1
         for (int ks = 0; ks < ks_n; ++ks) {
+          if (ks == claim_at) next = static_cast<int>(gridDim.x) + atomicAdd(&p.ctrl[kCtrlClaim], 1);
           if (!mbar_wait(bar(kBarEmpty + stage), phase ^ 1u, err, kErrTimeoutEmpty)) {
             ok = false;
             break;
