@@ -56,19 +56,27 @@ extern "C" {
 
 /* ---- expert weight formats ---------------------------------------------- */
 #define MM_WEIGHT_MXFP4 0 /* E2M1 codes + one E8M0 scale per 32 along K      */
+#define MM_WEIGHT_NVFP4 1 /* E2M1 codes + one E4M3 scale per 16 along K and
+                             an fp32 second-level scale per expert (ModelOpt
+                             NVFP4; glm5_3/sm103/moe/api.py:39-53)            */
 
 /* One group of experts in the canonical layout (SGLang FusedMoE w13/w2):
  *   w13       u8 [n, 2*I, H/2]  E2M1 pairs, low nibble = even element;
  *                               rows [0, I) are gate (w1), rows [I, 2I) up (w3)
  *   w13_scale u8 [n, 2*I, H/32] E8M0 (value 2^(byte-127)) per 32 elements
+ *             (NVFP4: [n, 2*I, H/16] E4M3 per 16 elements)
  *   w2        u8 [n, H, I/2]
- *   w2_scale  u8 [n, H, I/32]
+ *   w2_scale  u8 [n, H, I/32]   (NVFP4: [n, H, I/16] E4M3)
+ *   w13_scale_2, w2_scale_2     NVFP4 only: fp32 [n] per-expert second-level
+ *             scales (weight = e2m1 * e4m3 * scale_2); NULL for MXFP4
  * w13 and w2 must be 16-byte aligned (TMA tensor maps). */
 typedef struct mm_expert_weights {
   const void *w13;
   const void *w13_scale;
   const void *w2;
   const void *w2_scale;
+  const float *w13_scale_2;
+  const float *w2_scale_2;
 } mm_expert_weights;
 
 typedef struct mm_layer_desc {
@@ -79,16 +87,21 @@ typedef struct mm_layer_desc {
   int32_t expert_offset;  /* router id of local expert 0 (expert parallelism)      */
   int32_t top_k;          /* 1..16                                                 */
   int32_t max_tokens;     /* largest T a call may pass: 1..256                     */
-  int32_t weight_format;  /* MM_WEIGHT_MXFP4                                       */
-  int32_t act_terms;      /* MXFP4 terms carrying each activation into the GEMMs:
-                             x ~ t0 + t1 + t2, t_i the MXFP4 quantization of the
-                             residual of the earlier terms. 1..3; 3 is the default
-                             numerics (about 1e-3 relative), 1 is plain MXFP4.      */
+  int32_t weight_format;  /* MM_WEIGHT_MXFP4 or MM_WEIGHT_NVFP4                   */
+  int32_t act_terms;      /* FP4 terms carrying each activation into the GEMMs (in
+                             the weights' format): x ~ t0 + t1 + t2, t_i the FP4
+                             quantization of the residual of the earlier terms.
+                             1..3; 3 is the default numerics (about 1e-3 relative),
+                             1 is plain MXFP4 / NVFP4.                              */
   int32_t device;         /* CUDA device ordinal the weights live on               */
   mm_expert_weights routed; /* n = experts                                         */
   mm_expert_weights shared; /* n = 1; shared.w13 == NULL: no shared expert          */
   const float *clamp;       /* [experts] SwiGLU clamp limit or NULL (no clamp)      */
   const float *shared_clamp;/* [1] or NULL                                          */
+  float input_scale[2];     /* NVFP4: the static input scales of the gate_up and
+                               down GEMMs (activation = e2m1 * e4m3 * input_scale;
+                               the reference's FC1 / FC2 input scales, gs = 1 /
+                               input_scale); ignored for MXFP4                     */
 } mm_layer_desc;
 
 typedef struct mm_layer mm_layer; /* opaque handle */

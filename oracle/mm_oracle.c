@@ -439,3 +439,35 @@ void or_allreduce_norm(const uint16_t *y, const uint16_t *residual, const uint16
   }
   free(pre);
 }
+
+/* ---------------------------------------------------------------------------
+ * NVFP4 terms (E2M1 codes, an E4M3 scale per 16 under a global scale gs; the
+ * reference's rule glm5_3/sm103/primitives/ptx_tc.py:320-337 written with IEEE
+ * operations): per block of 16, term t quantizes the residual r left by the
+ * earlier terms: sf = e4m3(gs * (amax(|r|) * fp32(1/6))) RN saturating, the
+ * multiplier f = gs / value(sf) (0 when sf is 0), codes e2m1(r * f) RN
+ * saturating, r -= (e2m1 * value(sf)) * inv_gs. q: [terms][nblocks * 8] bytes
+ * (element 2j in the low nibble), s: [terms][nblocks].
+ * ------------------------------------------------------------------------- */
+uint8_t or_nv4_scale_code(float amax, float gs) { return or_e4m3(gs * (amax * 0x1.555556p-3f)); }
+
+void or_nvfp4_quant(const float *v, int nblocks, int terms, float gs, float inv_gs, uint8_t *q, uint8_t *s) {
+  for (int b = 0; b < nblocks; ++b) {
+    float r[16];
+    for (int i = 0; i < 16; ++i) r[i] = v[(size_t)b * 16 + i];
+    for (int t = 0; t < terms; ++t) {
+      float amax = 0.0f;
+      for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(r[i]));
+      const uint8_t c = or_nv4_scale_code(amax, gs);
+      const float sv = or_e4m3_value(c);
+      const float f = sv == 0.0f ? 0.0f : gs / sv;
+      for (int i = 0; i < 16; i += 2) {
+        const uint8_t lo = or_e2m1(r[i] * f), hi = or_e2m1(r[i + 1] * f);
+        q[(size_t)t * nblocks * 8 + (size_t)b * 8 + i / 2] = (uint8_t)(lo | (hi << 4));
+        r[i] = r[i] - (or_e2m1_value(lo) * sv) * inv_gs;
+        r[i + 1] = r[i + 1] - (or_e2m1_value(hi) * sv) * inv_gs;
+      }
+      s[(size_t)t * nblocks + b] = c;
+    }
+  }
+}

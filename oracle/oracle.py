@@ -59,6 +59,8 @@ def lib() -> ctypes.CDLL:
         h.or_sigmoid.argtypes = [c_float]
         h.or_e4m3.restype = c_uint8
         h.or_e4m3.argtypes = [c_float]
+        h.or_nv4_scale_code.restype = c_uint8
+        h.or_nv4_scale_code.argtypes = [c_float, c_float]
         h.or_route_words.restype = c_int
         h.or_gate_topk.argtypes = [c_void_p, c_void_p, c_int, c_int, c_int, c_float, c_float, c_int, c_int, c_int,
                                    c_void_p, c_void_p]
@@ -171,11 +173,60 @@ def fp4_dequant(q: np.ndarray, s: np.ndarray) -> np.ndarray:
     return out.sum(axis=0)
 
 
-def act_roundtrip(v: np.ndarray, terms: int = 3) -> np.ndarray:
+def act_roundtrip(v: np.ndarray, terms: int = 3, fmt: str = "mxfp4", input_scale: float = 1.0) -> np.ndarray:
     """The value the kernels multiply in place of activation v: the sum of its
-    MXFP4 terms."""
+    MXFP4 terms, or of its NVFP4 terms under the static input scale."""
+    if fmt == "nvfp4":
+        q, s = nvfp4_quant(v, terms, input_scale)
+        return nvfp4_dequant(q, s, input_scale)
     q, s = fp4_quant(v, terms)
     return fp4_dequant(q, s).astype(np.float32)
+
+
+_E4M3_LUT = None
+
+
+def e4m3_lut() -> np.ndarray:
+    """fp32 value of every E4M3 byte (exact decode)."""
+    global _E4M3_LUT
+    if _E4M3_LUT is None:
+        _E4M3_LUT = e4m3_table()
+    return _E4M3_LUT
+
+
+def nvfp4_quant(v: np.ndarray, terms: int, input_scale: float):
+    """fp32 [..., K] -> (codes u8 [terms, ..., K/2], E4M3 scales u8 [terms, ..., K/16]):
+    the kernels' NVFP4 activation terms under global scale gs = 1 / input_scale."""
+    v = np.ascontiguousarray(v, dtype=np.float32)
+    nb = v.size // 16
+    q = np.zeros((terms, nb * 8), dtype=np.uint8)
+    s = np.zeros((terms, nb), dtype=np.uint8)
+    gs = np.float32(1.0) / np.float32(input_scale)
+    lib().or_nvfp4_quant(_p(v), nb, terms, c_float(gs), c_float(input_scale), _p(q), _p(s))
+    lead = v.shape[:-1]
+    return q.reshape(terms, *lead, v.shape[-1] // 2), s.reshape(terms, *lead, v.shape[-1] // 16)
+
+
+def nvfp4_dequant(q: np.ndarray, s: np.ndarray, input_scale: float) -> np.ndarray:
+    """Sum over terms of e2m1 * e4m3 * input_scale (float64, returned as fp32)."""
+    lo = E2M1[q & 0x0F].astype(np.float64)
+    hi = E2M1[q >> 4].astype(np.float64)
+    vals = np.stack([lo, hi], axis=-1).reshape(*q.shape[:-1], q.shape[-1] * 2)
+    sc = e4m3_lut()[s].astype(np.float64)
+    out = (vals.reshape(*s.shape, 16) * sc[..., None]).reshape(vals.shape)
+    return (out.sum(axis=0) * float(input_scale)).astype(np.float32)
+
+
+def dequant_nvfp4(codes: torch.Tensor, scales: torch.Tensor, scale_2: float) -> torch.Tensor:
+    """u8 [..., K/2] codes + u8 [..., K/16] E4M3 + fp32 second-level scale ->
+    fp32 [..., K] (ModelOpt NVFP4: w = e2m1 * e4m3 * scale_2)."""
+    lut = torch.from_numpy(E2M1)
+    lo = lut[(codes & 0x0F).long()]
+    hi = lut[(codes >> 4).long()]
+    vals = torch.stack([lo, hi], dim=-1).reshape(*codes.shape[:-1], codes.shape[-1] * 2).double()
+    sc = torch.from_numpy(e4m3_lut())[scales.long()].double()
+    out = (vals.reshape(*scales.shape, 16) * sc[..., None]).reshape(vals.shape) * float(scale_2)
+    return out.float()
 
 
 def finalize(rows_bf16: np.ndarray, weights: np.ndarray, permuted: np.ndarray,
@@ -239,13 +290,15 @@ def dequant_mxfp4(codes: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
 
 
 def expert_mlp(x: torch.Tensor, w13: torch.Tensor, s13: torch.Tensor, w2: torch.Tensor, s2: torch.Tensor,
-               clamp: Optional[float], numerics: str, terms: int = 3) -> torch.Tensor:
-    """fp32 [n, H] of one expert on fp32 rows x [n, H] (CPU)."""
+               clamp: Optional[float], numerics: str, terms: int = 3, nv: Optional[tuple] = None) -> torch.Tensor:
+    """fp32 [n, H] of one expert on fp32 rows x [n, H] (CPU). ``nv`` = (w13
+    scale_2, w2 scale_2, (fc1 input scale, fc2 input scale)) for NVFP4 weights."""
     inter = w13.shape[0] // 2
-    W13 = dequant_mxfp4(w13, s13)
+    fmt = "nvfp4" if nv is not None else "mxfp4"
+    W13 = dequant_nvfp4(w13, s13, nv[0]) if nv is not None else dequant_mxfp4(w13, s13)
     xin = x
     if numerics == "kernel":
-        xin = torch.from_numpy(act_roundtrip(x.numpy(), terms))
+        xin = torch.from_numpy(act_roundtrip(x.numpy(), terms, fmt, nv[2][0] if nv is not None else 1.0))
     gu = xin @ W13.T
     gate, up = gu[:, :inter], gu[:, inter:]
     if clamp is not None:
@@ -253,8 +306,8 @@ def expert_mlp(x: torch.Tensor, w13: torch.Tensor, s13: torch.Tensor, w2: torch.
         gate = gate.clamp(max=clamp)
     h = up * (gate * torch.sigmoid(gate))
     if numerics == "kernel":
-        h = torch.from_numpy(act_roundtrip(h.numpy(), terms))
-    W2 = dequant_mxfp4(w2, s2)
+        h = torch.from_numpy(act_roundtrip(h.numpy(), terms, fmt, nv[2][1] if nv is not None else 1.0))
+    W2 = dequant_nvfp4(w2, s2, nv[1]) if nv is not None else dequant_mxfp4(w2, s2)
     return h @ W2.T
 
 
@@ -275,17 +328,25 @@ def moe_layer(x_bf16: torch.Tensor, ids: np.ndarray, weights: np.ndarray, layer:
             e = int(ids[t, k]) - expert_offset
             if 0 <= e < E:
                 by_expert.setdefault(e, []).append((t, k))
+    nvl = layer.get("fmt") == "nvfp4"
+    ins = layer.get("input_scale")
+
+    def nv_of(sc13, sc2, e):
+        return (float(sc13[e]), float(sc2[e]), ins) if nvl else None
+
     for e, slots in sorted(by_expert.items()):
         toks = torch.tensor([t for t, _ in slots])
         lim = None if clamp is None else float(clamp[e])
-        y = expert_mlp(x[toks], w13[e], s13[e], w2[e], s2[e], lim, numerics, terms)
+        y = expert_mlp(x[toks], w13[e], s13[e], w2[e], s2[e], lim, numerics, terms,
+                       nv_of(layer.get("w13_scale_2"), layer.get("w2_scale_2"), e))
         for j, slot in enumerate(slots):
             rows[slot] = y[j]
     shared = None
     if layer.get("shared") is not None:
         sw = layer["shared"]
         lim = layer.get("shared_clamp")
-        shared = expert_mlp(x, sw[0][0], sw[1][0], sw[2][0], sw[3][0], lim, numerics, terms)
+        shared = expert_mlp(x, sw[0][0], sw[1][0], sw[2][0], sw[3][0], lim, numerics, terms,
+                            nv_of(sw[4], sw[5], 0) if nvl else None)
     out = torch.zeros_like(x)
     for (t, k), y in rows.items():
         out[t] += float(weights[t, k]) * y
@@ -315,6 +376,46 @@ def make_layer(H: int, I: int, E: int, *, shared: bool, seed: int, scale_lo: int
     if shared:
         layer["shared"] = (rnd((1, 2 * I, H // 2), 0, 255), rnd((1, 2 * I, H // 32), scale_lo, scale_hi),
                            rnd((1, H, I // 2), 0, 255), rnd((1, H, I // 32), scale_lo, scale_hi))
+    return layer
+
+
+def make_nvfp4_layer(H: int, I: int, E: int, *, shared: bool, seed: int, sf_lo: float = 0.5, sf_hi: float = 4.0,
+                     clamp: Optional[float] = None) -> dict:
+    """Seeded NVFP4 layer (canonical ModelOpt layout): E2M1 codes uniform over
+    the 16 nibbles, E4M3 scales of values ~U[sf_lo, sf_hi] per 16 elements, a
+    per-expert fp32 scale_2 of 2^-8 (1 + u/4), u ~ U[0, 1); the static input
+    scales are calibrated on a sample: FC1 for |x| <= 8, FC2 for twice the
+    largest |h| of 8 rows of x ~ N(0, 1) through expert 0."""
+    g = torch.Generator().manual_seed(seed)
+
+    def rnd(shape):
+        return torch.randint(0, 256, shape, dtype=torch.uint8, generator=g)
+
+    def sf(shape):
+        v = sf_lo + (sf_hi - sf_lo) * torch.rand(shape, generator=g)
+        return v.to(torch.float8_e4m3fn).view(torch.uint8)
+
+    def s2(n):
+        return (2.0 ** -8 * (1.0 + 0.25 * torch.rand((n,), generator=g))).float()
+
+    layer = {
+        "fmt": "nvfp4",
+        "w13": rnd((E, 2 * I, H // 2)), "w13_scale": sf((E, 2 * I, H // 16)),
+        "w2": rnd((E, H, I // 2)), "w2_scale": sf((E, H, I // 16)),
+        "w13_scale_2": s2(E), "w2_scale_2": s2(E),
+        "clamp": None if clamp is None else torch.full((E,), float(clamp)),
+        "shared": None,
+    }
+    if shared:
+        layer["shared"] = (rnd((1, 2 * I, H // 2)), sf((1, 2 * I, H // 16)), rnd((1, H, I // 2)),
+                           sf((1, H, I // 16)), s2(1), s2(1))
+    fc1 = 8.0 / (6.0 * 448.0)
+    xs = torch.randn((8, H), generator=g)
+    W13 = dequant_nvfp4(layer["w13"][0], layer["w13_scale"][0], float(layer["w13_scale_2"][0]))
+    gu = xs @ W13.T
+    h = gu[:, I:] * (gu[:, :I] * torch.sigmoid(gu[:, :I]))
+    fc2 = 2.0 * float(h.abs().max()) / (6.0 * 448.0)
+    layer["input_scale"] = (float(np.float32(fc1)), float(np.float32(fc2)))
     return layer
 
 

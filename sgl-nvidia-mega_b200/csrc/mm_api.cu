@@ -119,7 +119,12 @@ struct mm_layer {
   int max_ctas, rows_cap, shared_row_base, route_words_max, max_segs;
   int has_shared;
   int num_sms;
+  int fmt;        // kFmtMx or kFmtNv
+  int block;      // elements per weight / activation scale: 32 or 16
+  int sf_stage;   // scale-chunk bytes of one pipeline stage (Fmt<fmt>::kSfStageBytes)
+  float gs1 = 1.0f, gs2 = 1.0f;  // NVFP4: 1 / input_scale[0], 1 / input_scale[1]
   uint8_t *sfa13 = nullptr, *sfa2 = nullptr, *ssfa13 = nullptr, *ssfa2 = nullptr;
+  float *alpha = nullptr;  // NVFP4: [alpha13 E][alpha2 E][shared alpha13][shared alpha2]
   uint8_t *xq = nullptr, *xs = nullptr, *hq = nullptr, *hs = nullptr;
   int4 *segs = nullptr;
   int *ctrl = nullptr, *flags = nullptr;
@@ -245,14 +250,16 @@ int mm_finalize_partial(const float *partial, uint16_t *out, int32_t tokens, int
 static void free_layer(mm_layer *L) {
   if (!L) return;
   void *ptrs[] = {L->sfa13, L->sfa2, L->ssfa13, L->ssfa2, L->xq, L->xs, L->hq, L->hs, L->segs,
-                  L->ctrl, L->flags, L->err, L->logits, L->weights, L->ids, L->permuted, L->record};
+                  L->ctrl, L->flags, L->err, L->logits, L->weights, L->ids, L->permuted, L->record, L->alpha};
   for (void *p : ptrs)
     if (p) cudaFree(p);
   delete L;
 }
 
-static int check_weights(const mm_expert_weights &w, const char *what) {
+static int check_weights(const mm_expert_weights &w, const char *what, bool nv) {
   if (!w.w13 || !w.w13_scale || !w.w2 || !w.w2_scale) return fail(MM_ERR_INVALID, "%s: null weight pointer", what);
+  if (nv && (!w.w13_scale_2 || !w.w2_scale_2))
+    return fail(MM_ERR_INVALID, "%s: NVFP4 weights need w13_scale_2 and w2_scale_2", what);
   if (!aligned(w.w13, 16) || !aligned(w.w2, 16))
     return fail(MM_ERR_INVALID, "%s: packed weights must be 16-byte aligned", what);
   return MM_OK;
@@ -273,13 +280,19 @@ int mm_layer_create(const mm_layer_desc *desc, mm_layer **out) {
                 d.expert_offset + d.experts, d.router_experts);
   if (d.top_k < 1 || d.top_k > kMaxTopK) return fail(MM_ERR_INVALID, "top_k %d outside 1..%d", d.top_k, kMaxTopK);
   if (d.max_tokens < 1 || d.max_tokens > kMaxTokens) return fail(MM_ERR_INVALID, "max_tokens %d outside 1..%d", d.max_tokens, kMaxTokens);
-  if (d.weight_format != MM_WEIGHT_MXFP4) return fail(MM_ERR_UNSUPPORTED, "weight format %d is not built (MXFP4)", d.weight_format);
+  if (d.weight_format != MM_WEIGHT_MXFP4 && d.weight_format != MM_WEIGHT_NVFP4)
+    return fail(MM_ERR_UNSUPPORTED, "weight format %d is not built (MXFP4, NVFP4)", d.weight_format);
+  const bool nv = d.weight_format == MM_WEIGHT_NVFP4;
+  if (nv && !(d.input_scale[0] > 0.0f && d.input_scale[1] > 0.0f && d.input_scale[0] < INFINITY &&
+              d.input_scale[1] < INFINITY))
+    return fail(MM_ERR_INVALID, "NVFP4 input scales must be positive and finite (%g, %g)", d.input_scale[0],
+                d.input_scale[1]);
   if (d.act_terms < 1 || d.act_terms > kMaxTerms)
     return fail(MM_ERR_INVALID, "act_terms %d outside 1..%d", d.act_terms, kMaxTerms);
-  int rc = check_weights(d.routed, "routed");
+  int rc = check_weights(d.routed, "routed", nv);
   if (rc) return rc;
   const int has_shared = d.shared.w13 != nullptr;
-  if (has_shared && (rc = check_weights(d.shared, "shared"))) return rc;
+  if (has_shared && (rc = check_weights(d.shared, "shared", nv))) return rc;
 
   MM_CUDA(cudaSetDevice(d.device));
   mm_layer *L = new mm_layer();
@@ -293,6 +306,13 @@ int mm_layer_create(const mm_layer_desc *desc, mm_layer **out) {
   L->Tmax = d.max_tokens;
   L->terms = d.act_terms;
   L->has_shared = has_shared;
+  L->fmt = nv ? kFmtNv : kFmtMx;
+  L->block = nv ? 16 : 32;
+  L->sf_stage = nv ? Fmt<kFmtNv>::kSfStageBytes : Fmt<kFmtMx>::kSfStageBytes;
+  if (nv) {
+    L->gs1 = 1.0f / d.input_scale[0];
+    L->gs2 = 1.0f / d.input_scale[1];
+  }
   L->m1 = L->I / 64;
   L->m2 = L->H / 128;
   L->ks1 = L->H / kStageK;
@@ -320,20 +340,23 @@ int mm_layer_create(const mm_layer_desc *desc, mm_layer **out) {
   } while (0)
 
   const size_t E = L->E, H = L->H, I = L->I;
-  const size_t sfa13_bytes = E * L->m1 * L->ks1 * 1024;
-  const size_t sfa2_bytes = E * L->m2 * L->ks2 * 1024;
+  const size_t sfs = static_cast<size_t>(L->sf_stage);
+  const size_t sfa13_bytes = E * L->m1 * L->ks1 * sfs;
+  const size_t sfa2_bytes = E * L->m2 * L->ks2 * sfs;
   ALLOC(L->sfa13, sfa13_bytes);
   ALLOC(L->sfa2, sfa2_bytes);
   if (has_shared) {
-    ALLOC(L->ssfa13, static_cast<size_t>(L->m1) * L->ks1 * 1024);
-    ALLOC(L->ssfa2, static_cast<size_t>(L->m2) * L->ks2 * 1024);
+    ALLOC(L->ssfa13, static_cast<size_t>(L->m1) * L->ks1 * sfs);
+    ALLOC(L->ssfa2, static_cast<size_t>(L->m2) * L->ks2 * sfs);
   }
+  if (nv) ALLOC(L->alpha, sizeof(float) * (2 * E + 2));
   const size_t xq_bytes = kMaxTerms * static_cast<size_t>(L->Tmax) * H / 2;
   const size_t hq_bytes = kMaxTerms * static_cast<size_t>(L->rows_cap) * I / 2;
+  const size_t xs_bytes = xq_bytes * 2 / L->block, hs_bytes = hq_bytes * 2 / L->block;
   ALLOC(L->xq, xq_bytes);
-  ALLOC(L->xs, xq_bytes / 16);
+  ALLOC(L->xs, xs_bytes);
   ALLOC(L->hq, hq_bytes);
-  ALLOC(L->hs, hq_bytes / 16);
+  ALLOC(L->hs, hs_bytes);
   ALLOC(L->segs, sizeof(int4) * L->max_segs);
   ALLOC(L->ctrl, sizeof(int) * kCtrlWords);
   ALLOC(L->flags, sizeof(int) * L->max_segs);
@@ -347,19 +370,20 @@ int mm_layer_create(const mm_layer_desc *desc, mm_layer **out) {
   ce = cudaMemset(L->ctrl, 0, sizeof(int) * kCtrlWords);
   if (ce == cudaSuccess) ce = cudaMemset(L->err, 0, sizeof(uint32_t));
   if (ce == cudaSuccess) ce = cudaMemset(L->hq, 0, hq_bytes);
-  if (ce == cudaSuccess) ce = cudaMemset(L->hs, 0, hq_bytes / 16);
+  if (ce == cudaSuccess) ce = cudaMemset(L->hs, 0, hs_bytes);
   if (ce == cudaSuccess) ce = cudaMemset(L->xq, 0, xq_bytes);
-  if (ce == cudaSuccess) ce = cudaMemset(L->xs, 0, xq_bytes / 16);
+  if (ce == cudaSuccess) ce = cudaMemset(L->xs, 0, xs_bytes);
   if (ce != cudaSuccess) {
     free_layer(L);
     return fail(MM_ERR_CUDA, "cudaMemset: %s", cudaGetErrorString(ce));
   }
 
-  // scale repack (once): canonical E8M0 -> UMMA scale chunks
+  // scale repack (once): canonical scales -> UMMA scale chunks
   auto repack = [&](const void *src, uint8_t *dst, int n, int rows, int k, int gate_up) -> int {
-    const size_t total = static_cast<size_t>(n) * (rows / 128) * (k / kStageK) * 1024;
+    const size_t total = static_cast<size_t>(n) * (rows / 128) * (k / kStageK) * sfs;
     const int blocks = static_cast<int>(total / 256 < 65536 ? (total + 255) / 256 : 65536);
-    repack_scales_kernel<<<blocks, 256>>>(static_cast<const uint8_t *>(src), dst, n, rows, k, gate_up, L->I);
+    repack_scales_kernel<<<blocks, 256>>>(static_cast<const uint8_t *>(src), dst, n, rows, k, gate_up, L->I,
+                                          L->block);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(MM_ERR_CUDA, "repack_scales_kernel: %s", cudaGetErrorString(e));
     return MM_OK;
@@ -370,6 +394,20 @@ int mm_layer_create(const mm_layer_desc *desc, mm_layer **out) {
       (has_shared && (rc = repack(d.shared.w2_scale, L->ssfa2, 1, L->H, L->I, 0)))) {
     free_layer(L);
     return rc;
+  }
+  if (nv) {  // accumulator multipliers: scale_2 x the GEMM's input scale
+    const int eb = (L->E + 255) / 256;
+    nv_alpha_kernel<<<eb, 256>>>(d.routed.w13_scale_2, d.input_scale[0], L->alpha, L->E);
+    nv_alpha_kernel<<<eb, 256>>>(d.routed.w2_scale_2, d.input_scale[1], L->alpha + L->E, L->E);
+    if (has_shared) {
+      nv_alpha_kernel<<<1, 32>>>(d.shared.w13_scale_2, d.input_scale[0], L->alpha + 2 * L->E, 1);
+      nv_alpha_kernel<<<1, 32>>>(d.shared.w2_scale_2, d.input_scale[1], L->alpha + 2 * L->E + 1, 1);
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+      free_layer(L);
+      return fail(MM_ERR_CUDA, "nv_alpha_kernel: %s", cudaGetErrorString(e));
+    }
   }
   ce = cudaDeviceSynchronize();
   if (ce != cudaSuccess) {
@@ -401,6 +439,14 @@ int mm_layer_create(const mm_layer_desc *desc, mm_layer **out) {
   ea.err = L->err;
   ea.clamp = d.clamp;
   ea.shared_clamp = d.shared_clamp;
+  if (nv) {
+    ea.alpha13 = L->alpha;
+    ea.alpha2 = L->alpha + L->E;
+    ea.salpha13 = has_shared ? L->alpha + 2 * L->E : L->alpha;
+    ea.salpha2 = has_shared ? L->alpha + 2 * L->E + 1 : L->alpha + L->E;
+    ea.gs2 = L->gs2;
+    ea.inv_gs2 = d.input_scale[1];
+  }
   ea.hidden = L->H;
   ea.inter = L->I;
   ea.max_tokens = L->Tmax;
@@ -411,7 +457,10 @@ int mm_layer_create(const mm_layer_desc *desc, mm_layer **out) {
   ea.ks1 = L->ks1;
   ea.ks2 = L->ks2;
 
-  ce = cudaFuncSetAttribute(expert_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc);
+  ce = nv ? cudaFuncSetAttribute(expert_kernel<kFmtNv>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 Fmt<kFmtNv>::kSmemAlloc)
+          : cudaFuncSetAttribute(expert_kernel<kFmtMx>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 Fmt<kFmtMx>::kSmemAlloc);
   if (ce == cudaSuccess)
     ce = cudaFuncSetAttribute(front_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               static_cast<int>(route_smem_bytes(kMaxTokens, kMaxRouterExperts)));
@@ -443,8 +492,14 @@ int mm_layer_get_info(const mm_layer *L, mm_layer_info *info) {
   info->rows_capacity = L->rows_cap;
   info->shared_row_base = L->shared_row_base;
   info->route_words = L->route_words_max;
-  info->weight_bytes = 3LL * L->H * L->I / 2 + 3LL * L->H * L->I / 32;
+  info->weight_bytes = 3LL * L->H * L->I / 2 + 3LL * L->H * L->I / L->block;
   return MM_OK;
+}
+
+static cudaError_t launch_experts(mm_layer *L, const ExpertArgs &ea, void *stream) {
+  const dim3 grid(kCtasPerSm * L->num_sms), block(kExpertThreads);
+  return L->fmt == kFmtNv ? launch(expert_kernel<kFmtNv>, grid, block, Fmt<kFmtNv>::kSmemAlloc, stream, ea)
+                          : launch(expert_kernel<kFmtMx>, grid, block, Fmt<kFmtMx>::kSmemAlloc, stream, ea);
 }
 
 // One launch of the router GEMV (w non-null) and the MXFP4-terms quantization
@@ -466,6 +521,9 @@ static int launch_router_quant(mm_layer *L, const uint16_t *x, const uint16_t *w
   a.xs = L->xs;
   a.max_tokens = L->Tmax;
   a.terms = L->terms;
+  a.fmt = L->fmt;
+  a.gs = L->gs1;
+  a.inv_gs = L->fmt == kFmtNv ? L->d.input_scale[0] : 1.0f;
   const int quant_ctas = (tokens * (L->H / 32) + 255) / 256;
   dim3 grid(a.gemv_ctas + quant_ctas, w ? (tokens + 7) / 8 : 1);
   MM_CUDA(launch(router_quant_kernel, grid, dim3(256), 0, stream, a));
@@ -513,7 +571,7 @@ static int run_front_and_experts(mm_layer *L, const uint16_t *x, const mm_gate_a
   ea.rows_out = rows;
   ea.record = record;
   ea.token_off = 4 + 2 * route_cta_words(route_max_ctas(tokens, L->K, L->E));
-  MM_CUDA(launch(expert_kernel, dim3(kCtasPerSm * L->num_sms), dim3(kExpertThreads), kSmemAlloc, stream, ea));
+  MM_CUDA(launch_experts(L, ea, stream));
   return MM_OK;
 }
 
@@ -525,7 +583,7 @@ int mm_layer_rerun_experts(mm_layer *L, int32_t tokens, const int32_t *record, u
   ea.rows_out = rows;
   ea.record = record;
   ea.token_off = 4 + 2 * route_cta_words(route_max_ctas(tokens, L->K, L->E));
-  MM_CUDA(launch(expert_kernel, dim3(kCtasPerSm * L->num_sms), dim3(kExpertThreads), kSmemAlloc, stream, ea));
+  MM_CUDA(launch_experts(L, ea, stream));
   return MM_OK;
 }
 

@@ -113,18 +113,44 @@ __device__ __forceinline__ void mma_mxf4(uint32_t d_tmem, uint64_t adesc, uint64
       : "memory");
 }
 
+// Instruction descriptor of kind::mxf4nvf4 block16: A and B E2M1 (format 1),
+// both K-major, E4M3 scales (scale format 0), M = 128, N = n, K = 64; each MMA
+// consumes four scale bytes per row (scale-factor id 0).
+__device__ __forceinline__ uint32_t idesc_nvf4(uint32_t n) {
+  uint32_t d = 0;
+  d |= 1u << 7;             // A format E2M1
+  d |= 1u << 10;            // B format E2M1
+  d |= ((n >> 3) & 0x3fu) << 17;
+  d |= (128u >> 4) << 24;   // M = 128
+  return d;
+}
+
+__device__ __forceinline__ void mma_nvf4(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%4], [%5], p;\n\t}" ::
+          "r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(sfa_tmem), "r"(sfb_tmem), "r"(accumulate)
+      : "memory");
+}
+
 }  // namespace
 
+template <int F>
 __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(const __grid_constant__ ExpertArgs p) {
+  using L = Fmt<F>;
+  constexpr bool kNv = F == kFmtNv;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   unsigned char *sbase = smem_raw + (base - raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t bars = base + kSmemBar;
+  const uint32_t bars = base + L::kSmemBar;
   auto bar = [&](int i) -> uint32_t { return bars + 8u * static_cast<uint32_t>(i); };
-  int *work_ids = reinterpret_cast<int *>(sbase + kSmemWorkIds);
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sbase + kSmemTmemBase);
+  int *work_ids = reinterpret_cast<int *>(sbase + L::kSmemWorkIds);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sbase + L::kSmemTmemBase);
   uint32_t *err = p.err;
 
   pdl_launch_dependents();
@@ -149,8 +175,8 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
     fence_barrier_init();
   }
   {  // zero the activation and scale areas once: rows a unit does not load stay finite
-    uint4 *z = reinterpret_cast<uint4 *>(sbase + kSmemB);
-    const int n16 = (kSmemEpi - kSmemB) / 16;
+    uint4 *z = reinterpret_cast<uint4 *>(sbase + L::kSmemB);
+    const int n16 = (L::kSmemEpi - L::kSmemB) / 16;
     for (int i = threadIdx.x; i < n16; i += blockDim.x) z[i] = make_uint4(0u, 0u, 0u, 0u);
     fence_proxy_async_smem();
   }
@@ -202,7 +228,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
         const CUtensorMap *map = g2 ? (sh ? &p.sw2_map : &p.w2_map) : (sh ? &p.sw13_map : &p.w13_map);
         const int ks_n = g2 ? p.ks2 : p.ks1;
         const uint8_t *sfa = g2 ? (sh ? p.ssfa2 : p.sfa2) : (sh ? p.ssfa13 : p.sfa13);
-        sfa += (static_cast<size_t>(e) * (g2 ? p.m2 : p.m1) + m) * static_cast<size_t>(ks_n) * 1024u;
+        sfa += (static_cast<size_t>(e) * (g2 ? p.m2 : p.m1) + m) * static_cast<size_t>(ks_n) * L::kSfStageBytes;
         const int claim_at = ks_n > 3 ? ks_n - 3 : 0;
 #pragma unroll 1
         for (int ks = 0; ks < ks_n; ++ks) {
@@ -212,8 +238,8 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
             break;
           }
           const uint32_t full = bar(kBarFull + stage);
-          mbar_expect_tx(full, kATxBytes + kSfaStageBytes);
-          const uint32_t sa = base + kSmemA + stage * kAStageBytes;
+          mbar_expect_tx(full, kATxBytes + L::kSfStageBytes);
+          const uint32_t sa = base + L::kSmemA + stage * kAStageBytes;
           const int x = ks * kRowBytes;  // byte offset along K
           if (!g2) {
             tma_load_3d(sa, map, x, 64 * m, e, full, policy);
@@ -221,8 +247,8 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
           } else {
             tma_load_3d(sa, map, x, 128 * m, e, full, policy);
           }
-          bulk_load(base + kSmemSfa + stage * kSfaStageBytes, sfa + static_cast<size_t>(ks) * 1024u,
-                    kSfaStageBytes, full, policy);
+          bulk_load(base + L::kSmemSfa + stage * L::kSfStageBytes,
+                    sfa + static_cast<size_t>(ks) * L::kSfStageBytes, L::kSfStageBytes, full, policy);
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
         }
       }
@@ -242,7 +268,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
       // 1 KB between 8-row groups; scale chunks: 32 rows x 16 B, 128 B apart
       const uint64_t sw_hi = smem_desc(0, 0, 1024, kLayoutSw128);
       const uint64_t sf_hi = smem_desc(0, 0, 128, kLayoutNone);
-      const uint32_t idesc_base = idesc_mxf4(0, 0);
+      const uint32_t idesc_base = kNv ? idesc_nvf4(0) : idesc_mxf4(0, 0);
 #pragma unroll 1
       while (true) {
         if (!mbar_wait(bar(kBarWorkFull + ws), wphase, err, kErrTimeoutWork)) break;
@@ -257,11 +283,11 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
         const uint32_t n = static_cast<uint32_t>((sg.z + 7) & ~7);
         const uint32_t nmma = n * static_cast<uint32_t>(p.terms);  // term 0 rows, term 1 rows, ...
         const uint32_t id0 = idesc_base | ((nmma >> 3) << 17);
-        const uint32_t id2 = id0 | (2u << 4) | (2u << 29);
+        const uint32_t id2 = id0 | (2u << 4) | (2u << 29);  // MXFP4: the chunk's second byte pair
         const int ks_n = g2 ? p.ks2 : p.ks1;
         if (!mbar_wait(bar(kBarAccEmpty + acc), acc_phase ^ 1u, err, kErrTimeoutAcc)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tbase + kTmemAcc + acc * kBRows;
+        const uint32_t d_tmem = tbase + L::kTmemAcc + acc * kBRows;
         bool ok = true;
 #pragma unroll 1
         for (int ks = 0; ks < ks_n; ++ks) {
@@ -271,22 +297,27 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
           }
           tc_fence_after();
           fence_proxy_async_smem();  // activation rows and B scales arrived via cp.async
-          const uint32_t sfa_t = tbase + kTmemSfa + stage * 8;
-          const uint32_t sfb_t = tbase + kTmemSfb + stage * 8;
-          const uint64_t sfa_d = sf_hi | ((base + kSmemSfa + stage * kSfaStageBytes) >> 4);
-          const uint64_t sfb_d = sf_hi | ((base + kSmemSfb + stage * kSfbStageBytes) >> 4);
-          tc_cp_32x128b_warpx4(sfa_t, sfa_d);
-          tc_cp_32x128b_warpx4(sfa_t + 4, sfa_d + (512 >> 4));
-          tc_cp_32x128b_warpx4(sfb_t, sfb_d);
-          tc_cp_32x128b_warpx4(sfb_t + 4, sfb_d + (512 >> 4));
-          const uint64_t a_d = sw_hi | ((base + kSmemA + stage * kAStageBytes) >> 4);
-          const uint64_t b_d = sw_hi | ((base + kSmemB + stage * kBStageBytes) >> 4);
-          // four K = 64 steps of 32 bytes along the 128-byte swizzled row;
-          // scale chunk c = k / 2 holds k-blocks 2k, 2k + 1 at bytes (k % 2) * 2
+          const uint32_t sfa_t = tbase + L::kTmemSfa + stage * L::kTmemSfCols;
+          const uint32_t sfb_t = tbase + L::kTmemSfb + stage * L::kTmemSfCols;
+          const uint64_t sfa_d = sf_hi | ((base + L::kSmemSfa + stage * L::kSfStageBytes) >> 4);
+          const uint64_t sfb_d = sf_hi | ((base + L::kSmemSfb + stage * L::kSfStageBytes) >> 4);
+#pragma unroll
+          for (int c = 0; c < L::kChunks; ++c) {
+            tc_cp_32x128b_warpx4(sfa_t + 4 * c, sfa_d + ((512 * c) >> 4));
+            tc_cp_32x128b_warpx4(sfb_t + 4 * c, sfb_d + ((512 * c) >> 4));
+          }
+          const uint64_t a_d = sw_hi | ((base + L::kSmemA + stage * kAStageBytes) >> 4);
+          const uint64_t b_d = sw_hi | ((base + L::kSmemB + stage * kBStageBytes) >> 4);
+          // four K = 64 steps of 32 bytes along the 128-byte swizzled row.
+          // MXFP4: scale chunk k / 2 holds the k-blocks of steps 2j, 2j + 1 at
+          // byte pairs 0 and 2; NVFP4: chunk k holds step k's four k-blocks
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            mma_mxf4(d_tmem, a_d + 2 * k, b_d + 2 * k, (k & 1) ? id2 : id0, sfa_t + 4 * (k >> 1),
-                     sfb_t + 4 * (k >> 1), (ks | k) != 0 ? 1u : 0u);
+            if constexpr (kNv)
+              mma_nvf4(d_tmem, a_d + 2 * k, b_d + 2 * k, id0, sfa_t + 4 * k, sfb_t + 4 * k, (ks | k) != 0 ? 1u : 0u);
+            else
+              mma_mxf4(d_tmem, a_d + 2 * k, b_d + 2 * k, (k & 1) ? id2 : id0, sfa_t + 4 * (k >> 1),
+                       sfb_t + 4 * (k >> 1), (ks | k) != 0 ? 1u : 0u);
           }
           tc_commit(bar(kBarEmpty + stage));
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
@@ -348,7 +379,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
       const uint8_t *dsc = g2 ? p.hs : p.xs;
       const uint32_t rowb = static_cast<uint32_t>(K) >> 1;  // packed bytes per row
       const uint32_t term_q = static_cast<uint32_t>(g2 ? p.rows_cap : p.max_tokens) * rowb;
-      const uint32_t term_s = term_q >> 4;
+      const uint32_t term_s = term_q / (L::kBlock / 2);
       uint32_t soff[kPieces], doff[kPieces], sbytes[kPieces];
 #pragma unroll
       for (int i = 0; i < kPieces; ++i) {
@@ -360,8 +391,9 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
         doff[i] = (rr >> 3) * 1024 + (rr & 7) * 128 + ((pc ^ (rr & 7)) << 4);
         sbytes[i] = (rr < nb && r < rows) ? 16u : 0u;
       }
-      // scale pieces: B rows rr = lane and lane + 32, chunks 0 and 1
-      uint32_t s_soff[4], s_doff[4], s_bytes[4];
+      // scale pieces: B rows rr = lane and lane + 32, every chunk of the stage
+      constexpr int kC = L::kChunks;
+      uint32_t s_soff[2 * kC], s_doff[2 * kC], s_bytes[2 * kC];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int rr = lane + 32 * h;
@@ -369,10 +401,11 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
         const int r = rr - t * n;
         const int sr = __shfl_sync(0xffffffffu, src, r & 31);
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          s_soff[2 * h + c] = static_cast<uint32_t>(t) * term_s + static_cast<uint32_t>(sr) * (K >> 5) + c * 4;
-          s_doff[2 * h + c] = c * 512 + (rr & 31) * 16 + (rr >> 5) * 4;
-          s_bytes[2 * h + c] = (rr < nb && r < rows) ? 4u : 0u;
+        for (int c = 0; c < kC; ++c) {
+          s_soff[kC * h + c] =
+              static_cast<uint32_t>(t) * term_s + static_cast<uint32_t>(sr) * (K / L::kBlock) + c * 4;
+          s_doff[kC * h + c] = c * 512 + (rr & 31) * 16 + (rr >> 5) * 4;
+          s_bytes[kC * h + c] = (rr < nb && r < rows) ? 4u : 0u;
         }
       }
       const int ks_n = g2 ? p.ks2 : p.ks1;
@@ -382,19 +415,19 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
         if (lane == 0) oke = mbar_wait(bar(kBarEmpty + stage), phase ^ 1u, err, kErrTimeoutEmpty) ? 1 : 0;
         oke = __shfl_sync(0xffffffffu, oke, 0);
         if (!oke) break;
-        const uint32_t sb = base + kSmemB + stage * kBStageBytes;
+        const uint32_t sb = base + L::kSmemB + stage * kBStageBytes;
         const uint8_t *gq = dq + ks * kRowBytes;
 #pragma unroll
         for (int i = 0; i < kPieces; ++i) {
           if (quarter + 4 * i < nb) cp_async_16(sb + doff[i], gq + soff[i], sbytes[i]);
         }
-        const uint32_t ssb = base + kSmemSfb + stage * kSfbStageBytes;
-        const uint8_t *gs = dsc + ks * 8;
+        const uint32_t ssb = base + L::kSmemSfb + stage * L::kSfStageBytes;
+        const uint8_t *gs = dsc + ks * L::kSfRow;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           if (lane + 32 * h < nb) {
-            cp_async_4(ssb + s_doff[2 * h], gs + s_soff[2 * h], s_bytes[2 * h]);
-            cp_async_4(ssb + s_doff[2 * h + 1], gs + s_soff[2 * h + 1], s_bytes[2 * h + 1]);
+#pragma unroll
+            for (int c = 0; c < kC; ++c) cp_async_4(ssb + s_doff[kC * h + c], gs + s_soff[kC * h + c], s_bytes[kC * h + c]);
           }
         }
         cp_async_arrive_noinc(bar(kBarFull + stage));
@@ -411,7 +444,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
     const int nseg = p.ctrl[kCtrlSegments];
     const int q = warp & 3;             // TMEM lane quadrant of this warp
     const int row = 32 * q + lane;      // accumulator row (weight-tile row)
-    float *ex = reinterpret_cast<float *>(sbase + kSmemEpi);
+    float *ex = reinterpret_cast<float *>(sbase + L::kSmemEpi);
     uint32_t ws = 0, wphase = 0, acc = 0, acc_phase = 0, ex_phase = 0;
 #pragma unroll 1
     while (true) {
@@ -439,7 +472,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
       if (!ok) break;
       tc_fence_after();
       uint32_t ra[32], rb[16];
-      const uint32_t taddr = tbase + (static_cast<uint32_t>(32 * q) << 16) + kTmemAcc + acc * kBRows;
+      const uint32_t taddr = tbase + (static_cast<uint32_t>(32 * q) << 16) + L::kTmemAcc + acc * kBRows;
       tc_ld_32x32b_x32(taddr, ra);
       tc_ld_32x32b_x16(taddr + 32, rb);
       tc_wait_ld();
@@ -455,6 +488,11 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
         if (p.terms > 1) a = __fadd_rn(a, __uint_as_float(n == 8 ? ra[8 + j] : ra[16 + j]));
         if (p.terms > 2) a = __fadd_rn(a, __uint_as_float(n == 8 ? ra[16 + j] : rb[j]));
         v[j] = a;
+      }
+      if constexpr (kNv) {  // the product of the two second-level scales
+        const float al = sg.x < 0 ? (g2 ? p.salpha2[0] : p.salpha13[0]) : (g2 ? p.alpha2[sg.x] : p.alpha13[sg.x]);
+#pragma unroll
+        for (int j = 0; j < kSegRows; ++j) v[j] = __fmul_rn(v[j], al);
       }
       if (!g2) {
         // rows 0..63: gate of features 64m + row; rows 64..127: up of the same features
@@ -481,7 +519,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
           const int f = 64 * m + 32 * q + lane;  // feature (column of h)
           const size_t rowb = static_cast<size_t>(p.inter) >> 1;
           const size_t tq = static_cast<size_t>(p.rows_cap) * rowb;  // term stride of hq
-          const size_t ts = tq >> 4;                                  // term stride of hs
+          const size_t ts = tq / (L::kBlock / 2);                     // term stride of hs
 #pragma unroll
           for (int j = 0; j < kSegRows; ++j) {
             if (j >= rows) break;
@@ -493,15 +531,28 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
             }
             float r = __fmul_rn(up, __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
             const size_t prow = static_cast<size_t>(sg.y + j);
-            // MXFP4 terms of the 32 features of this warp for token row j
+            // FP4 terms of the 32 features of this warp for token row j: one
+            // MXFP4 block of 32, or two NVFP4 blocks of 16 (lane halves)
             for (int t = 0; t < p.terms; ++t) {
-              const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(r))));
-              const uint32_t code = mx4_scale_code(amax);
-              const uint32_t nib = e2m1x2(__fmul_rn(r, mx_inverse(code)), 0.0f) & 15u;
-              r = __fsub_rn(r, __fmul_rn(e2m1_value(nib), mx_scale_value(code)));
+              uint32_t nib, code;
+              if constexpr (kNv) {
+                float amax = fabsf(r);
+#pragma unroll
+                for (int off = 8; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+                code = nv4_scale_code(amax, p.gs2);
+                const float sv = e4m3_value(static_cast<uint8_t>(code));
+                nib = e2m1x2(__fmul_rn(r, nv4_multiplier(sv, p.gs2)), 0.0f) & 15u;
+                r = __fsub_rn(r, __fmul_rn(__fmul_rn(e2m1_value(nib), sv), p.inv_gs2));
+              } else {
+                const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(r))));
+                code = mx4_scale_code(amax);
+                nib = e2m1x2(__fmul_rn(r, mx_inverse(code)), 0.0f) & 15u;
+                r = __fsub_rn(r, __fmul_rn(e2m1_value(nib), mx_scale_value(code)));
+              }
               const uint32_t up_nib = __shfl_down_sync(0xffffffffu, nib, 1);
               if ((lane & 1) == 0) p.hq[t * tq + prow * rowb + (f >> 1)] = static_cast<uint8_t>(nib | (up_nib << 4));
-              if (lane == 0) p.hs[t * ts + prow * (p.inter >> 5) + (f >> 5)] = static_cast<uint8_t>(code);
+              if ((lane & (L::kBlock - 1)) == 0)
+                p.hs[t * ts + prow * (p.inter / L::kBlock) + f / L::kBlock] = static_cast<uint8_t>(code);
             }
           }
           // publish this warp's 32 features of every row: two increments per unit
@@ -545,19 +596,23 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
 }
 
 // ============================================================================
-// Scale repack (layer creation): canonical E8M0 [n][rows][K/32] -> UMMA scale
-// chunks [n][tile][K/256][2][32 m0][4 m1][4 kk]. gate_up tiles take gate rows
-// 64t + r (r < 64) and up rows I + 64t + r - 64; down tiles rows 128t + r.
+// Scale repack (layer creation): canonical scales [n][rows][K/block] -> UMMA
+// scale chunks [n][tile][K/256][chunks][32 m0][4 m1][4 kk], chunks = 256 /
+// block / 4 (2 for MXFP4's E8M0 per 32, 4 for NVFP4's E4M3 per 16); chunk c
+// byte kk of row r holds k-block 4c + kk of the stage. gate_up tiles take gate
+// rows 64t + r (r < 64) and up rows I + 64t + r - 64; down tiles rows 128t + r.
 // ============================================================================
 __global__ void repack_scales_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst,
-                                     int n, int rows, int k, int gate_up, int inter) {
+                                     int n, int rows, int k, int gate_up, int inter, int block) {
   const int ks_n = k / kStageK;
   const int tiles = rows / 128;
-  const size_t total = static_cast<size_t>(n) * tiles * ks_n * 1024;
+  const int per_row = kStageK / block;          // scale bytes of a row per stage
+  const int stage_bytes = per_row * 128;        // = chunks * 512
+  const size_t total = static_cast<size_t>(n) * tiles * ks_n * stage_bytes;
   for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
        idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
-    const int b = static_cast<int>(idx & 1023);
-    size_t rest = idx >> 10;
+    const int b = static_cast<int>(idx % stage_bytes);
+    size_t rest = idx / stage_bytes;
     const int ks = static_cast<int>(rest % ks_n);
     rest /= ks_n;
     const int t = static_cast<int>(rest % tiles);
@@ -565,10 +620,21 @@ __global__ void repack_scales_kernel(const uint8_t *__restrict__ src, uint8_t *_
     const int c = b >> 9, w = b & 511;
     const int m0 = w >> 4, m1 = (w >> 2) & 3, kk = w & 3;
     const int r = m0 + 32 * m1;
-    const int kb = ks * 8 + 4 * c + kk;
+    const int kb = ks * per_row + 4 * c + kk;
     const int srow = gate_up ? (r < 64 ? 64 * t + r : inter + 64 * t + (r - 64)) : 128 * t + r;
-    dst[idx] = src[(static_cast<size_t>(e) * rows + srow) * (k >> 5) + kb];
+    dst[idx] = src[(static_cast<size_t>(e) * rows + srow) * (k / block) + kb];
   }
 }
+
+// NVFP4 accumulator multipliers: alpha[e] = scale_2[e] * input_scale (the
+// reference's g1_alpha / g2_alpha, glm5_3/sm103/moe/api.py:49-50).
+__global__ void nv_alpha_kernel(const float *__restrict__ scale_2, float input_scale, float *__restrict__ alpha,
+                                int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) alpha[i] = __fmul_rn(scale_2[i], input_scale);
+}
+
+template __global__ void expert_kernel<kFmtMx>(const __grid_constant__ ExpertArgs p);
+template __global__ void expert_kernel<kFmtNv>(const __grid_constant__ ExpertArgs p);
 
 }  // namespace mm

@@ -50,9 +50,11 @@ struct RouterArgs {
   int tokens, experts, hidden;
   int gemv_ctas;             // E, or 0 for quantization only
   uint8_t *xq;               // [kMaxTerms][max_tokens][H/2] packed E2M1, or null
-  uint8_t *xs;               // [kMaxTerms][max_tokens][H/32] E8M0
+  uint8_t *xs;               // [kMaxTerms][max_tokens][H/32] E8M0 (NVFP4: [H/16] E4M3)
   int max_tokens;
   int terms;
+  int fmt;                   // kFmtMx or kFmtNv
+  float gs, inv_gs;          // NVFP4: 1 / input_scale[0] and input_scale[0]
 };
 
 struct alignas(64) ExpertArgs {
@@ -60,14 +62,21 @@ struct alignas(64) ExpertArgs {
   CUtensorMap w2_map;        // routed down codes, u8 {I/2, H, E}, box {128, 128, 1}
   CUtensorMap sw13_map;      // shared expert (same shapes, E = 1)
   CUtensorMap sw2_map;
-  const uint8_t *sfa13;      // [E][I/64][H/256][1024] scale chunks
-  const uint8_t *sfa2;       // [E][H/128][I/256][1024]
+  const uint8_t *sfa13;      // [E][I/64][H/256][scale chunks of a stage]
+  const uint8_t *sfa2;       // [E][H/128][I/256][...]
   const uint8_t *ssfa13;
   const uint8_t *ssfa2;
   const uint8_t *xq;         // [kMaxTerms][max_tokens][H/2]
-  const uint8_t *xs;         // [kMaxTerms][max_tokens][H/32]
+  const uint8_t *xs;         // [kMaxTerms][max_tokens][H/block]
   uint8_t *hq;               // [kMaxTerms][rows_cap][I/2]
-  uint8_t *hs;               // [kMaxTerms][rows_cap][I/32]
+  uint8_t *hs;               // [kMaxTerms][rows_cap][I/block]
+  // NVFP4 only: accumulator multipliers per expert (weight scale_2 x the
+  // GEMM's input scale) and the down GEMM's input quantization scale
+  const float *alpha13;      // [E]
+  const float *alpha2;       // [E]
+  const float *salpha13;     // [1] shared expert
+  const float *salpha2;      // [1]
+  float gs2, inv_gs2;        // 1 / input_scale[1] and input_scale[1]
   uint16_t *rows_out;        // [rows_cap][H] bf16
   const int *record;
   const int4 *segs;
@@ -120,6 +129,37 @@ __device__ __forceinline__ void quantize_block32_fp4(const float (&v)[32], int t
   }
 }
 
+// NVFP4 terms of 16 fp32 values (one block) under the global scale gs: term t
+// is the NVFP4 quantization of the residual left by terms 0..t-1 (E4M3 scale
+// sf = nv4_scale_code(amax, gs), codes e2m1(r * gs / sf) RN saturating,
+// residual r -= (e2m1 * sf) * inv_gs). Writes 8 bytes of codes per term at
+// q + t * q_stride and the scale byte at s + t * s_stride.
+__device__ __forceinline__ void quantize_block16_nvfp4(const float *v, int terms, float gs, float inv_gs,
+                                                       uint8_t *q, size_t q_stride, uint8_t *s,
+                                                       size_t s_stride) {
+  float r[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) r[i] = v[i];
+  for (int t = 0; t < terms; ++t) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(r[i]));
+    const uint32_t c = nv4_scale_code(amax, gs);
+    const float sv = e4m3_value(static_cast<uint8_t>(c));
+    const float f = nv4_multiplier(sv, gs);
+    uint32_t packed[2] = {0u, 0u};
+#pragma unroll
+    for (int i = 0; i < 16; i += 2) {
+      const uint32_t b = e2m1x2(__fmul_rn(r[i], f), __fmul_rn(r[i + 1], f));
+      packed[i >> 3] |= b << (8 * ((i >> 1) & 3));
+      r[i] = __fsub_rn(r[i], __fmul_rn(__fmul_rn(e2m1_value(b & 15u), sv), inv_gs));
+      r[i + 1] = __fsub_rn(r[i + 1], __fmul_rn(__fmul_rn(e2m1_value(b >> 4), sv), inv_gs));
+    }
+    *reinterpret_cast<uint2 *>(q + t * q_stride) = make_uint2(packed[0], packed[1]);
+    s[t * s_stride] = static_cast<uint8_t>(c);
+  }
+}
+
 // Host helpers shared by the .cu files (mm_api.cu defines them).
 int set_error(int code, const char *fmt, ...);
 // dynamic shared memory of the route build for (tokens, local experts)
@@ -133,9 +173,12 @@ __global__ void router_quant_kernel(RouterArgs a);
 __global__ void gate_topk_kernel(GateArgs g);
 __global__ void route_kernel(RouteArgs r);
 __global__ void front_kernel(FrontArgs f);
+template <int F>
 __global__ void expert_kernel(const __grid_constant__ ExpertArgs p);
 __global__ void repack_scales_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst,
-                                     int n, int rows, int k, int gate_up, int inter);
+                                     int n, int rows, int k, int gate_up, int inter, int block);
+__global__ void nv_alpha_kernel(const float *__restrict__ scale_2, float input_scale, float *__restrict__ alpha,
+                                int n);
 __global__ void finalize_kernel(FinalizeArgs a);
 __global__ void finalize_partial_kernel(const float *__restrict__ partial, uint16_t *__restrict__ out,
                                         int tokens, int hidden);

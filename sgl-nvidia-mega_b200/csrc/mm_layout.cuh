@@ -3,13 +3,14 @@
 // HBM, per layer (all device memory, allocated once at layer creation):
 //   weights     caller-owned canonical MXFP4 (E2M1 codes, [n, rows, K/2] u8) read
 //               in place by TMA (128-byte rows, 128-byte swizzle);
-//   sfa13/sfa2  the E8M0 weight scales re-laid once as UMMA scale chunks:
-//               [n][m_tile][k_stage][2 chunks][32 m0][4 m1][4 kk] bytes, so one
-//               1 KB bulk copy per pipeline stage lands them ready for tcgen05.cp;
-//   xq/xs       the routed input as MXFP4 terms: [term][T][H/2] packed E2M1 and
-//               [term][T][H/32] E8M0, written by the front kernel;
-//   hq/hs       the SwiGLU output of gate_up, [term][rows][I/2] and [term][rows][I/32],
-//               rows in the reference's padded permuted order;
+//   sfa13/sfa2  the weight scales re-laid once as UMMA scale chunks:
+//               [n][m_tile][k_stage][chunks][32 m0][4 m1][4 kk] bytes (2 chunks
+//               for MXFP4, 4 for NVFP4), so one bulk copy per pipeline stage
+//               lands them ready for tcgen05.cp;
+//   xq/xs       the routed input as FP4 terms: [term][T][H/2] packed E2M1 and
+//               [term][T][H/block] scales, written by the router launch;
+//   hq/hs       the SwiGLU output of gate_up, [term][rows][I/2] and
+//               [term][rows][I/block], rows in the reference's padded permuted order;
 //   segs/ctrl   work tables built by the front kernel (below);
 //   err         the device error word.
 #pragma once
@@ -55,10 +56,10 @@ constexpr int kCtrlDone = 4;      // expert kernel's finished CTAs (reset by the
 constexpr int kCtrlWords = 8;
 
 // ---- the persistent expert kernel's shared memory -----------------------------------
-// Weights and activations are both packed E2M1 (two codes per byte) with an E8M0
-// scale per 32 along K, multiplied by tcgen05.mma kind::mxf4 (block32, K = 64).
-// The activations are carried as up to kMaxTerms MXFP4 terms (x ~ t0 + t1 + t2,
-// each term the MXFP4 quantization of the previous residual); a stage's B rows
+// Weights and activations are both packed E2M1 (two codes per byte) with a block
+// scale along K (format below), multiplied by tcgen05.mma with K = 64.
+// The activations are carried as up to kMaxTerms FP4 terms (x ~ t0 + t1 + t2,
+// each term the FP4 quantization of the previous residual); a stage's B rows
 // hold term 0 of the segment's n rows at [0, n), term 1 at [n, 2n), term 2 at
 // [2n, 3n) (n = rows rounded up to 8), so one MMA with N = terms * n multiplies
 // every term, each into its own accumulator columns.
@@ -73,17 +74,9 @@ constexpr int kRowBytes = kStageK / 2;          // 128: one 128-byte swizzle row
 constexpr int kAStageBytes = 128 * kRowBytes;   // 16 KB: 128 weight rows
 constexpr int kBRows = kMaxTerms * kSegRows;    // 48
 constexpr int kBStageBytes = kBRows * kRowBytes;  // 6 KB
-constexpr int kSfaStageBytes = 1024;            // 2 chunks x (32 m0 x 4 m1 x 4 kk)
-constexpr int kSfbStageBytes = 1024;            // 2 chunks x (32 x 4 x 4), rows < 64
 constexpr int kEpiBytes = 64 * kSegRows * 4;    // gate_up epilogue exchange
 constexpr int kWorkSlots = 4;
 
-constexpr int kSmemA = 0;
-constexpr int kSmemB = kSmemA + kStages * kAStageBytes;
-constexpr int kSmemSfa = kSmemB + kStages * kBStageBytes;
-constexpr int kSmemSfb = kSmemSfa + kStages * kSfaStageBytes;
-constexpr int kSmemEpi = kSmemSfb + kStages * kSfbStageBytes;
-constexpr int kSmemBar = kSmemEpi + kEpiBytes;
 // barriers: full[S], empty[S], acc_full[2], acc_empty[2], work_full[W], work_empty[W], drain,
 // epilogue staging full / free
 constexpr int kBarFull = 0;
@@ -96,23 +89,49 @@ constexpr int kBarDrain = 2 * kStages + 4 + 2 * kWorkSlots;
 constexpr int kBarExFull = kBarDrain + 1;   // gate_up epilogue: up rows staged
 constexpr int kBarExFree = kBarDrain + 2;   // gate_up epilogue: staging consumed
 constexpr int kNumBars = kBarDrain + 3;
-constexpr int kSmemWorkIds = kSmemBar + 8 * kNumBars;
-constexpr int kSmemTmemBase = kSmemWorkIds + 4 * kWorkSlots;
-constexpr int kSmemTotal = kSmemTmemBase + 16;
-constexpr int kSmemAlloc = kSmemTotal + 1024;  // room to align the base to 1 KB
-static_assert(kSmemAlloc <= 232448, "expert kernel shared memory over the 227 KB limit");
-static_assert(kCtasPerSm * (kSmemAlloc + 1024) <= 233472, "two CTAs must fit one SM's 228 KB");
-static_assert(kSmemB % 1024 == 0 && kBStageBytes % 1024 == 0 && kSmemSfa % 128 == 0 &&
-                  kSmemSfb % 128 == 0,
-              "alignment");
 
-// TMEM columns: 2 accumulators of kBRows fp32 columns, then per stage the A
-// scale chunks (8 columns) and the B scale chunks (8 columns).
-constexpr int kTmemAcc = 0;
-constexpr int kTmemSfa = 2 * kBRows;
-constexpr int kTmemSfb = kTmemSfa + kStages * 8;
+// ---- block-scaled FP4 formats ----------------------------------------------------
+// kFmtMx (MXFP4): an E8M0 scale per 32 elements along K, tcgen05.mma
+//   kind::mxf4 block32 (two scale bytes of a row per K = 64 instruction);
+// kFmtNv (NVFP4): an E4M3 scale per 16 elements along K (and an fp32
+//   second-level scale per expert, applied in the epilogue), tcgen05.mma
+//   kind::mxf4nvf4 block16 (four scale bytes of a row per instruction).
+// A stage's scales travel as 512-byte chunks (128 rows x 4 bytes: byte
+// 16 m0 + 4 m1 + kk holds row m0 + 32 m1's k-block kk), copied to TMEM by
+// tcgen05.cp 32x128b.warpx4 into 4 columns each.
+constexpr int kFmtMx = 0;
+constexpr int kFmtNv = 1;
+template <int F>
+struct Fmt {
+  static constexpr int kBlock = F == kFmtNv ? 16 : 32;     // elements per scale
+  static constexpr int kSfRow = kStageK / kBlock;          // scale bytes per row per stage
+  static constexpr int kChunks = kSfRow / 4;               // 512-byte chunks per stage
+  static constexpr int kSfStageBytes = kChunks * 512;      // 1 KB or 2 KB
+  // shared memory (offsets from the 1 KB-aligned base)
+  static constexpr int kSmemA = 0;
+  static constexpr int kSmemB = kSmemA + kStages * kAStageBytes;
+  static constexpr int kSmemSfa = kSmemB + kStages * kBStageBytes;
+  static constexpr int kSmemSfb = kSmemSfa + kStages * kSfStageBytes;
+  static constexpr int kSmemEpi = kSmemSfb + kStages * kSfStageBytes;
+  static constexpr int kSmemBar = kSmemEpi + kEpiBytes;
+  static constexpr int kSmemWorkIds = kSmemBar + 8 * kNumBars;
+  static constexpr int kSmemTmemBase = kSmemWorkIds + 4 * kWorkSlots;
+  static constexpr int kSmemTotal = kSmemTmemBase + 16;
+  static constexpr int kSmemAlloc = kSmemTotal + 1024;  // room to align the base to 1 KB
+  // TMEM columns: 2 accumulators of kBRows fp32 columns, then per stage the A
+  // scale chunks and the B scale chunks (4 columns per chunk)
+  static constexpr int kTmemAcc = 0;
+  static constexpr int kTmemSfCols = 4 * kChunks;
+  static constexpr int kTmemSfa = 2 * kBRows;
+  static constexpr int kTmemSfb = kTmemSfa + kStages * kTmemSfCols;
+  static constexpr int kTmemEnd = kTmemSfb + kStages * kTmemSfCols;
+  static_assert(kSmemAlloc <= 232448, "expert kernel shared memory over the 227 KB limit");
+  static_assert(kCtasPerSm * (kSmemAlloc + 1024) <= 233472, "two CTAs must fit one SM's 228 KB");
+  static_assert(kSmemB % 1024 == 0 && kBStageBytes % 1024 == 0 && kSmemSfa % 128 == 0 && kSmemSfb % 128 == 0,
+                "alignment");
+};
 constexpr int kTmemCols = 256;  // x kCtasPerSm = the SM's 512 columns
-static_assert(kTmemSfb + kStages * 8 <= kTmemCols, "TMEM columns");
+static_assert(Fmt<kFmtMx>::kTmemEnd <= kTmemCols && Fmt<kFmtNv>::kTmemEnd <= kTmemCols, "TMEM columns");
 static_assert(kCtasPerSm * kTmemCols <= 512, "TMEM columns per SM");
 
 constexpr int kExpertThreads = 224;  // 7 warps: producer, MMA, B loader, 4 epilogue

@@ -126,6 +126,19 @@ __device__ __forceinline__ float e4m3_value(uint8_t code) {
   return s ? -v : v;
 }
 
+// NVFP4 block scale of a 16-element block with absolute maximum amax under
+// the global scale gs: the E4M3 byte of gs * (amax * fp32(1/6)), RN, saturating
+// to 448 (the reference's rule, glm5_3/sm103/primitives/ptx_tc.py:320-337,
+// written with IEEE operations where the reference uses approximate ones).
+__device__ __forceinline__ uint32_t nv4_scale_code(float amax, float gs) {
+  const float s = __fmul_rn(gs, __fmul_rn(amax, 0x1.555556p-3f));
+  return static_cast<uint32_t>(e4m3x2(s, 0.0f) & 0xffu);
+}
+// The multiplier mapping a block onto E2M1: gs / sf (IEEE), 0 for a zero scale.
+__device__ __forceinline__ float nv4_multiplier(float sf, float gs) {
+  return sf == 0.0f ? 0.0f : __fdiv_rn(gs, sf);
+}
+
 // Two floats -> one byte of two E2M1 codes (RN, saturating to +-6); lo in bits 0-3.
 __device__ __forceinline__ uint32_t e2m1x2(float lo, float hi) {
   uint32_t r;

@@ -33,8 +33,9 @@ namespace mm {
 // are exact in fp32. The weight row is static, so its loads are issued before
 // the grid-dependency wait.
 //
-// CTAs [gemv_ctas, ...) (blockIdx.y == 0): the MXFP4 terms of x, one 32-element
-// block of one token per thread (independent of the routing).
+// CTAs [gemv_ctas, ...) (blockIdx.y == 0): the FP4 terms of x, one 32-element
+// chunk of one token per thread (one MXFP4 block or two NVFP4 blocks;
+// independent of the routing).
 // ============================================================================
 __global__ void __launch_bounds__(256) router_quant_kernel(RouterArgs a) {
   pdl_launch_dependents();
@@ -59,9 +60,16 @@ __global__ void __launch_bounds__(256) router_quant_kernel(RouterArgs a) {
       }
     }
     const size_t q_stride = static_cast<size_t>(a.max_tokens) * (a.hidden >> 1);
-    const size_t s_stride = static_cast<size_t>(a.max_tokens) * blocks;
-    quantize_block32_fp4(v, a.terms, a.xq + static_cast<size_t>(t) * (a.hidden >> 1) + 16 * b, q_stride,
-                         a.xs + static_cast<size_t>(t) * blocks + b, s_stride);
+    uint8_t *q = a.xq + static_cast<size_t>(t) * (a.hidden >> 1) + 16 * b;
+    if (a.fmt == kFmtNv) {  // two NVFP4 blocks of 16
+      const size_t s_stride = static_cast<size_t>(a.max_tokens) * 2 * blocks;
+      uint8_t *sc = a.xs + static_cast<size_t>(t) * 2 * blocks + 2 * b;
+      quantize_block16_nvfp4(v, a.terms, a.gs, a.inv_gs, q, q_stride, sc, s_stride);
+      quantize_block16_nvfp4(v + 16, a.terms, a.gs, a.inv_gs, q + 8, q_stride, sc + 1, s_stride);
+    } else {
+      const size_t s_stride = static_cast<size_t>(a.max_tokens) * blocks;
+      quantize_block32_fp4(v, a.terms, q, q_stride, a.xs + static_cast<size_t>(t) * blocks + b, s_stride);
+    }
     return;
   }
   __shared__ float part_sum[kMaxRouterParts][8];

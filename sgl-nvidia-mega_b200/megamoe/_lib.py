@@ -28,10 +28,12 @@ MM_SCORE_SQRTSOFTPLUS = 2
 SCORES = {"sigmoid": MM_SCORE_SIGMOID, "softmax": MM_SCORE_SOFTMAX, "sqrtsoftplus": MM_SCORE_SQRTSOFTPLUS}
 
 MM_WEIGHT_MXFP4 = 0
+MM_WEIGHT_NVFP4 = 1
 
 
 class MMExpertWeights(ctypes.Structure):
-    _fields_ = [("w13", c_void_p), ("w13_scale", c_void_p), ("w2", c_void_p), ("w2_scale", c_void_p)]
+    _fields_ = [("w13", c_void_p), ("w13_scale", c_void_p), ("w2", c_void_p), ("w2_scale", c_void_p),
+                ("w13_scale_2", c_void_p), ("w2_scale_2", c_void_p)]
 
 
 class MMLayerDesc(ctypes.Structure):
@@ -50,6 +52,7 @@ class MMLayerDesc(ctypes.Structure):
         ("shared", MMExpertWeights),
         ("clamp", c_void_p),
         ("shared_clamp", c_void_p),
+        ("input_scale", c_float * 2),
     ]
 
 

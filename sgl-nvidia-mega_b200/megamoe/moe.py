@@ -51,11 +51,15 @@ def _u8(t: torch.Tensor) -> torch.Tensor:
 
 
 class RoutedMoE:
-    """The routed-MoE chain bound to one MoE layer's MXFP4 weights.
+    """The routed-MoE chain bound to one MoE layer's FP4 weights.
 
     Weights (canonical layout, read in place; see include/megamoe.h):
       w13 u8 [E, 2I, H/2], w13_scale u8 [E, 2I, H/32], w2 u8 [E, H, I/2],
       w2_scale u8 [E, H, I/32]; ``shared`` = the same four tensors with E = 1.
+    ``weight_format="nvfp4"``: the scales are E4M3 per 16 ([E, 2I, H/16],
+    [E, H, I/16]), ``w13_scale_2`` / ``w2_scale_2`` are the fp32 [E] per-expert
+    second-level scales, ``input_scale`` the static (FC1, FC2) input scales,
+    and ``shared`` carries six tensors (the four, then its two scale_2 [1]).
     ``router_experts``: the router's expert count (default: the local ones);
     ``expert_offset``: router id of local expert 0 (expert parallelism);
     ``clamp``: fp32 [E] SwiGLU clamp limits or None;
@@ -78,16 +82,32 @@ class RoutedMoE:
         shared: Optional[Sequence[torch.Tensor]] = None,
         shared_clamp: Optional[torch.Tensor] = None,
         act_terms: int = 3,
+        weight_format: str = "mxfp4",
+        w13_scale_2: Optional[torch.Tensor] = None,
+        w2_scale_2: Optional[torch.Tensor] = None,
+        input_scale: Optional[Sequence[float]] = None,
     ):
+        if weight_format not in ("mxfp4", "nvfp4"):
+            raise ValueError(f"unknown weight format {weight_format!r}")
+        nv = weight_format == "nvfp4"
+        block = 16 if nv else 32
         w13, w13_scale, w2, w2_scale = (_u8(t) for t in (w13, w13_scale, w2, w2_scale))
         if w13.dim() != 3:
             raise ValueError(f"w13: expected [E, 2I, H/2], got {tuple(w13.shape)}")
         experts, two_i, half_h = w13.shape
         hidden, inter = 2 * half_h, two_i // 2
         _expect(w13, (experts, 2 * inter, hidden // 2), "w13")
-        _expect(w13_scale, (experts, 2 * inter, hidden // 32), "w13_scale")
+        _expect(w13_scale, (experts, 2 * inter, hidden // block), "w13_scale")
         _expect(w2, (experts, hidden, inter // 2), "w2")
-        _expect(w2_scale, (experts, hidden, inter // 32), "w2_scale")
+        _expect(w2_scale, (experts, hidden, inter // block), "w2_scale")
+        if nv:
+            if w13_scale_2 is None or w2_scale_2 is None or input_scale is None or len(input_scale) != 2:
+                raise ValueError("nvfp4 needs w13_scale_2, w2_scale_2 and input_scale=(fc1, fc2)")
+            for name, t in (("w13_scale_2", w13_scale_2), ("w2_scale_2", w2_scale_2)):
+                _expect(t, (experts,), name, 4)
+                if t.dtype != torch.float32 or t.device != w13.device:
+                    raise ValueError(f"{name} must be fp32 [E] on the weights' device")
+        self.weight_format = weight_format
         if not w13.is_cuda:
             raise ValueError("weights must be CUDA tensors")
         self.device = w13.device
@@ -108,19 +128,31 @@ class RoutedMoE:
         desc.expert_offset = self.expert_offset
         desc.top_k = self.top_k
         desc.max_tokens = self.max_rows
-        desc.weight_format = _lib.MM_WEIGHT_MXFP4
+        desc.weight_format = _lib.MM_WEIGHT_NVFP4 if nv else _lib.MM_WEIGHT_MXFP4
         desc.act_terms = self.act_terms
         desc.device = self.device.index if self.device.index is not None else torch.cuda.current_device()
-        desc.routed = _lib.MMExpertWeights(*(t.data_ptr() for t in (w13, w13_scale, w2, w2_scale)))
+        desc.routed = _lib.MMExpertWeights(*(t.data_ptr() for t in (w13, w13_scale, w2, w2_scale)),
+                                           _ptr(w13_scale_2) if nv else None, _ptr(w2_scale_2) if nv else None)
+        if nv:
+            desc.input_scale[0], desc.input_scale[1] = float(input_scale[0]), float(input_scale[1])
+            keep += [w13_scale_2, w2_scale_2]
         self.has_shared = shared is not None
         if shared is not None:
-            s13, s13s, s2, s2s = (_u8(t) for t in shared)
+            if len(shared) != (6 if nv else 4):
+                raise ValueError(f"shared: expected {6 if nv else 4} tensors")
+            s13, s13s, s2, s2s = (_u8(t) for t in shared[:4])
             _expect(s13, (1, 2 * inter, hidden // 2), "shared w13")
-            _expect(s13s, (1, 2 * inter, hidden // 32), "shared w13_scale")
+            _expect(s13s, (1, 2 * inter, hidden // block), "shared w13_scale")
             _expect(s2, (1, hidden, inter // 2), "shared w2")
-            _expect(s2s, (1, hidden, inter // 32), "shared w2_scale")
-            desc.shared = _lib.MMExpertWeights(*(t.data_ptr() for t in (s13, s13s, s2, s2s)))
-            keep += [s13, s13s, s2, s2s, shared_clamp]
+            _expect(s2s, (1, hidden, inter // block), "shared w2_scale")
+            extra = [None, None]
+            if nv:
+                extra = list(shared[4:6])
+                for t in extra:
+                    _expect(t, (1,), "shared scale_2", 4)
+            desc.shared = _lib.MMExpertWeights(*(t.data_ptr() for t in (s13, s13s, s2, s2s)),
+                                               *(_ptr(t) for t in extra))
+            keep += [s13, s13s, s2, s2s, shared_clamp] + extra
         desc.clamp = _ptr(clamp)
         desc.shared_clamp = _ptr(shared_clamp)
         handle = ctypes.c_void_p()

@@ -34,8 +34,12 @@ def to_gpu_layer(layer, top_k, max_rows, act_terms=3, router_experts=None, exper
     if layer.get("shared") is not None:
         shared = [t.to(dev) for t in layer["shared"]]
     clamp = None if layer.get("clamp") is None else sel(layer["clamp"]).to(dev)
+    nv = {}
+    if layer.get("fmt") == "nvfp4":
+        nv = dict(weight_format="nvfp4", w13_scale_2=sel(layer["w13_scale_2"]).contiguous().to(dev),
+                  w2_scale_2=sel(layer["w2_scale_2"]).contiguous().to(dev), input_scale=layer["input_scale"])
     return mm.RoutedMoE(*w, top_k, max_rows, clamp=clamp, router_experts=router_experts,
-                        expert_offset=expert_offset, shared=shared, act_terms=act_terms)
+                        expert_offset=expert_offset, shared=shared, act_terms=act_terms, **nv)
 
 
 # ----------------------------------------------------------------------------- routing
@@ -151,11 +155,16 @@ def _run_and_check(layer, x, ids, weights, K, max_rows, act_terms=3, expert_offs
     # deferred rows against the oracle with the kernels' quantization
     got_rows = np.stack([rows_c[perm_c[t, k]].numpy() for (t, k) in kn_rows])
     want_rows = np.stack([v.numpy() for v in kn_rows.values()])
-    assert O.max_abs_rel(got_rows, want_rows) <= ROWS_TOL
+    # with one term a code the fp32 accumulation order moves across a rounding
+    # boundary is a whole E2M1 step of that activation, not a residual's
+    rows_tol = ROWS_TOL if act_terms > 1 else 5e-2
+    assert O.max_abs_rel(got_rows, want_rows) <= rows_tol
     if kn_shared is not None:
         sh = rows_c[moe.shared_row_base: moe.shared_row_base + x.shape[0]].numpy()
-        assert O.max_abs_rel(sh, kn_shared.numpy()) <= ROWS_TOL
-    tol = OUT_TOL if act_terms == 3 else 1e-1
+        assert O.max_abs_rel(sh, kn_shared.numpy()) <= rows_tol
+    # one or two activation terms are coarser numerics: plain NVFP4 / MXFP4
+    # activations sit about 1e-1 from the fp32 path (the oracle measures it)
+    tol = {3: OUT_TOL, 2: 1e-1, 1: 2.5e-1}[act_terms]
     err = O.max_abs_rel(out.float().cpu().numpy(), ex_out.numpy())
     assert err <= tol, err
     return moe, out
@@ -195,6 +204,47 @@ def test_experts_clamp_and_single_term():
     w = torch.rand((T, K), generator=g)
     _run_and_check(layer, x, ids, w, K, max_rows=8)
     _run_and_check(layer, x, ids, w, K, max_rows=8, act_terms=2)
+
+
+# ----------------------------------------------------------------------------- NVFP4
+def test_nvfp4_experts_config1_shape():
+    """NVFP4 weights (E2M1 + E4M3 per 16 + per-expert scale_2, kind::mxf4nvf4
+    block16) at the config-1 shape, softmax top-2, with a shared expert."""
+    mm = _mm()
+    H, I, E, K, T = 1024, 512, 16, 2, 4
+    layer = O.make_nvfp4_layer(H, I, E, shared=True, seed=2)
+    x, wr, _ = O.make_inputs(T, H, E, seed=2)
+    logits = mm.router_gemv(x.cuda(), wr.cuda())
+    w, ids = mm.gate_topk(logits, None, K, score="softmax")
+    _run_and_check(layer, x, ids.cpu(), w.cpu(), K, max_rows=8)
+
+
+@pytest.mark.parametrize("T,distinct", [(1, None), (16, None), (24, 8)])
+def test_nvfp4_experts_config4_hidden(T, distinct):
+    """NVFP4 at config 4's hidden size (6144) with a shared expert, sigmoid-style
+    random routing; distinct = 8 gives experts segments of 16 rows."""
+    H, I, E, K = 6144, 256, 32, 8
+    layer = O.make_nvfp4_layer(H, I, E, shared=True, seed=60 + T)
+    x, _, _ = O.make_inputs(T, H, E, seed=60 + T)
+    g = torch.Generator().manual_seed(60 + T)
+    ids = _random_ids(T, K, E, g, distinct)
+    w = torch.rand((T, K), generator=g)
+    _run_and_check(layer, x, ids, w, K, max_rows=32)
+
+
+def test_nvfp4_single_term_and_ep_window():
+    """NVFP4 with one activation term (plain NVFP4 activations, looser bar) and
+    an EP window of 16 of 32 experts."""
+    H, I, E, K, T = 2048, 256, 32, 4, 8
+    layer = O.make_nvfp4_layer(H, I, E, shared=False, seed=71)
+    x, _, _ = O.make_inputs(T, H, E, seed=71)
+    g = torch.Generator().manual_seed(71)
+    ids = _random_ids(T, K, E, g)
+    w = torch.rand((T, K), generator=g)
+    half = {k: (v[16:32] if k in ("w13", "w13_scale", "w2", "w2_scale", "w13_scale_2", "w2_scale_2") else v)
+            for k, v in layer.items()}
+    _run_and_check(half, x, ids, w, K, max_rows=8, expert_offset=16, local=16, router_experts=32)
+    _run_and_check(layer, x, ids, w, K, max_rows=8, act_terms=1)
 
 
 def test_experts_expert_parallel_window():

@@ -274,3 +274,35 @@ def test_moe_layer_oracle_shapes_and_linearity():
     assert out.shape == (T, H) and len(rows) == T * K and shared.shape == (T, H)
     out2, _, _ = O.moe_layer(x, ids, 2 * w, layer)
     assert torch.allclose(out2 - shared, 2 * (out - shared), rtol=1e-5, atol=1e-5)
+
+
+def test_nvfp4_codec_known_answers():
+    # scale rule: sf = e4m3(gs * amax / 6); a block whose amax maps to 6 * 448 / gs
+    # saturates at 448, and codes use E2M1's nearest-even grid
+    gs = 2.0
+    v = np.zeros((1, 16), np.float32)
+    v[0, :4] = [6.0, -3.0, 1.0, 0.75]  # amax 6 -> sf = e4m3(2) = 2.0, multiplier gs / sf = 1
+    q, s = O.nvfp4_quant(v, 1, 1.0 / gs)
+    assert O.e4m3_table()[s[0, 0, 0]] == 2.0
+    codes = [(q[0, 0, i // 2] >> (4 * (i % 2))) & 15 for i in range(4)]
+    assert [float(O.E2M1[c]) for c in codes] == [6.0, -3.0, 1.0, 1.0]  # 0.75 ties to even (1.0)
+    big = np.full((1, 16), 1e6, np.float32)
+    _, s = O.nvfp4_quant(big, 1, 1.0 / gs)
+    assert O.e4m3_table()[s[0, 0, 0]] == 448.0
+    # three terms converge on smooth data
+    x = np.random.RandomState(1).randn(8, 256).astype(np.float32)
+    errs = [np.abs(O.act_roundtrip(x, t, "nvfp4", 8.0 / 2688.0) - x).max() for t in (1, 2, 3)]
+    assert errs[0] > errs[1] > errs[2] and errs[2] < 1e-2 * np.abs(x).max()
+
+
+def test_nvfp4_weight_dequant_matches_definition():
+    L = O.make_nvfp4_layer(256, 256, 2, shared=False, seed=9)
+    W = O.dequant_nvfp4(L["w2"][1], L["w2_scale"][1], float(L["w2_scale_2"][1]))
+    codes, sc = L["w2"][1].numpy(), L["w2_scale"][1].numpy()
+    r, k = 5, 37
+    byte = codes[r, k // 2]
+    e2 = O.E2M1[(byte >> 4) if k % 2 else (byte & 15)]
+    want = np.float64(e2) * np.float64(O.e4m3_table()[sc[r, k // 16]]) * np.float64(L["w2_scale_2"][1])
+    assert abs(float(W[r, k]) - want) <= 1e-7 * max(1.0, abs(want))
+    vals = O.e4m3_table()[L["w13_scale"].numpy()]
+    assert vals.min() >= 0.5 and vals.max() <= 4.0
