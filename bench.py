@@ -41,6 +41,10 @@ import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 H, I, E, K, SCALE = 7168, 2048, 384, 8, 2.5
+CONFIGS = {  # BASELINE configs this bench runs: (hidden, intermediate, routed experts, weight format)
+    "2": (7168, 2048, 384, "mxfp4"),
+    "4": (6144, 2048, 256, "nvfp4"),
+}
 METRIC = "routed-MoE tokens/s per layer (us/layer = 1e3 * ms_per_step)"
 POOL = 64
 
@@ -50,7 +54,10 @@ def parse_args():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=3000)
     ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--tokens", type=int, default=8)
+    ap.add_argument("--tokens", type=int, default=None, help="default: 8 (config 2), 80 (config 4)")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="2",
+                    help="BASELINE config: 2 (MXFP4, hidden 7168, 384 + 1 experts) or 4 (NVFP4, hidden 6144, "
+                         "256 + 1 experts; TP x EP2 at N > 1)")
     ap.add_argument("--experts", type=int, default=384,
                     help="routed experts (384 = config 2; fewer only for small profiling cases)")
     ap.add_argument("--impl", choices=["mm", "reference"], default="mm")
@@ -73,10 +80,11 @@ def peaks():
         return 6650.0, "fallback"
 
 
-def expert_bytes(hidden, inter):
-    """Algorithmic bytes of one expert's MXFP4 weights: 3 matrices of H x I,
-    half a byte per element plus one E8M0 byte per 32 elements."""
-    return 3 * hidden * inter // 2 + 3 * hidden * inter // 32
+def expert_bytes(hidden, inter, block=32):
+    """Algorithmic bytes of one expert's FP4 weights: 3 matrices of H x I, half
+    a byte per element plus one scale byte per block (32: MXFP4's E8M0, 16:
+    NVFP4's E4M3; NVFP4's per-expert fp32 scale_2 is negligible)."""
+    return 3 * hidden * inter // 2 + 3 * hidden * inter // block
 
 
 # --------------------------------------------------------------------------- clocks
@@ -136,32 +144,83 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------------- layer
-def build_layer(rank, world, tokens, device):
+def partition(world, fmt):
+    """(tp, ep) of the bench's layer over `world` ranks: config 2 is TP-N on the
+    intermediate; config 4 is TP (N/2) x EP2 at N >= 2 (BASELINE: TP4 x EP2 at 8)."""
+    if fmt == "nvfp4" and world >= 2:
+        return world // 2, 2
+    return world, 1
+
+
+def build_layer(rank, world, tokens, device, fmt="mxfp4"):
+    """This rank's part of the seeded random layer: (moe, routed weights,
+    shared weights or None, router, bias, x pool, info). Rank r holds EP
+    window r // tp with the TP slice r % tp of the intermediate; the shared
+    expert is TP-split within EP group 0."""
     import megamoe
 
-    ir = I // world
+    tp, ep = partition(world, fmt)
+    ep_rank = rank // tp
+    local = E // ep
+    offset = ep_rank * local
+    ir = I // tp
     g = torch.Generator(device=device).manual_seed(1000 + rank)
 
     def rnd(shape, lo, hi):
         return torch.randint(lo, hi + 1, shape, dtype=torch.uint8, device=device, generator=g)
 
-    w = [rnd((E, 2 * ir, H // 2), 0, 255), rnd((E, 2 * ir, H // 32), 117, 121),
-         rnd((E, H, ir // 2), 0, 255), rnd((E, H, ir // 32), 117, 121)]
-    shared = [rnd((1, 2 * ir, H // 2), 0, 255), rnd((1, 2 * ir, H // 32), 117, 121),
-              rnd((1, H, ir // 2), 0, 255), rnd((1, H, ir // 32), 117, 121)]
-    moe = megamoe.RoutedMoE(*w, K, max(tokens, 8), shared=shared)
+    has_shared = ep_rank == 0
+    extra = {}
+    if fmt == "mxfp4":
+        w = [rnd((local, 2 * ir, H // 2), 0, 255), rnd((local, 2 * ir, H // 32), 117, 121),
+             rnd((local, H, ir // 2), 0, 255), rnd((local, H, ir // 32), 117, 121)]
+        shared = [rnd((1, 2 * ir, H // 2), 0, 255), rnd((1, 2 * ir, H // 32), 117, 121),
+                  rnd((1, H, ir // 2), 0, 255), rnd((1, H, ir // 32), 117, 121)] if has_shared else None
+    else:
+        # NVFP4: E2M1 codes uniform, E4M3 scales of values ~U[0.5, 4] per 16,
+        # per-expert fp32 scale_2 = 2^-8 (1 + u/4), static input scales
+        def sf(shape):
+            v = 0.5 + 3.5 * torch.rand(shape, device=device, generator=g)
+            return v.to(torch.float8_e4m3fn).view(torch.uint8)
+
+        def s2(n):
+            return (2.0 ** -8 * (1.0 + 0.25 * torch.rand((n,), device=device, generator=g))).float()
+
+        w = [rnd((local, 2 * ir, H // 2), 0, 255), sf((local, 2 * ir, H // 16)),
+             rnd((local, H, ir // 2), 0, 255), sf((local, H, ir // 16))]
+        w13_s2, w2_s2 = s2(local), s2(local)
+        shared = [rnd((1, 2 * ir, H // 2), 0, 255), sf((1, 2 * ir, H // 16)), rnd((1, H, ir // 2), 0, 255),
+                  sf((1, H, ir // 16)), s2(1), s2(1)] if has_shared else None
+        # FC2's input scale from twice the largest |h| of 8 rows through expert 0
+        lut = torch.tensor([0, .5, 1, 1.5, 2, 3, 4, 6, -0., -.5, -1, -1.5, -2, -3, -4, -6], device=device)
+        codes, scales = w[0][0], w[1][0]
+        vals = torch.stack([lut[(codes & 15).long()], lut[(codes >> 4).long()]], -1).reshape(2 * ir, H)
+        sc = scales.view(torch.float8_e4m3fn).float().repeat_interleave(16, dim=1)
+        w13_0 = vals * sc * w13_s2[0]
+        xs0 = torch.randn((8, H), device=device, generator=g)
+        gu = xs0 @ w13_0.T
+        hh = gu[:, ir:] * (gu[:, :ir] * torch.sigmoid(gu[:, :ir]))
+        fc2 = 2.0 * float(hh.abs().max()) / (6.0 * 448.0)
+        extra = dict(weight_format="nvfp4", w13_scale_2=w13_s2, w2_scale_2=w2_s2,
+                     input_scale=(8.0 / (6.0 * 448.0), fc2))
+    moe = megamoe.RoutedMoE(*w, K, max(tokens, 8), router_experts=E, expert_offset=offset, shared=shared,
+                            **extra)
     gx = torch.Generator(device=device).manual_seed(7)  # identical on every rank: replicated routing
     router = (torch.randn((E, H), device=device, generator=gx) * 0.02).to(torch.bfloat16)
     bias = (torch.randn((E,), device=device, generator=gx) * 0.01).float()
     xs = torch.randn((POOL, tokens, H), device=device, generator=gx).to(torch.bfloat16)
-    return moe, w, shared, router, bias, xs
+    info = dict(tp=tp, ep=ep, offset=offset, local=local, ir=ir, has_shared=has_shared,
+                block=16 if fmt == "nvfp4" else 32)
+    return moe, w, shared, router, bias, xs, info
 
 
 def run_mm(args):
     import megamoe
 
-    global E
-    E = args.experts
+    global H, I, E
+    H, I, E, fmt = CONFIGS[args.config]
+    if args.config == "2":
+        E = args.experts
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -174,8 +233,8 @@ def run_mm(args):
         import torch.distributed as dist
 
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
-    T = args.tokens
-    moe, w, shared, router, bias, xs = build_layer(rank, world, T, dev)
+    T = args.tokens if args.tokens is not None else (80 if args.config == "4" else 8)
+    moe, w, shared, router, bias, xs, info = build_layer(rank, world, T, dev, fmt)
     bufs = {}
     out_buf = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
     peer = world > 1 and args.combine == "peer"
@@ -225,13 +284,20 @@ def run_mm(args):
 
     # distinct local experts per step (seeded routings, averaged over the pool)
     distinct = []
+    lo, hi = info["offset"], info["offset"] + info["local"]
     for i in range(POOL):
         step(xs[i])
-        distinct.append(int(torch.unique(bufs["ids"]).numel()))
+        ids = bufs["ids"]
+        distinct.append(int(torch.unique(ids[(ids >= lo) & (ids < hi)]).numel()))
     torch.cuda.synchronize()
     d_mean = float(np.mean(distinct))
-    eb = expert_bytes(H, I // world)
-    layer_bytes = (d_mean + 1) * eb + E * H * 2
+    eb = expert_bytes(H, info["ir"], info["block"])
+    n_shared = 1 if info["has_shared"] else 0
+    layer_bytes = (d_mean + n_shared) * eb + E * H * 2
+    if dist is not None:  # the roofline of a sharded layer is its busiest rank's bytes
+        t = torch.tensor([layer_bytes], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        layer_bytes = float(t.item())
 
     # dominant kernel alone: the expert kernel relaunched on the last step's tables
     last_d = distinct[-1]
@@ -246,7 +312,7 @@ def run_mm(args):
     torch.cuda.synchronize()
     k_ms = float(np.mean([a.elapsed_time(b) for a, b in evs]))
     moe.check()
-    k_bytes = (last_d + 1) * eb
+    k_bytes = (last_d + n_shared) * eb
     peak, peak_kind = peaks()
     achieved = k_bytes / (k_ms / 1e3) / 1e9
 
@@ -288,7 +354,16 @@ def run_mm(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(w, shared, router, bias, xs, T)
+        cpu = cpu_baseline(w, shared, router, bias, xs, T, moe if fmt == "nvfp4" else None,
+                           max_experts=None if args.config == "2" else 6)
+    fmt_name = "MXFP4" if fmt == "mxfp4" else "NVFP4"
+    if args.config == "2":
+        par = f"tp{world}" if world > 1 else "single"
+        split = f" (TP{world}: {I // world} per rank)" if world > 1 else ""
+    else:
+        par = f"tp{info['tp']}xep{info['ep']}" if world > 1 else "single"
+        split = (f" (TP{info['tp']} x EP{info['ep']}: {info['local']} experts x {info['ir']} per rank)"
+                 if world > 1 else "")
 
     line = {
         "metric": METRIC,
@@ -302,15 +377,16 @@ def run_mm(args):
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
-        "dtype": "mxfp4 weights x mxfp8(hi+lo) activations, fp32 accumulate",
-        "data": "synthetic (seeded random MXFP4 weights, bf16 x ~ N(0,1))",
+        "dtype": f"{fmt} weights x {fmt}(3-term) activations, fp32 accumulate",
+        "data": f"synthetic (seeded random {fmt_name} weights, bf16 x ~ N(0,1))",
         "config": {
-            "workload": f"BASELINE config 2: one routed-MoE layer, hidden {H}, {E} routed + 1 shared experts, "
-                        f"intermediate {I}" + (f" (TP{world}: {I // world} per rank)" if world > 1 else "")
-                        + f", sigmoid+bias top-{K}, scale {SCALE}, MXFP4, {T} tokens",
+            "workload": f"BASELINE config {args.config}: one routed-MoE layer, hidden {H}, {E} routed + 1 shared "
+                        f"experts, intermediate {I}{split}, sigmoid+bias top-{K}, scale {SCALE}, {fmt_name}, "
+                        f"{T} tokens",
             "tokens": T,
-            "parallelism": f"tp{world}" if world > 1 else "single",
-            "l2": "inputs larger than L2 (~1.4 GB of expert weights per step, 64 distinct token batches)",
+            "parallelism": par,
+            "l2": f"inputs larger than L2 (~{layer_bytes / 1e9:.2f} GB of expert weights per step, "
+                  f"{POOL} distinct token batches)",
             "launch": "eager, PDL-chained launches",
             "combine": ("fused combine + all-reduce over NVLink peer memory" if peer else
                         "NCCL all-reduce of fp32 partials + round" if world > 1 else "combine"),
@@ -374,7 +450,7 @@ def run_stack(args):
         import torch.distributed as dist
 
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
-    T, L = args.tokens, args.layers
+    T, L = (args.tokens if args.tokens is not None else 8), args.layers
     per = E // ep
     offset = rank * per
     moes, routers, biases, gammas = [], [], [], []
@@ -546,24 +622,34 @@ def run_stack(args):
 
 
 # --------------------------------------------------------------------------- CPU legs
-def _cpu_layer_step(x_bf16, router_bf16, bias, experts_w, shared_w, oracle):
+def _cpu_layer_step(x_bf16, router_bf16, bias, experts_w, shared_w, oracle, max_experts=None):
+    """One layer on the CPU oracle: routing, then the activated experts (all of
+    them, or the first max_experts) and the shared expert. Returns (seconds of
+    routing, seconds per expert MLP, distinct experts)."""
+    t0 = time.perf_counter()
     logits = oracle.router_gemv(oracle.bf16_bits(x_bf16), oracle.bf16_bits(router_bf16))
     w, ids = oracle.gate_topk(logits, bias.numpy(), K, scale=SCALE)
+    t1 = time.perf_counter()
     x = x_bf16.float()
     out = torch.zeros_like(x)
-    for e in sorted(set(ids.flatten().tolist())):
+    experts = sorted(set(ids.flatten().tolist()))
+    ran = experts if max_experts is None else experts[:max_experts]
+    for e in ran:
         toks = [t for t in range(ids.shape[0]) if e in ids[t]]
         ws = [float(w[t][list(ids[t]).index(e)]) for t in toks]
-        y = oracle.expert_mlp(x[toks], *experts_w(e), None, "exact")
+        y = oracle.expert_mlp(x[toks], *experts_w(e))
         for j, t in enumerate(toks):
             out[t] += ws[j] * y[j]
-    out += oracle.expert_mlp(x, *shared_w, None, "exact")
-    return out, ids
+    out += oracle.expert_mlp(x, *shared_w)
+    t2 = time.perf_counter()
+    return t1 - t0, (t2 - t1) / (len(ran) + 1), len(experts)
 
 
-def cpu_baseline(w, shared, router, bias, xs, T):
-    """The oracle port timed on this host's cores: one full layer step of the
-    same workload (all activated experts + shared), after one warm-up step."""
+def cpu_baseline(w, shared, router, bias, xs, T, nv_moe=None, max_experts=None):
+    """The oracle port timed on this host's cores on the same workload, after
+    one warm-up step: a full layer step (every activated expert + shared), or
+    with max_experts a bounded sample whose layer time is routing + (distinct
+    + 1) x the mean expert time."""
     from oracle import oracle
 
     threads = torch.get_num_threads()
@@ -573,16 +659,28 @@ def cpu_baseline(w, shared, router, bias, xs, T):
     for xi in xc:
         logits = oracle.router_gemv(oracle.bf16_bits(xi), oracle.bf16_bits(router_c))
         _, ids = oracle.gate_topk(logits, bias_c.numpy(), K, scale=SCALE)
-        needed |= set(ids.flatten().tolist())
-    cache = {e: tuple(t[e].cpu() for t in w) for e in needed}
-    sh = tuple(t[0].cpu() for t in shared)
-    _cpu_layer_step(xc[0], router_c, bias_c, lambda e: cache[e], sh, oracle)  # warm-up
-    t0 = time.perf_counter()
-    _cpu_layer_step(xc[1], router_c, bias_c, lambda e: cache[e], sh, oracle)
-    dt = time.perf_counter() - t0
-    return {"value": T / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"1 full layer step ({T} tokens, every activated expert + shared) after 1 warm-up; "
-                      f"{dt:.1f} s"}
+        ex = sorted(set(ids.flatten().tolist()))
+        needed |= set(ex if max_experts is None else ex[:max_experts])
+    if nv_moe is None:
+        cache = {e: tuple(t[e].cpu() for t in w) + (None, "exact") for e in needed}
+        sh = tuple(t[0].cpu() for t in shared) + (None, "exact")
+    else:  # NVFP4: scale_2 per expert and the layer's static input scales
+        s13, s2 = nv_moe.w13_scale_2.cpu(), nv_moe.w2_scale_2.cpu()
+        ins = nv_moe.input_scale
+        cache = {e: tuple(t[e].cpu() for t in w) + (None, "exact", 3, (float(s13[e]), float(s2[e]), ins))
+                 for e in needed}
+        sh = tuple(t[0].cpu() for t in shared[:4]) + (None, "exact", 3,
+                                                       (float(shared[4][0]), float(shared[5][0]), ins))
+    _cpu_layer_step(xc[0], router_c, bias_c, lambda e: cache[e], sh, oracle, max_experts)  # warm-up
+    route_s, per_expert_s, d = _cpu_layer_step(xc[1], router_c, bias_c, lambda e: cache[e], sh, oracle,
+                                               max_experts)
+    layer_s = route_s + (d + 1) * per_expert_s
+    sample = (f"1 full layer step ({T} tokens, every activated expert + shared) after 1 warm-up"
+              if max_experts is None else
+              f"routing + {max_experts} of {d} activated experts + shared ({T} tokens) after 1 warm-up; layer "
+              f"time = routing + (distinct + 1) x mean expert time")
+    return {"value": T / layer_s, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{sample}; {layer_s:.1f} s per layer"}
 
 
 def run_reference(args):
@@ -598,7 +696,7 @@ def run_reference(args):
         return
     torch.set_num_threads(os.cpu_count() or 1)
     threads = torch.get_num_threads()
-    T = args.tokens
+    T = args.tokens if args.tokens is not None else 8
     g = torch.Generator().manual_seed(1000)
 
     def rnd(shape, lo, hi):

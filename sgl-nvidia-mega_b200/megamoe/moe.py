@@ -133,8 +133,10 @@ class RoutedMoE:
         desc.device = self.device.index if self.device.index is not None else torch.cuda.current_device()
         desc.routed = _lib.MMExpertWeights(*(t.data_ptr() for t in (w13, w13_scale, w2, w2_scale)),
                                            _ptr(w13_scale_2) if nv else None, _ptr(w2_scale_2) if nv else None)
+        self.w13_scale_2, self.w2_scale_2 = (w13_scale_2, w2_scale_2) if nv else (None, None)
+        self.input_scale = (float(input_scale[0]), float(input_scale[1])) if nv else None
         if nv:
-            desc.input_scale[0], desc.input_scale[1] = float(input_scale[0]), float(input_scale[1])
+            desc.input_scale[0], desc.input_scale[1] = self.input_scale
             keep += [w13_scale_2, w2_scale_2]
         self.has_shared = shared is not None
         if shared is not None:

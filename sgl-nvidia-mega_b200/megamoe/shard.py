@@ -19,9 +19,10 @@ import torch
 
 
 def tp_slice(w13: torch.Tensor, w13_scale: torch.Tensor, w2: torch.Tensor, w2_scale: torch.Tensor,
-             rank: int, world: int) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
-    """Rank ``rank``'s TP slice of canonical [n, 2I, H/2] / [n, 2I, H/32] /
-    [n, H, I/2] / [n, H, I/32] weights (contiguous copies)."""
+             rank: int, world: int, block: int = 32) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Rank ``rank``'s TP slice of canonical [n, 2I, H/2] / [n, 2I, H/block] /
+    [n, H, I/2] / [n, H, I/block] weights (contiguous copies); block 32 for
+    MXFP4, 16 for NVFP4 (whose per-expert scale_2 is not sliced)."""
     two_i = w13.shape[1]
     inter = two_i // 2
     if inter % world or (inter // world) % 64:
@@ -31,7 +32,7 @@ def tp_slice(w13: torch.Tensor, w13_scale: torch.Tensor, w2: torch.Tensor, w2_sc
     s13 = torch.cat([w13[:, g0:g0 + part], w13[:, u0:u0 + part]], dim=1).contiguous()
     s13s = torch.cat([w13_scale[:, g0:g0 + part], w13_scale[:, u0:u0 + part]], dim=1).contiguous()
     s2 = w2[:, :, rank * part // 2:(rank + 1) * part // 2].contiguous()
-    s2s = w2_scale[:, :, rank * part // 32:(rank + 1) * part // 32].contiguous()
+    s2s = w2_scale[:, :, rank * part // block:(rank + 1) * part // block].contiguous()
     return s13, s13s, s2, s2s
 
 
