@@ -52,7 +52,8 @@ extern "C" {
 /* ---- routing score functions ------------------------------------------- */
 #define MM_SCORE_SIGMOID 0      /* s = 1/(1+exp(-x)), key = s + bias            */
 #define MM_SCORE_SOFTMAX 1      /* key = x + bias, w = softmax over the top-k   */
-#define MM_SCORE_SQRTSOFTPLUS 2 /* s = sqrt(log1p(exp(x))), key = s + bias     */
+#define MM_SCORE_SQRTSOFTPLUS 2 /* s = sqrt(log1p(exp(x))) (x above 20: sqrt x),
+                                   key = s + bias, w = s / sum (DeepSeek-V4.1) */
 
 /* ---- expert weight formats ---------------------------------------------- */
 #define MM_WEIGHT_MXFP4 0 /* E2M1 codes + one E8M0 scale per 32 along K      */
@@ -84,7 +85,9 @@ typedef struct mm_layer_desc {
   int32_t intermediate;   /* I (this rank's slice): multiple of 256                */
   int32_t experts;        /* local routed experts (this rank's window)             */
   int32_t router_experts; /* experts the router scores (>= expert_offset+experts)  */
-  int32_t expert_offset;  /* router id of local expert 0 (expert parallelism)      */
+  int32_t expert_offset;  /* router id of local expert 0 (expert parallelism);
+                             -1 - g (g = 0, 1): balanced dealing to group g of two
+                             (the rank holds every expert; route.cuh:39-46)       */
   int32_t top_k;          /* 1..16                                                 */
   int32_t max_tokens;     /* largest T a call may pass: 1..256                     */
   int32_t weight_format;  /* MM_WEIGHT_MXFP4 or MM_WEIGHT_NVFP4                   */
@@ -118,6 +121,12 @@ typedef struct mm_gate_args {
   float renorm_eps;          /* > 0: divide by sum + eps; else by the guarded sum */
   float *weights;            /* out [T, top_k] fp32                               */
   int32_t *ids;              /* out [T, top_k] int32 (router ids)                 */
+  /* vision routing (gate_topk.cuh:290-346): a valid row whose input token is
+   * alt_token_id ranks with bias_alt (NULL: bias) instead of bias */
+  const float *bias_alt;     /* [router_experts] fp32 or NULL                     */
+  const void *input_ids;     /* [T] int32 (int64 when input_ids64) or NULL        */
+  int32_t input_ids64;
+  int64_t alt_token_id;
 } mm_gate_args;
 
 /* Sizes of the caller-owned buffers of a layer call. */
@@ -155,6 +164,10 @@ typedef struct mm_forward_args {
   mm_comm *comm;            /* non-NULL: out receives the group's all-reduced
                                output (mm_finalize_allreduce) instead of this
                                rank's own combine; partial must then be NULL   */
+  const float *bias_alt;    /* vision routing, as in mm_gate_args              */
+  const void *input_ids;
+  int32_t input_ids64;
+  int64_t alt_token_id;
   const uint16_t *residual; /* non-NULL (needs comm): the hop epilogue of
                                mm_finalize_allreduce_norm; out receives the
                                normalized output (NULL: none)                  */
@@ -181,7 +194,9 @@ int mm_gate_topk(const mm_gate_args *args, int32_t tokens, int32_t router_expert
 int64_t mm_route_words(int32_t tokens, int32_t top_k, int32_t experts);
 
 /* Route record + slot -> row map from top-k ids, bit for bit the reference's
- * (route.cuh:6-46, route_wide.cu:1-14). expert_offset >= 0. T <= 256. */
+ * (route.cuh:6-46, route_wide.cu:1-14). expert_offset >= 0: the router id of
+ * local expert 0; -1 / -2: balanced dealing to group 0 / 1 (experts = all the
+ * router's experts). T <= 256. */
 int mm_route(const int32_t *ids, int32_t *permuted, int32_t *record, int32_t tokens,
              int32_t top_k, int32_t experts, int32_t expert_offset, void *stream);
 

@@ -93,6 +93,47 @@ float or_det_exp(float x) {
 
 float or_sigmoid(float x) { return 1.0f / (1.0f + or_det_exp(-x)); }
 
+/* log(u), u >= 1 finite: u = m 2^k, m in [sqrt(1/2), sqrt(2)), log u = k ln2 +
+ * 2 atanh(f / (2 + f)), f = m - 1, atanh by its odd series to s^11 (Horner in
+ * z = s^2, fma); the kernel's sequence (mm_numerics.cuh det_log). */
+float or_det_log(float u) {
+  const uint32_t bits = f2u(u);
+  int k = (int)((bits >> 23) & 0xffu) - 127;
+  float m = u2f((bits & 0x7fffffu) | 0x3f800000u);
+  if (m > 0x1.6a09e6p+0f) { m = m * 0.5f; k += 1; }
+  const float f = m - 1.0f;
+  const float s = f / (2.0f + f);
+  const float z = s * s;
+  float q = 0x1.745d18p-4f;
+  q = fmaf(q, z, 0x1.c71c72p-4f);
+  q = fmaf(q, z, 0x1.24924ap-3f);
+  q = fmaf(q, z, 0x1.99999ap-3f);
+  q = fmaf(q, z, 0x1.555556p-2f);
+  q = fmaf(q, z, 1.0f);
+  const float lm = (s + s) * q;
+  const float kf = (float)k;
+  return fmaf(kf, 0x1.62e400p-1f, fmaf(kf, 0x1.7f7d1cp-20f, lm));
+}
+
+/* log1p(y), y >= 0: Goldberg's log(1 + y) * y / ((1 + y) - 1). */
+float or_det_log1p(float y) {
+  const float u = 1.0f + y;
+  if (u == 1.0f) return y;
+  return or_det_log(u) * (y / (u - 1.0f));
+}
+
+/* sqrt(softplus(x)) (deepseek_v41/sm103/moe/src/gate_topk.cuh:99-104): x above
+ * 20, else log1p(exp(x)); IEEE square root. */
+float or_sqrtsoftplus(float x) {
+  if (x != x) return x;
+  const float sp = x > 20.0f ? x : or_det_log1p(or_det_exp(x));
+  return sqrtf(sp);
+}
+
+static float or_score(int score_func, float l) {
+  return score_func == 0 ? or_sigmoid(l) : score_func == 2 ? or_sqrtsoftplus(l) : l;
+}
+
 /* Order-preserving key of score + bias: -0 as +0 (gate_topk.cuh:129-145), NaN
  * below every number (glm5_3/sm103/primitives/ptx_tc.py:393-402). */
 uint32_t or_routing_key(float v) {
@@ -105,17 +146,22 @@ uint32_t or_routing_key(float v) {
  * Router top-k of every row (reference: gate_topk.cuh:101-303 and
  * glm5_3/sm103/moe/routing.py:3-11,32-70; softmax over the selected logits as
  * qwen3_5/sm103/moe/src/route_topk.cu:1-6). score_func 0: s = sigmoid(logit),
- * key = s + bias; 1: s = logit, key = logit + bias, weights = softmax over the
- * k selected logits. Selection: k times the largest key, the lowest expert id on
+ * key = s + bias; 2: s = sqrt(softplus(logit)), key = s + bias (DeepSeek-V4.1,
+ * gate_topk.cuh:99-104); 1: s = logit, key = logit + bias, weights = softmax
+ * over the k selected logits. Selection: k times the largest key, the lowest expert id on
  * ties; slot order = selection order. Weights: s / (sum + eps) when eps > 0,
  * else s / (sum > 0 ? sum : 1), sum in slot order, times the routed scale;
  * renormalize 0: s * scale. Rows >= num_valid: id -1, weight 0.
  * ------------------------------------------------------------------------- */
-void or_gate_topk(const float *logits, const float *bias, int num_valid, int score_func,
+void or_gate_topk(const float *logits, const float *bias_main, int num_valid, int score_func,
                   int renormalize, float scale, float eps, int T, int E, int K, float *weights,
-                  int *ids) {
+                  int *ids, const float *bias_alt, const int64_t *input_ids, int64_t alt_token_id) {
   for (int t = 0; t < T; ++t) {
     const float *l = logits + (size_t)t * E;
+    /* vision routing (gate_topk.cuh:290-346): a valid row whose token is
+     * alt_token_id ranks with bias_alt (bias when bias_alt is NULL) */
+    const int alt = input_ids && t < num_valid && input_ids[t] == alt_token_id;
+    const float *bias = alt && bias_alt ? bias_alt : bias_main;
     int sel[64];
     unsigned char taken[4096];
     memset(taken, 0, (size_t)E);
@@ -124,7 +170,7 @@ void or_gate_topk(const float *logits, const float *bias, int num_valid, int sco
       uint32_t bkey = 0;
       for (int e = 0; e < E; ++e) {
         if (taken[e]) continue;
-        const float s = score_func == 0 ? or_sigmoid(l[e]) : l[e];
+        const float s = or_score(score_func, l[e]);
         const uint32_t key = or_routing_key(s + (bias ? bias[e] : 0.0f));
         if (best < 0 || key > bkey) { best = e; bkey = key; }
       }
@@ -140,7 +186,7 @@ void or_gate_topk(const float *logits, const float *bias, int num_valid, int sco
       for (int k = 0; k < K; ++k) w[k] = (w[k] / sum) * scale;
     } else {
       float sum = 0.0f;
-      for (int k = 0; k < K; ++k) { w[k] = or_sigmoid(l[sel[k]]); sum = sum + w[k]; }
+      for (int k = 0; k < K; ++k) { w[k] = or_score(score_func, l[sel[k]]); sum = sum + w[k]; }
       if (renormalize) {
         const float norm = eps > 0.0f ? sum + eps : (sum > 0.0f ? sum : 1.0f);
         for (int k = 0; k < K; ++k) w[k] = (w[k] / norm) * scale;
@@ -180,9 +226,22 @@ void or_route(const int *ids, int *permuted, int *record, int T, int K, int expe
   memset(record, 0, sizeof(int) * (size_t)or_route_words(T, K, experts));
   static int count[4096], first[4096];
   for (int e = 0; e < experts; ++e) count[e] = 0;
+  /* balanced dealing (route.cuh:39-46, route_wide.cu:87-110): a negative
+   * offset selects group -1 - offset of two; ids are global, and of the step's
+   * distinct experts in id order the k-th belongs to group k % 2 */
+  const int deal = offset < 0, group = deal ? -1 - offset : 0;
+  if (deal) offset = 0;
   for (int s = 0; s < slots; ++s) {
     const int e = ids[s] - offset;
     if (e >= 0 && e < experts) count[e]++;
+  }
+  if (deal) {
+    int rank = 0;
+    for (int e = 0; e < experts; ++e) {
+      if (!count[e]) continue;
+      if ((rank & 1) != group) count[e] = 0;
+      rank++;
+    }
   }
   int tiles = 0;
   for (int e = 0; e < experts; ++e) { first[e] = tiles; tiles += (count[e] + 7) / 8; }
@@ -190,7 +249,7 @@ void or_route(const int *ids, int *permuted, int *record, int T, int K, int expe
   record[1] = tiles;
   for (int s = 0; s < slots; ++s) {
     const int t = s / K, e = ids[s] - offset;
-    if (e < 0 || e >= experts) { permuted[s] = -1; continue; }
+    if (e < 0 || e >= experts || count[e] == 0) { permuted[s] = -1; continue; }
     int rank = 0;  /* earlier rows that chose e (top-k ids of a row are distinct) */
     for (int s2 = 0; s2 < slots; ++s2)
       if (s2 / K < t && ids[s2] - offset == e) rank++;

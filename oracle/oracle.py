@@ -63,7 +63,7 @@ def lib() -> ctypes.CDLL:
         h.or_nv4_scale_code.argtypes = [c_float, c_float]
         h.or_route_words.restype = c_int
         h.or_gate_topk.argtypes = [c_void_p, c_void_p, c_int, c_int, c_int, c_float, c_float, c_int, c_int, c_int,
-                                   c_void_p, c_void_p]
+                                   c_void_p, c_void_p, c_void_p, c_void_p, ctypes.c_int64]
         _lib = h
     return _lib
 
@@ -85,15 +85,20 @@ def router_gemv(x_bf16: np.ndarray, w_bf16: np.ndarray) -> np.ndarray:
 
 
 def gate_topk(logits: np.ndarray, bias: Optional[np.ndarray], top_k: int, *, score: str = "sigmoid",
-              renormalize: bool = True, scale: float = 1.0, eps: float = 0.0, num_valid: Optional[int] = None):
+              renormalize: bool = True, scale: float = 1.0, eps: float = 0.0, num_valid: Optional[int] = None,
+              bias_alt: Optional[np.ndarray] = None, input_ids: Optional[np.ndarray] = None,
+              alt_token_id: int = -1):
     logits = np.ascontiguousarray(logits, dtype=np.float32)
     T, E = logits.shape
     b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+    ba = None if bias_alt is None else np.ascontiguousarray(bias_alt, dtype=np.float32)
+    tok = None if input_ids is None else np.ascontiguousarray(input_ids, dtype=np.int64)
     w = np.empty((T, top_k), dtype=np.float32)
     ids = np.empty((T, top_k), dtype=np.int32)
-    sf = {"sigmoid": 0, "softmax": 1}[score]
+    sf = {"sigmoid": 0, "softmax": 1, "sqrtsoftplus": 2}[score]
     lib().or_gate_topk(_p(logits), _p(b), T if num_valid is None else int(num_valid), sf, int(renormalize),
-                       c_float(scale), c_float(eps), T, E, top_k, _p(w), _p(ids))
+                       c_float(scale), c_float(eps), T, E, top_k, _p(w), _p(ids), _p(ba), _p(tok),
+                       ctypes.c_int64(alt_token_id))
     return w, ids
 
 
@@ -312,7 +317,7 @@ def expert_mlp(x: torch.Tensor, w13: torch.Tensor, s13: torch.Tensor, w2: torch.
 
 
 def moe_layer(x_bf16: torch.Tensor, ids: np.ndarray, weights: np.ndarray, layer: dict, *, numerics: str = "exact",
-              terms: int = 3, expert_offset: int = 0, local_experts: Optional[int] = None):
+              terms: int = 3, expert_offset: int = 0, local_experts: Optional[int] = None, deal_group: int = -1):
     """Oracle of one MoE layer given routing. Returns (out fp32 [T, H] before
     bf16 rounding of the final sum, per-slot rows fp32 {(t, k): [H]}, shared
     fp32 [T, H] or None). Weights are CPU uint8 tensors in the canonical layout."""
@@ -323,10 +328,14 @@ def moe_layer(x_bf16: torch.Tensor, ids: np.ndarray, weights: np.ndarray, layer:
     clamp = layer.get("clamp")
     rows = {}
     by_expert = {}
+    dealt = None
+    if deal_group >= 0:  # balanced dealing: the step's distinct experts, k-th to group k % 2
+        present = sorted({int(i) for i in ids.flatten() if 0 <= int(i) < E})
+        dealt = {e for r, e in enumerate(present) if r % 2 == deal_group}
     for t in range(T):
         for k in range(ids.shape[1]):
             e = int(ids[t, k]) - expert_offset
-            if 0 <= e < E:
+            if 0 <= e < E and (dealt is None or e in dealt):
                 by_expert.setdefault(e, []).append((t, k))
     nvl = layer.get("fmt") == "nvfp4"
     ins = layer.get("input_scale")

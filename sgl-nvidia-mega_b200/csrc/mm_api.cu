@@ -169,8 +169,10 @@ static int check_gate(const mm_gate_args *a, int tokens, int E, int K) {
   if (tokens < 1 || tokens > kMaxTokens) return fail(MM_ERR_INVALID, "gate: tokens %d outside 1..%d", tokens, kMaxTokens);
   if (E < 1 || E > kMaxRouterExperts) return fail(MM_ERR_INVALID, "gate: %d experts outside 1..%d", E, kMaxRouterExperts);
   if (K < 1 || K > kMaxTopK || K > E) return fail(MM_ERR_INVALID, "gate: top_k %d outside 1..min(16, experts)", K);
-  if (a->score_func != MM_SCORE_SIGMOID && a->score_func != MM_SCORE_SOFTMAX)
-    return fail(MM_ERR_UNSUPPORTED, "gate: score function %d is not built (sigmoid, softmax)", a->score_func);
+  if (a->score_func != MM_SCORE_SIGMOID && a->score_func != MM_SCORE_SOFTMAX &&
+      a->score_func != MM_SCORE_SQRTSOFTPLUS)
+    return fail(MM_ERR_UNSUPPORTED, "gate: score function %d is not built (sigmoid, softmax, sqrtsoftplus)",
+                a->score_func);
   return MM_OK;
 }
 
@@ -187,6 +189,10 @@ static GateArgs gate_args(const mm_gate_args *a, int E, int K) {
   g.top_k = K;
   g.weights_out = a->weights;
   g.ids_out = a->ids;
+  g.bias_alt = a->bias_alt;
+  g.input_ids = a->input_ids;
+  g.input_ids64 = a->input_ids64;
+  g.alt_token_id = a->alt_token_id;
   return g;
 }
 
@@ -209,7 +215,8 @@ int mm_route(const int32_t *ids, int32_t *permuted, int32_t *record, int32_t tok
   if (tokens < 1 || tokens > kMaxTokens) return fail(MM_ERR_INVALID, "mm_route: tokens %d outside 1..%d", tokens, kMaxTokens);
   if (top_k < 1 || top_k > kMaxTopK) return fail(MM_ERR_INVALID, "mm_route: top_k %d outside 1..%d", top_k, kMaxTopK);
   if (experts < 1 || experts > kMaxRouterExperts) return fail(MM_ERR_INVALID, "mm_route: %d experts outside 1..%d", experts, kMaxRouterExperts);
-  if (expert_offset < 0) return fail(MM_ERR_UNSUPPORTED, "mm_route: balanced dealing (negative expert_offset) is not built");
+  if (expert_offset < -2)
+    return fail(MM_ERR_INVALID, "mm_route: expert_offset %d (balanced dealing: -1 or -2)", expert_offset);
   RouteArgs r = {};
   r.ids = ids;
   r.permuted = permuted;
@@ -275,9 +282,14 @@ int mm_layer_create(const mm_layer_desc *desc, mm_layer **out) {
   if (d.experts < 1 || d.experts > kMaxRouterExperts) return fail(MM_ERR_INVALID, "experts %d outside 1..%d", d.experts, kMaxRouterExperts);
   if (d.router_experts < d.experts || d.router_experts > kMaxRouterExperts)
     return fail(MM_ERR_INVALID, "router_experts %d outside experts..%d", d.router_experts, kMaxRouterExperts);
-  if (d.expert_offset < 0 || d.expert_offset + d.experts > d.router_experts)
+  if (d.expert_offset < 0) {  // balanced dealing: the rank holds every expert
+    if (d.expert_offset < -2 || d.experts != d.router_experts)
+      return fail(MM_ERR_INVALID, "balanced dealing (expert_offset %d) needs group -1 or -2 and all %d experts",
+                  d.expert_offset, d.router_experts);
+  } else if (d.expert_offset + d.experts > d.router_experts) {
     return fail(MM_ERR_INVALID, "local experts [%d, %d) outside the router's %d", d.expert_offset,
                 d.expert_offset + d.experts, d.router_experts);
+  }
   if (d.top_k < 1 || d.top_k > kMaxTopK) return fail(MM_ERR_INVALID, "top_k %d outside 1..%d", d.top_k, kMaxTopK);
   if (d.max_tokens < 1 || d.max_tokens > kMaxTokens) return fail(MM_ERR_INVALID, "max_tokens %d outside 1..%d", d.max_tokens, kMaxTokens);
   if (d.weight_format != MM_WEIGHT_MXFP4 && d.weight_format != MM_WEIGHT_NVFP4)
@@ -621,6 +633,10 @@ int mm_layer_forward(mm_layer *L, const mm_forward_args *a, void *stream) {
   g.renormalize = a->renormalize;
   g.routed_scaling = a->routed_scaling;
   g.renorm_eps = a->renorm_eps;
+  g.bias_alt = a->bias_alt;
+  g.input_ids = a->input_ids;
+  g.input_ids64 = a->input_ids64;
+  g.alt_token_id = a->alt_token_id;
   g.weights = a->weights ? a->weights : L->weights;
   g.ids = a->ids ? a->ids : L->ids;
   int32_t *perm = a->permuted ? a->permuted : L->permuted;

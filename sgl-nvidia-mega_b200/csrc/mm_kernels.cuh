@@ -12,7 +12,7 @@ struct GateArgs {
   const float *logits;       // [T, router_experts]
   const float *bias;         // [router_experts] or null
   const int *num_valid;      // [1] or null
-  int score_func;            // 0 sigmoid, 1 softmax
+  int score_func;            // 0 sigmoid, 1 softmax, 2 sqrt(softplus)
   int renormalize;
   float routed_scaling;
   float renorm_eps;
@@ -20,6 +20,10 @@ struct GateArgs {
   int top_k;
   float *weights_out;        // [T, top_k]
   int *ids_out;              // [T, top_k]
+  const float *bias_alt;     // [router_experts] or null (vision rows rank with it)
+  const void *input_ids;     // [T] int32 / int64, or null
+  int input_ids64;
+  long long alt_token_id;
 };
 
 struct RouteArgs {

@@ -18,8 +18,9 @@
 //    multiply by the exact inverse power of two, e4m3 RN satfinite); the same
 //    rule with E2M1 codes (largest magnitude 6, fp32(1/6)) for the MXFP4 terms
 //    of the activations.
-// The sigmoid uses this file's own exp (Cody-Waite reduction + Taylor
-// polynomial) instead of the reference's tanh.approx, whose bits no CPU code
+// The sigmoid and sqrt(softplus) use this file's own exp and log (Cody-Waite
+// reduction + Taylor polynomial; atanh series) instead of the reference's
+// tanh.approx / libm / approximate-reciprocal sequences, whose bits no CPU code
 // can reproduce; everything else is the reference's rule.
 #pragma once
 #include <cstdint>
@@ -60,6 +61,48 @@ __device__ __forceinline__ float det_exp(float x) {
 
 __device__ __forceinline__ float det_sigmoid(float x) {
   return __fdiv_rn(1.0f, __fadd_rn(1.0f, det_exp(-x)));
+}
+
+// log(u) for finite u >= 1: u = m 2^k with m in [sqrt(1/2), sqrt(2)), log u =
+// k ln2 + 2 atanh(f / (2 + f)), f = m - 1 (exact), atanh(s) = s (1 + z/3 +
+// z^2/5 + z^3/7 + z^4/9 + z^5/11), z = s^2 (|s| <= 0.172: the next term is
+// below fp32 resolution); ln2 split in two constants as in det_exp.
+__device__ __forceinline__ float det_log(float u) {
+  const uint32_t bits = __float_as_uint(u);
+  int k = static_cast<int>((bits >> 23) & 0xffu) - 127;
+  float m = __uint_as_float((bits & 0x7fffffu) | 0x3f800000u);
+  if (m > 0x1.6a09e6p+0f) {
+    m = __fmul_rn(m, 0.5f);
+    k += 1;
+  }
+  const float f = __fsub_rn(m, 1.0f);
+  const float s = __fdiv_rn(f, __fadd_rn(2.0f, f));
+  const float z = __fmul_rn(s, s);
+  float q = 0x1.745d18p-4f;              // 1/11
+  q = __fmaf_rn(q, z, 0x1.c71c72p-4f);   // 1/9
+  q = __fmaf_rn(q, z, 0x1.24924ap-3f);   // 1/7
+  q = __fmaf_rn(q, z, 0x1.99999ap-3f);   // 1/5
+  q = __fmaf_rn(q, z, 0x1.555556p-2f);   // 1/3
+  q = __fmaf_rn(q, z, 1.0f);
+  const float lm = __fmul_rn(__fadd_rn(s, s), q);
+  const float kf = static_cast<float>(k);
+  return __fmaf_rn(kf, 0x1.62e400p-1f, __fmaf_rn(kf, 0x1.7f7d1cp-20f, lm));
+}
+
+// log1p(y) for y >= 0 (Goldberg's form): u = 1 + y; y when u == 1, else
+// log(u) * (y / (u - 1)), which cancels the rounding of 1 + y.
+__device__ __forceinline__ float det_log1p(float y) {
+  const float u = __fadd_rn(1.0f, y);
+  if (u == 1.0f) return y;
+  return __fmul_rn(det_log(u), __fdiv_rn(y, __fsub_rn(u, 1.0f)));
+}
+
+// sqrt(softplus(x)), the DeepSeek-V4.1 router score (gate_topk.cuh:99-104):
+// softplus(x) = x above 20, else log1p(exp(x)); the square root is IEEE.
+__device__ __forceinline__ float det_sqrtsoftplus(float x) {
+  if (x != x) return x;
+  const float sp = x > 20.0f ? x : det_log1p(det_exp(x));
+  return __fsqrt_rn(sp);
 }
 
 // Order-preserving key of v (larger key = better candidate); -0 ranks as +0

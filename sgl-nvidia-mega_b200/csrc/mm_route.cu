@@ -167,6 +167,14 @@ __device__ void gate_row(const GateArgs &g, int row, int valid_rows, GateSmem &s
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int E = g.router_experts, K = g.top_k;
   const float *lrow = g.logits + static_cast<size_t>(row) * E;
+  // a valid row whose input token is alt_token_id ranks with bias_alt
+  bool alt = false;
+  if (g.input_ids != nullptr && row < valid_rows) {
+    const long long token = g.input_ids64 ? static_cast<const long long *>(g.input_ids)[row]
+                                          : static_cast<long long>(static_cast<const int *>(g.input_ids)[row]);
+    alt = token == g.alt_token_id;
+  }
+  const float *bias = alt && g.bias_alt != nullptr ? g.bias_alt : g.bias;
   unsigned long long pk[2];
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
@@ -174,9 +182,10 @@ __device__ void gate_row(const GateArgs &g, int row, int valid_rows, GateSmem &s
     pk[h] = 0ull;
     if (e < E) {
       const float l = lrow[e];
-      const float b = g.bias != nullptr ? g.bias[e] : 0.0f;
+      const float b = bias != nullptr ? bias[e] : 0.0f;
       float s;
       if (g.score_func == 0) s = det_sigmoid(l);
+      else if (g.score_func == 2) s = det_sqrtsoftplus(l);
       else s = l;  // softmax: rank the (biased) logits
       sm.score[e] = s;
       sm.logit[e] = l;
@@ -307,10 +316,16 @@ __device__ void build_route(const RouteArgs &r, unsigned char *smem_raw) {
   const int rec_words = token_off + kTile * max_ctas;
   for (int i = tid; i < E * words; i += blockDim.x) rowmask[i] = 0u;
   for (int i = tid; i < rec_words; i += blockDim.x) r.record[i] = 0;
+  // balanced dealing (route.cuh:39-46): a negative offset selects group
+  // -1 - offset of two; ids are global, and of the step's distinct experts in
+  // id order the k-th belongs to group k % 2
+  const bool deal = r.expert_offset < 0;
+  const int group = deal ? -1 - r.expert_offset : 0;
+  const int offset = deal ? 0 : r.expert_offset;
   __syncthreads();
   for (int s = tid; s < slots; s += blockDim.x) {
     const int t = s / K;
-    const int e = __ldcg(r.ids + s) - r.expert_offset;  // written by other CTAs: L2
+    const int e = __ldcg(r.ids + s) - offset;  // written by other CTAs: L2
     if (e >= 0 && e < E) atomicOr(&rowmask[e * words + (t >> 5)], 1u << (t & 31));
   }
   __syncthreads();
@@ -318,6 +333,18 @@ __device__ void build_route(const RouteArgs &r, unsigned char *smem_raw) {
     int c = 0;
     for (int wd = 0; wd < words; ++wd) c += __popc(rowmask[e * words + wd]);
     counts[e] = c;
+    first[e] = c > 0 ? 1 : 0;  // presence, ranked below when dealing
+  }
+  __syncthreads();
+  if (deal) {
+    int present = 0;
+    block_exclusive_scan_512(first, E, warp_tot, present);
+    for (int e = tid; e < E; e += blockDim.x)
+      if (counts[e] > 0 && (first[e] & 1) != group) counts[e] = 0;
+    __syncthreads();
+  }
+  for (int e = tid; e < E; e += blockDim.x) {
+    const int c = counts[e];
     first[e] = (c + kTile - 1) / kTile;               // tiles
     seg_first[e] = (c + kSegRows - 1) / kSegRows;     // segments
   }
@@ -331,8 +358,8 @@ __device__ void build_route(const RouteArgs &r, unsigned char *smem_raw) {
   }
   for (int s = tid; s < slots; s += blockDim.x) {
     const int t = s / K;
-    const int e = __ldcg(r.ids + s) - r.expert_offset;  // written by other CTAs: L2
-    if (e < 0 || e >= E) {
+    const int e = __ldcg(r.ids + s) - offset;  // written by other CTAs: L2
+    if (e < 0 || e >= E || counts[e] == 0) {  // not held, or dealt to the other group
       r.permuted[s] = -1;
       continue;
     }
@@ -504,7 +531,8 @@ extern "C" int mm_gate_route_noalloc(const mm_gate_args *gate, int32_t tokens, i
   if (experts < 1 || experts > kMaxRouterExperts || expert_offset < 0 || expert_offset + experts > router_experts)
     return set_error(MM_ERR_INVALID, "mm_gate_route_noalloc: local experts [%d, %d) outside the router's %d",
                      expert_offset, expert_offset + experts, router_experts);
-  if (gate->score_func != MM_SCORE_SIGMOID && gate->score_func != MM_SCORE_SOFTMAX)
+  if (gate->score_func != MM_SCORE_SIGMOID && gate->score_func != MM_SCORE_SOFTMAX &&
+      gate->score_func != MM_SCORE_SQRTSOFTPLUS)
     return set_error(MM_ERR_UNSUPPORTED, "mm_gate_route_noalloc: score function %d is not built", gate->score_func);
   int device = 0;
   cudaError_t e = cudaGetDevice(&device);
@@ -525,6 +553,10 @@ extern "C" int mm_gate_route_noalloc(const mm_gate_args *gate, int32_t tokens, i
   g.top_k = top_k;
   g.weights_out = gate->weights;
   g.ids_out = scratch + kNoAllocIdsWord;
+  g.bias_alt = gate->bias_alt;
+  g.input_ids = gate->input_ids;
+  g.input_ids64 = gate->input_ids64;
+  g.alt_token_id = gate->alt_token_id;
   RouteArgs r = {};
   r.ids = scratch + kNoAllocIdsWord;
   r.permuted = permuted;

@@ -67,6 +67,10 @@ class MMGateArgs(ctypes.Structure):
         ("renorm_eps", c_float),
         ("weights", c_void_p),
         ("ids", c_void_p),
+        ("bias_alt", c_void_p),
+        ("input_ids", c_void_p),
+        ("input_ids64", c_int32),
+        ("alt_token_id", c_int64),
     ]
 
 
@@ -108,6 +112,10 @@ class MMForwardArgs(ctypes.Structure):
         ("out", c_void_p),
         ("partial", c_void_p),
         ("comm", c_void_p),
+        ("bias_alt", c_void_p),
+        ("input_ids", c_void_p),
+        ("input_ids64", c_int32),
+        ("alt_token_id", c_int64),
         ("residual", c_void_p),
         ("gamma", c_void_p),
         ("norm_eps", c_float),

@@ -62,6 +62,9 @@ class RoutedMoE:
     and ``shared`` carries six tensors (the four, then its two scale_2 [1]).
     ``router_experts``: the router's expert count (default: the local ones);
     ``expert_offset``: router id of local expert 0 (expert parallelism);
+    ``deal_group`` (0 or 1; -1 off): balanced dealing, the layer holds every
+    expert and keeps the step's distinct experts of even (0) or odd (1) rank
+    in id order (routed_expert_gemm.py:557-599, route.cuh:39-46);
     ``clamp``: fp32 [E] SwiGLU clamp limits or None;
     ``act_terms``: MXFP4 terms per activation (1..3, default 3: each term
     quantizes the residual of the previous ones; about 1e-3 relative).
@@ -79,6 +82,7 @@ class RoutedMoE:
         clamp: Optional[torch.Tensor] = None,
         router_experts: Optional[int] = None,
         expert_offset: int = 0,
+        deal_group: int = -1,
         shared: Optional[Sequence[torch.Tensor]] = None,
         shared_clamp: Optional[torch.Tensor] = None,
         act_terms: int = 3,
@@ -114,6 +118,11 @@ class RoutedMoE:
         self.hidden, self.inter, self.experts = hidden, inter, experts
         self.router_experts = experts if router_experts is None else int(router_experts)
         self.expert_offset = int(expert_offset)
+        self.deal_group = int(deal_group)
+        if self.deal_group not in (-1, 0, 1):
+            raise ValueError(f"deal_group {deal_group}: 0, 1 or -1 (off)")
+        if self.deal_group >= 0 and (self.expert_offset != 0 or experts != self.router_experts):
+            raise ValueError(f"balanced dealing needs all {self.router_experts} experts and expert_offset 0")
         self.top_k = int(top_k)
         self.max_rows = int(max_rows)
         self.act_terms = int(act_terms)
@@ -125,7 +134,8 @@ class RoutedMoE:
         desc = _lib.MMLayerDesc()
         desc.hidden, desc.intermediate, desc.experts = hidden, inter, experts
         desc.router_experts = self.router_experts
-        desc.expert_offset = self.expert_offset
+        # the library's expert_offset: negative selects balanced dealing
+        desc.expert_offset = -1 - self.deal_group if self.deal_group >= 0 else self.expert_offset
         desc.top_k = self.top_k
         desc.max_tokens = self.max_rows
         desc.weight_format = _lib.MM_WEIGHT_NVFP4 if nv else _lib.MM_WEIGHT_MXFP4
@@ -233,15 +243,18 @@ class RoutedMoE:
         renormalize: bool = True,
         renormalize_epsilon: float = 0.0,
         ids_out: Optional[torch.Tensor] = None,
+        alt=None,
     ):
         """Top-k from fp32 router logits, then route + gate_up + down. Returns
-        (rows, weights, permuted, ids)."""
+        (rows, weights, permuted, ids). ``alt`` = (bias_alt, input_ids, token
+        id): rows whose token is that id rank with bias_alt (vision routing)."""
         rows = self._check_x(x)
         if logits.dtype != torch.float32 or tuple(logits.shape) != (rows, self.router_experts) or not logits.is_contiguous():
             raise ValueError(f"logits: expected contiguous fp32 [{rows}, {self.router_experts}]")
         weights = torch.empty((rows, self.top_k), dtype=torch.float32, device=self.device)
         ids = ids_out[:rows] if ids_out is not None else torch.empty((rows, self.top_k), dtype=torch.int32, device=self.device)
-        g = gate_args(logits, bias, num_valid, score, renormalize, routed_scaling_factor, renormalize_epsilon, weights, ids)
+        g = gate_args(logits, bias, num_valid, score, renormalize, routed_scaling_factor, renormalize_epsilon, weights, ids,
+                      alt)
         permuted, record, out_rows = self._outputs(rows)
         check(
             lib().mm_layer_gate_experts(
@@ -280,6 +293,7 @@ class RoutedMoE:
         comm=None,
         residual: Optional[torch.Tensor] = None,
         gamma: Optional[torch.Tensor] = None,
+        alt=None,
     ):
         """One whole MoE step on the current stream. Returns the bf16 [T, H]
         output (or the fp32 [2, T, H] partial sums with ``partial``; with
@@ -346,6 +360,7 @@ class RoutedMoE:
         a.out = _ptr(out)
         a.partial = _ptr(part)
         a.comm = None if comm is None else comm.handle
+        _alt_fields(a, alt)
         a.residual = _ptr(residual)
         a.gamma = _ptr(gamma)
         a.norm_eps = 0.0 if comm is None else comm.eps
@@ -372,12 +387,31 @@ def route_words(rows: int, top_k: int, experts: int) -> int:
     return int(lib().mm_route_words(rows, top_k, experts))
 
 
-def gate_args(logits, bias, num_valid, score, renormalize, scale, eps, weights, ids) -> _lib.MMGateArgs:
+def _alt_fields(obj, alt) -> None:
+    """Set the vision-routing fields of a gate / forward args struct from ``alt``
+    = (bias_alt fp32 [E] or None, input_ids int32/int64 [T], token id), the
+    reference's gate_topk_and_gemms ``alt`` (routed_expert_gemm.py:776-812)."""
+    if alt is None:
+        obj.bias_alt, obj.input_ids, obj.input_ids64, obj.alt_token_id = None, None, 0, -1
+        return
+    bias_alt, input_ids, token = alt
+    if bias_alt is not None and (bias_alt.dtype != torch.float32 or not bias_alt.is_contiguous()):
+        raise ValueError("bias_alt must be a contiguous fp32 tensor")
+    if input_ids.dtype not in (torch.int32, torch.int64) or not input_ids.is_contiguous():
+        raise ValueError("input_ids must be a contiguous int32 or int64 tensor")
+    obj.bias_alt = _ptr(bias_alt)
+    obj.input_ids = input_ids.data_ptr()
+    obj.input_ids64 = int(input_ids.dtype == torch.int64)
+    obj.alt_token_id = int(token)
+
+
+def gate_args(logits, bias, num_valid, score, renormalize, scale, eps, weights, ids, alt=None) -> _lib.MMGateArgs:
     if score not in _lib.SCORES:
         raise ValueError(f"unknown score function {score!r}")
     if bias is not None and (bias.dtype != torch.float32 or not bias.is_contiguous()):
         raise ValueError("bias must be a contiguous fp32 tensor")
     g = _lib.MMGateArgs()
+    _alt_fields(g, alt)
     g.logits = logits.data_ptr()
     g.bias = _ptr(bias)
     g.num_valid = _ptr(num_valid)
@@ -407,13 +441,15 @@ def router_gemv(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
 
 def gate_topk(logits: torch.Tensor, bias: Optional[torch.Tensor], top_k: int, *, score: str = "sigmoid",
               renormalize: bool = True, routed_scaling_factor: float = 1.0, renormalize_epsilon: float = 0.0,
-              num_valid: Optional[torch.Tensor] = None):
-    """(weights fp32 [T, k], ids int32 [T, k]) of the router top-k."""
+              num_valid: Optional[torch.Tensor] = None, alt=None):
+    """(weights fp32 [T, k], ids int32 [T, k]) of the router top-k; ``alt`` =
+    (bias_alt, input_ids, token id) for vision routing."""
     logits = logits.contiguous()
     tokens, experts = logits.shape
     weights = torch.empty((tokens, top_k), dtype=torch.float32, device=logits.device)
     ids = torch.empty((tokens, top_k), dtype=torch.int32, device=logits.device)
-    g = gate_args(logits, bias, num_valid, score, renormalize, routed_scaling_factor, renormalize_epsilon, weights, ids)
+    g = gate_args(logits, bias, num_valid, score, renormalize, routed_scaling_factor, renormalize_epsilon, weights, ids,
+                  alt)
     check(lib().mm_gate_topk(ctypes.byref(g), tokens, experts, top_k, _stream(logits.device)), "mm_gate_topk")
     return weights, ids
 

@@ -5,7 +5,8 @@ compiled for the CPU by `make -C oracle ref` (oracle/ref_route_shim.h runs one
 thread block as std::threads) and run on seeded top-k ids covering: one row,
 8 rows (route.cu), 9..64 rows (route_wide.cu), every expert taking every row
 (several tiles per expert), expert-parallel windows (expert_offset > 0, ids
-outside the window -> -1), and top-k 1..8 at 32..384 experts.
+outside the window -> -1), balanced dealing to either group (expert_offset -1
+and -2), and top-k 1..8 at 32..384 experts.
 
 Run from the repository root:  python tests/golden/make_golden.py
 Writes tests/golden/route_cases.npz (ids, expected permuted and record per case).
@@ -34,7 +35,7 @@ def main() -> None:
     shapes = [(1, 6, 384), (1, 8, 32), (6, 6, 384), (8, 8, 384), (8, 8, 64), (8, 3, 128), (9, 6, 384),
               (16, 6, 384), (16, 8, 256), (32, 8, 384), (48, 6, 384), (64, 8, 384), (64, 4, 32), (64, 8, 64)]
     for T, K, E in shapes:
-        for variant in ("random", "all_rows", "ep_low", "ep_high"):
+        for variant in ("random", "all_rows", "ep_low", "ep_high", "deal0", "deal1"):
             if variant == "all_rows":
                 pool = rng.permutation(E)[:K]
                 ids = np.stack([rng.permutation(pool) for _ in range(T)])
@@ -46,6 +47,8 @@ def main() -> None:
                 local = E // 2
             elif variant == "ep_high":
                 local, offset = E // 2, E // 2
+            elif variant.startswith("deal"):  # balanced dealing: group -1 - offset
+                offset = -1 - int(variant[-1])
             words = O.route_words(T, K, local)
             perm = np.empty((T, K), np.int32)
             rec = np.empty(words, np.int32)

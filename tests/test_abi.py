@@ -55,7 +55,7 @@ def test_invalid_arguments_are_rejected_before_the_device():
     assert b"null" in L.mm_last_error()
     buf = (ctypes.c_int32 * 4096)()
     assert L.mm_route(buf, buf, buf, 0, 8, 384, 0, None) == _lib.MM_ERR_INVALID
-    assert L.mm_route(buf, buf, buf, 8, 8, 384, -1, None) == _lib.MM_ERR_UNSUPPORTED
+    assert L.mm_route(buf, buf, buf, 8, 8, 384, -3, None) == _lib.MM_ERR_INVALID  # dealing is -1 / -2 only
     assert L.mm_router_gemv(buf, buf, buf, 8, 384, 1000, None) == _lib.MM_ERR_INVALID
     desc = _lib.MMLayerDesc()
     desc.hidden, desc.intermediate, desc.experts, desc.router_experts = 100, 2048, 384, 384

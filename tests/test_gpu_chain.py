@@ -73,7 +73,7 @@ def _logits(kind, T, E, g):
     raise ValueError(kind)
 
 
-@pytest.mark.parametrize("score", ["sigmoid", "softmax"])
+@pytest.mark.parametrize("score", ["sigmoid", "softmax", "sqrtsoftplus"])
 @pytest.mark.parametrize("kind", ["normal", "wide", "ties", "nan_rows", "tie_cutoff"])
 @pytest.mark.parametrize("E,K", [(16, 2), (384, 8), (256, 8), (512, 10)])
 def test_gate_topk_bitexact(score, kind, E, K):
@@ -91,6 +91,32 @@ def test_gate_topk_bitexact(score, kind, E, K):
                                    scale=2.5, num_valid=valid)
             assert np.array_equal(ids.cpu().numpy(), oids), (kind, T, trial)
             assert _same_bits(w.cpu().numpy(), ow), (kind, T, trial)
+
+
+@pytest.mark.parametrize("ids64", [False, True])
+def test_gate_topk_vision_alt_bias_bitexact(ids64):
+    """Rows whose input token is the image token rank with bias_alt (DSV4.1 VL
+    routing, gate_topk.cuh:290-346); padded rows stay -1 whatever their token."""
+    mm = _mm()
+    g = torch.Generator().manual_seed(99)
+    T, E, K, tok = 12, 384, 6, 128815
+    logits = torch.randn((T, E), generator=g)
+    bias = (torch.randn(E, generator=g) * 0.05).float()
+    bias_alt = (torch.randn(E, generator=g) * 0.5).float()
+    input_ids = torch.randint(0, 200000, (T,), generator=g)
+    input_ids[[0, 3, 4, 11]] = tok
+    input_ids = input_ids.to(torch.int64 if ids64 else torch.int32)
+    for score in ("sqrtsoftplus", "sigmoid"):
+        for valid in (T, T - 1):
+            nv = torch.tensor([valid], dtype=torch.int32, device="cuda")
+            w, ids = mm.gate_topk(logits.cuda(), bias.cuda(), K, score=score, routed_scaling_factor=2.5,
+                                  num_valid=nv, alt=(bias_alt.cuda(), input_ids.cuda(), tok))
+            ow, oids = O.gate_topk(logits.numpy(), bias.numpy(), K, score=score, scale=2.5, num_valid=valid,
+                                   bias_alt=bias_alt.numpy(), input_ids=input_ids.numpy(), alt_token_id=tok)
+            assert np.array_equal(ids.cpu().numpy(), oids), (score, valid)
+            assert _same_bits(w.cpu().numpy(), ow), (score, valid)
+            _, plain_ids = O.gate_topk(logits.numpy(), bias.numpy(), K, score=score, scale=2.5, num_valid=valid)
+            assert not np.array_equal(oids, plain_ids)  # the image rows did rank with bias_alt
 
 
 def _same_bits(a, b):
@@ -111,7 +137,8 @@ def _random_ids(T, K, E, g, distinct=None):
 def test_route_bitexact(T, K, E):
     mm = _mm()
     g = torch.Generator().manual_seed(7 * T + K)
-    for distinct, offset, local in ((None, 0, E), (K, 0, E), (None, E // 2, E // 2), (None, 0, E // 2)):
+    for distinct, offset, local in ((None, 0, E), (K, 0, E), (None, E // 2, E // 2), (None, 0, E // 2),
+                                    (None, -1, E), (None, -2, E), (K, -2, E)):  # -1/-2: balanced dealing
         ids = _random_ids(T, K, E, g, distinct)
         perm, rec = mm.route(ids.cuda(), local, offset)
         operm, orec = O.route(ids.numpy(), local, offset)
@@ -245,6 +272,37 @@ def test_nvfp4_single_term_and_ep_window():
             for k, v in layer.items()}
     _run_and_check(half, x, ids, w, K, max_rows=8, expert_offset=16, local=16, router_experts=32)
     _run_and_check(layer, x, ids, w, K, max_rows=8, act_terms=1)
+
+
+def test_experts_balanced_dealing_groups_sum_to_the_layer():
+    """Balanced dealing (route.cuh:39-46): each group keeps alternate distinct
+    experts; each group's rows match the oracle of its experts, and the two
+    groups' combined outputs add up to the whole layer's."""
+    mm = _mm()
+    H, I, E, K, T = 1024, 256, 32, 6, 8
+    layer = O.make_layer(H, I, E, shared=False, seed=13)
+    x, _, _ = O.make_inputs(T, H, E, seed=13)
+    g = torch.Generator().manual_seed(13)
+    ids = _random_ids(T, K, E, g)
+    w = torch.rand((T, K), generator=g)
+    dev = torch.device("cuda", 0)
+    wts = [layer[k].to(dev) for k in ("w13", "w13_scale", "w2", "w2_scale")]
+    parts = []
+    for group in (0, 1):
+        moe = mm.RoutedMoE(*wts, K, 8, deal_group=group)
+        rows, _, perm = moe(x.cuda(), ids.cuda())
+        operm, orec = O.route(ids.numpy(), E, -1 - group)
+        assert np.array_equal(perm.cpu().numpy(), operm)
+        _, kn_rows, _ = O.moe_layer(x, ids.numpy(), w.numpy(), layer, numerics="kernel", deal_group=group)
+        pc = perm.cpu().numpy()
+        got = np.stack([rows.float().cpu()[pc[t, k]].numpy() for (t, k) in kn_rows])
+        want = np.stack([v.numpy() for v in kn_rows.values()])
+        assert O.max_abs_rel(got, want) <= ROWS_TOL
+        parts.append(moe.finalize(rows, w.cuda(), perm, partial=True))
+        moe.check()
+    total = mm.finalize_partial(parts[0] + parts[1])
+    ex, _, _ = O.moe_layer(x, ids.numpy(), w.numpy(), layer, numerics="exact")
+    assert O.max_abs_rel(total.float().cpu().numpy(), ex.numpy()) <= OUT_TOL
 
 
 def test_experts_expert_parallel_window():

@@ -39,7 +39,13 @@ def test_route_matches_live_reference():
         E = int(rng.choice([32, 96, 128, 384]))
         K = min(K, 512 // T)
         ids = np.stack([rng.permutation(E)[:K] for _ in range(T)]).astype(np.int32)
-        local, offset = (E, 0) if rng.random() < 0.6 else (E // 2, int(rng.integers(0, 2)) * (E // 2))
+        u = rng.random()
+        if u < 0.45:
+            local, offset = E, 0
+        elif u < 0.8:
+            local, offset = E // 2, int(rng.integers(0, 2)) * (E // 2)
+        else:  # balanced dealing to group 0 or 1 (route.cuh:39-46)
+            local, offset = E, -1 - int(rng.integers(0, 2))
         perm, rec = O.route(ids, local, offset)
         rp, rr = np.empty_like(perm), np.empty_like(rec)
         ref.ref_route_wide(P(ids), P(rp), P(rr), T, K, local, offset)
@@ -306,3 +312,36 @@ def test_nvfp4_weight_dequant_matches_definition():
     assert abs(float(W[r, k]) - want) <= 1e-7 * max(1.0, abs(want))
     vals = O.e4m3_table()[L["w13_scale"].numpy()]
     assert vals.min() >= 0.5 and vals.max() <= 4.0
+
+
+def test_sqrtsoftplus_known_answers_and_accuracy():
+    h = O.lib()
+    h.or_sqrtsoftplus.restype = ctypes.c_float
+    h.or_sqrtsoftplus.argtypes = [ctypes.c_float]
+    assert h.or_sqrtsoftplus(25.0) == 5.0                     # above 20: sqrt(x)
+    assert h.or_sqrtsoftplus(-200.0) == 0.0                   # exp underflows
+    assert math.isnan(h.or_sqrtsoftplus(float("nan")))
+    xs = np.concatenate([np.linspace(-80, 20, 4001), np.random.default_rng(2).normal(0, 6, 4000).clip(-80, 20)])
+    worst = 0.0
+    for x in xs.astype(np.float32):
+        want = math.sqrt(math.log1p(math.exp(float(x))))
+        worst = max(worst, abs(h.or_sqrtsoftplus(float(x)) - want) / want)
+    assert worst < 4 * 2.0 ** -24, worst                     # a couple of ulps
+
+
+def test_gate_topk_sqrtsoftplus_and_alt_bias():
+    rng = np.random.default_rng(3)
+    T, E, K = 6, 64, 4
+    logits = rng.normal(size=(T, E)).astype(np.float32)
+    w, ids = O.gate_topk(logits, None, K, score="sqrtsoftplus", scale=2.0)
+    s = np.sqrt(np.log1p(np.exp(logits.astype(np.float64))))
+    assert np.array_equal(np.sort(ids, 1), np.sort(np.argsort(-s, 1)[:, :K], 1))
+    sel = np.take_along_axis(s, ids.astype(np.int64), 1)
+    assert np.allclose(w, 2.0 * sel / sel.sum(1, keepdims=True), rtol=1e-6)
+    # image rows (token 7) rank with bias_alt: a huge alt bias on expert 9 wins
+    bias_alt = np.zeros(E, np.float32)
+    bias_alt[9] = 100.0
+    toks = np.array([7, 1, 7, 2, 3, 7], np.int64)
+    _, ids2 = O.gate_topk(logits, np.zeros(E, np.float32), K, score="sqrtsoftplus", bias_alt=bias_alt,
+                          input_ids=toks, alt_token_id=7)
+    assert [int(ids2[t, 0]) == 9 for t in range(T)] == [True, False, True, False, False, True]
