@@ -41,24 +41,6 @@ int fail(int code, const char *fmt, ...) {
 
 bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
-// Launch with programmatic stream serialization: the kernel may start while its
-// predecessor runs; it reads the predecessor's outputs after griddepcontrol.wait.
-template <typename... KArgs, typename... Args>
-cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, void *stream,
-                   Args &&...args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = static_cast<cudaStream_t>(stream);
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
-}
-
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
@@ -469,10 +451,7 @@ int mm_layer_create(const mm_layer_desc *desc, mm_layer **out) {
   ea.ks1 = L->ks1;
   ea.ks2 = L->ks2;
 
-  ce = nv ? cudaFuncSetAttribute(expert_kernel<kFmtNv>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 Fmt<kFmtNv>::kSmemAlloc)
-          : cudaFuncSetAttribute(expert_kernel<kFmtMx>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 Fmt<kFmtMx>::kSmemAlloc);
+  ce = expert_kernel_configure(L->fmt);
   if (ce == cudaSuccess)
     ce = cudaFuncSetAttribute(front_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               static_cast<int>(route_smem_bytes(kMaxTokens, kMaxRouterExperts)));
@@ -509,9 +488,7 @@ int mm_layer_get_info(const mm_layer *L, mm_layer_info *info) {
 }
 
 static cudaError_t launch_experts(mm_layer *L, const ExpertArgs &ea, void *stream) {
-  const dim3 grid(kCtasPerSm * L->num_sms), block(kExpertThreads);
-  return L->fmt == kFmtNv ? launch(expert_kernel<kFmtNv>, grid, block, Fmt<kFmtNv>::kSmemAlloc, stream, ea)
-                          : launch(expert_kernel<kFmtMx>, grid, block, Fmt<kFmtMx>::kSmemAlloc, stream, ea);
+  return expert_kernel_launch(L->fmt, kCtasPerSm * L->num_sms, ea, stream);
 }
 
 // One launch of the router GEMV (w non-null) and the MXFP4-terms quantization

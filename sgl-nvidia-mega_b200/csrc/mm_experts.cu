@@ -69,6 +69,21 @@ __device__ __forceinline__ int ld_shared_volatile(const int *p) {
   return *reinterpret_cast<const volatile int *>(p);
 }
 
+// The segment descriptor of unit work, cached across a role's consecutive units
+// of the same segment (a run of short units would otherwise wait on one L2
+// round trip per unit for it).
+struct SegCache {
+  int seg = -1;
+  int4 sg;
+  __device__ __forceinline__ const int4 &get(const int4 *segs, int s) {
+    if (s != seg) {
+      sg = segs[s];
+      seg = s;
+    }
+    return sg;
+  }
+};
+
 // Wait until `flag` >= target; false (and the error word set) on timeout.
 __device__ bool wait_flag(const int *flag, int target, uint32_t *err) {
   if (ld_acquire(flag) >= target) return true;
@@ -204,16 +219,24 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
       // CTA b's first unit is unit b, unclaimed: the first wave gives every CTA
       // exactly one unit (with claims, a CTA could take two long gate_up units
       // while another took two short down units). Later units come from the
-      // counter, offset by the grid, and are claimed three stages before the
-      // current unit's last load: the claim's round trip hides behind the
-      // stages in flight, and a CTA takes a unit only when it is about to run it.
-      int next = static_cast<int>(blockIdx.x);
+      // counter, offset by the grid, in batches of max(1, 8 / stages)
+      // consecutive units: one claim per about eight stages of loads, so a run
+      // of one-stage down units (narrow tensor-parallel slices) does not wait on
+      // a claim's round trip per unit. The next batch is claimed three stages
+      // before the last load of the current batch's last-but-one unit, so the
+      // round trip hides behind the stages in flight, and a CTA takes units
+      // only shortly before it runs them.
+      SegCache seg_cache;
+      int cur = static_cast<int>(blockIdx.x);
+      int a_next = total, a_end = total;  // the current batch's units not yet started
+      int b_next = total, b_end = total;  // the next batch, once claimed
+      bool b_claimed = false;
       bool ok = true;
 #pragma unroll 1
       while (ok) {
-        const int u = next;
+        const int u = cur;
         const bool have = u < total;
-        next = total;
+        cur = total;
         if (!mbar_wait(bar(kBarWorkEmpty + ws), wphase ^ 1u, err, kErrTimeoutWork)) break;
         work_ids[ws] = have ? u : -1;
         mbar_arrive(bar(kBarWorkFull + ws));
@@ -222,7 +245,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
         bool g2;
         int seg, m;
         decode_unit(u, nseg, p.m1, p.m2, g2, seg, m);
-        const int4 sg = p.segs[seg];
+        const int4 sg = seg_cache.get(p.segs, seg);
         const int e = sg.x < 0 ? 0 : sg.x;
         const bool sh = sg.x < 0;
         const CUtensorMap *map = g2 ? (sh ? &p.sw2_map : &p.w2_map) : (sh ? &p.sw13_map : &p.w13_map);
@@ -230,9 +253,15 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
         const uint8_t *sfa = g2 ? (sh ? p.ssfa2 : p.sfa2) : (sh ? p.ssfa13 : p.sfa13);
         sfa += (static_cast<size_t>(e) * (g2 ? p.m2 : p.m1) + m) * static_cast<size_t>(ks_n) * L::kSfStageBytes;
         const int claim_at = ks_n > 3 ? ks_n - 3 : 0;
+        const bool refill = !b_claimed && a_end - a_next <= 1;
 #pragma unroll 1
         for (int ks = 0; ks < ks_n; ++ks) {
-          if (ks == claim_at) next = static_cast<int>(gridDim.x) + atomicAdd(&p.ctrl[kCtrlClaim], 1);
+          if (refill && ks == claim_at) {
+            const int batch = ks_n >= 8 ? 1 : 8 / ks_n;
+            b_next = static_cast<int>(gridDim.x) + atomicAdd(&p.ctrl[kCtrlClaim], batch);
+            b_end = b_next + batch;
+            b_claimed = true;
+          }
           if (!mbar_wait(bar(kBarEmpty + stage), phase ^ 1u, err, kErrTimeoutEmpty)) {
             ok = false;
             break;
@@ -251,6 +280,12 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
                     sfa + static_cast<size_t>(ks) * L::kSfStageBytes, L::kSfStageBytes, full, policy);
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
         }
+        if (a_next >= a_end && b_claimed) {
+          a_next = b_next;
+          a_end = b_end;
+          b_claimed = false;
+        }
+        if (a_next < a_end) cur = a_next++;
       }
       // drain: every stage filled so far has been consumed, so no copy is in flight
       for (int i = 0; i < kStages; ++i) {
@@ -269,6 +304,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
       const uint64_t sw_hi = smem_desc(0, 0, 1024, kLayoutSw128);
       const uint64_t sf_hi = smem_desc(0, 0, 128, kLayoutNone);
       const uint32_t idesc_base = kNv ? idesc_nvf4(0) : idesc_mxf4(0, 0);
+      SegCache seg_cache;
 #pragma unroll 1
       while (true) {
         if (!mbar_wait(bar(kBarWorkFull + ws), wphase, err, kErrTimeoutWork)) break;
@@ -279,7 +315,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
         bool g2;
         int seg, m;
         decode_unit(u, nseg, p.m1, p.m2, g2, seg, m);
-        const int4 sg = p.segs[seg];
+        const int4 sg = seg_cache.get(p.segs, seg);
         const uint32_t n = static_cast<uint32_t>((sg.z + 7) & ~7);
         const uint32_t nmma = n * static_cast<uint32_t>(p.terms);  // term 0 rows, term 1 rows, ...
         const uint32_t id0 = idesc_base | ((nmma >> 3) << 17);
@@ -334,13 +370,25 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
     // ============================ B loader ===================================
     // Per unit, every lane fixes its share of a stage once: 16-byte piece
     // pc = lane % 8 of B rows rr = lane / 8 + 4 i (term t rows at [t n, (t+1) n));
-    // per stage it only issues the copies at the stage's K offset.
+    // per stage it only issues the copies at the stage's K offset. The shares
+    // depend only on the unit's segment and kind (gate_up or down), not on its
+    // weight tile, so they are kept while consecutive units share both: a run
+    // of short down units of one segment pays the set-up once.
     pdl_wait();
     const int nseg = p.ctrl[kCtrlSegments];
     uint32_t stage = 0, phase = 0, ws = 0, wphase = 0;
+    SegCache seg_cache;
+    int ready_seg = -1;                 // a segment whose mailbox is known complete
+    int share_seg = -1;                 // the segment / kind the shares below belong to
+    bool share_g2 = false;
     const int pc = lane & 7;            // 16-byte piece of the 128-byte stage row
     const int quarter = lane >> 3;
     constexpr int kPieces = kBRows / 4;  // rows per lane
+    constexpr int kC = L::kChunks;
+    uint32_t soff[kPieces], doff[kPieces], sbytes[kPieces];
+    uint32_t s_soff[2 * kC], s_doff[2 * kC], s_bytes[2 * kC];
+    int nb = 0;
+    const uint8_t *dq = nullptr, *dsc = nullptr;
 #pragma unroll 1
     while (true) {
       int u = -1, okw = 1;
@@ -358,54 +406,56 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
       bool g2;
       int seg, m;
       decode_unit(u, nseg, p.m1, p.m2, g2, seg, m);
-      const int4 sg = p.segs[seg];
-      const int rows = sg.z;
-      const int n = (rows + 7) & ~7;
-      const int nb = n * p.terms;  // B rows of this unit
-      if (g2) {
+      if (g2 && seg != ready_seg) {  // once complete, a mailbox stays complete in this launch
         int okf = 1;
         if (lane == 0) okf = wait_flag(p.flags + seg, 2 * p.m1, err) ? 1 : 0;
         okf = __shfl_sync(0xffffffffu, okf, 0);
         if (!okf) break;
+        ready_seg = seg;
       }
-      // source row of segment row `lane` (lanes >= rows: row 0, never read)
-      int src = 0;
-      if (lane < rows) {
-        if (g2) src = sg.y + lane;
-        else src = sg.w >= 0 ? sg.w + lane : __ldg(p.record + p.token_off + sg.y + lane);
-      }
-      const int K = g2 ? p.inter : p.hidden;
-      const uint8_t *dq = g2 ? p.hq : p.xq;
-      const uint8_t *dsc = g2 ? p.hs : p.xs;
-      const uint32_t rowb = static_cast<uint32_t>(K) >> 1;  // packed bytes per row
-      const uint32_t term_q = static_cast<uint32_t>(g2 ? p.rows_cap : p.max_tokens) * rowb;
-      const uint32_t term_s = term_q / (L::kBlock / 2);
-      uint32_t soff[kPieces], doff[kPieces], sbytes[kPieces];
+      if (seg != share_seg || g2 != share_g2) {
+        share_seg = seg;
+        share_g2 = g2;
+        const int4 sg = seg_cache.get(p.segs, seg);
+        const int rows = sg.z;
+        const int n = (rows + 7) & ~7;
+        nb = n * p.terms;  // B rows of this unit
+        // source row of segment row `lane` (lanes >= rows: row 0, never read)
+        int src = 0;
+        if (lane < rows) {
+          if (g2) src = sg.y + lane;
+          else src = sg.w >= 0 ? sg.w + lane : __ldg(p.record + p.token_off + sg.y + lane);
+        }
+        const int K = g2 ? p.inter : p.hidden;
+        dq = g2 ? p.hq : p.xq;
+        dsc = g2 ? p.hs : p.xs;
+        const uint32_t rowb = static_cast<uint32_t>(K) >> 1;  // packed bytes per row
+        const uint32_t term_q = static_cast<uint32_t>(g2 ? p.rows_cap : p.max_tokens) * rowb;
+        const uint32_t term_s = term_q / (L::kBlock / 2);
 #pragma unroll
-      for (int i = 0; i < kPieces; ++i) {
-        const int rr = quarter + 4 * i;
-        const int t = rr / n;
-        const int r = rr - t * n;
-        const int sr = __shfl_sync(0xffffffffu, src, r & 31);
-        soff[i] = static_cast<uint32_t>(t) * term_q + static_cast<uint32_t>(sr) * rowb + pc * 16;
-        doff[i] = (rr >> 3) * 1024 + (rr & 7) * 128 + ((pc ^ (rr & 7)) << 4);
-        sbytes[i] = (rr < nb && r < rows) ? 16u : 0u;
-      }
-      // scale pieces: B rows rr = lane and lane + 32, every chunk of the stage
-      constexpr int kC = L::kChunks;
-      uint32_t s_soff[2 * kC], s_doff[2 * kC], s_bytes[2 * kC];
+        for (int i = 0; i < kPieces; ++i) {
+          const int rr = quarter + 4 * i;
+          const int t = rr / n;
+          const int r = rr - t * n;
+          const int sr = __shfl_sync(0xffffffffu, src, r & 31);
+          soff[i] = static_cast<uint32_t>(t) * term_q + static_cast<uint32_t>(sr) * rowb + pc * 16;
+          doff[i] = (rr >> 3) * 1024 + (rr & 7) * 128 + ((pc ^ (rr & 7)) << 4);
+          sbytes[i] = (rr < nb && r < rows) ? 16u : 0u;
+        }
+        // scale pieces: B rows rr = lane and lane + 32, every chunk of the stage
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int rr = lane + 32 * h;
-        const int t = rr / n;
-        const int r = rr - t * n;
-        const int sr = __shfl_sync(0xffffffffu, src, r & 31);
+        for (int h = 0; h < 2; ++h) {
+          const int rr = lane + 32 * h;
+          const int t = rr / n;
+          const int r = rr - t * n;
+          const int sr = __shfl_sync(0xffffffffu, src, r & 31);
 #pragma unroll
-        for (int c = 0; c < kC; ++c) {
-          s_soff[kC * h + c] =
-              static_cast<uint32_t>(t) * term_s + static_cast<uint32_t>(sr) * (K / L::kBlock) + c * 4;
-          s_doff[kC * h + c] = c * 512 + (rr & 31) * 16 + (rr >> 5) * 4;
-          s_bytes[kC * h + c] = (rr < nb && r < rows) ? 4u : 0u;
+          for (int c = 0; c < kC; ++c) {
+            s_soff[kC * h + c] =
+                static_cast<uint32_t>(t) * term_s + static_cast<uint32_t>(sr) * (K / L::kBlock) + c * 4;
+            s_doff[kC * h + c] = c * 512 + (rr & 31) * 16 + (rr >> 5) * 4;
+            s_bytes[kC * h + c] = (rr < nb && r < rows) ? 4u : 0u;
+          }
         }
       }
       const int ks_n = g2 ? p.ks2 : p.ks1;
@@ -446,6 +496,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
     const int row = 32 * q + lane;      // accumulator row (weight-tile row)
     float *ex = reinterpret_cast<float *>(sbase + L::kSmemEpi);
     uint32_t ws = 0, wphase = 0, acc = 0, acc_phase = 0, ex_phase = 0;
+    SegCache seg_cache;
 #pragma unroll 1
     while (true) {
       int u = -1, okw = 1;
@@ -463,7 +514,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
       bool g2;
       int seg, m;
       decode_unit(u, nseg, p.m1, p.m2, g2, seg, m);
-      const int4 sg = p.segs[seg];
+      const int4 sg = seg_cache.get(p.segs, seg);
       const int rows = sg.z;
       const int n = (rows + 7) & ~7;
       int ok = 1;
@@ -634,7 +685,17 @@ __global__ void nv_alpha_kernel(const float *__restrict__ scale_2, float input_s
   if (i < n) alpha[i] = __fmul_rn(scale_2[i], input_scale);
 }
 
-template __global__ void expert_kernel<kFmtMx>(const __grid_constant__ ExpertArgs p);
-template __global__ void expert_kernel<kFmtNv>(const __grid_constant__ ExpertArgs p);
+cudaError_t expert_kernel_configure(int fmt) {
+  return fmt == kFmtNv ? cudaFuncSetAttribute(expert_kernel<kFmtNv>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              Fmt<kFmtNv>::kSmemAlloc)
+                       : cudaFuncSetAttribute(expert_kernel<kFmtMx>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              Fmt<kFmtMx>::kSmemAlloc);
+}
+
+cudaError_t expert_kernel_launch(int fmt, int ctas, const ExpertArgs &ea, void *stream) {
+  const dim3 grid(ctas), block(kExpertThreads);
+  return fmt == kFmtNv ? launch(expert_kernel<kFmtNv>, grid, block, Fmt<kFmtNv>::kSmemAlloc, stream, ea)
+                       : launch(expert_kernel<kFmtMx>, grid, block, Fmt<kFmtMx>::kSmemAlloc, stream, ea);
+}
 
 }  // namespace mm

@@ -1,5 +1,6 @@
 // Kernel argument blocks and the device helpers shared by several kernels.
 #pragma once
+#include <utility>
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -164,6 +165,24 @@ __device__ __forceinline__ void quantize_block16_nvfp4(const float *v, int terms
   }
 }
 
+// Launch with programmatic stream serialization: the kernel may start while its
+// predecessor runs; it reads the predecessor's outputs after griddepcontrol.wait.
+template <typename... KArgs, typename... Args>
+cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, void *stream,
+                   Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 // Host helpers shared by the .cu files (mm_api.cu defines them).
 int set_error(int code, const char *fmt, ...);
 // dynamic shared memory of the route build for (tokens, local experts)
@@ -177,8 +196,11 @@ __global__ void router_quant_kernel(RouterArgs a);
 __global__ void gate_topk_kernel(GateArgs g);
 __global__ void route_kernel(RouteArgs r);
 __global__ void front_kernel(FrontArgs f);
-template <int F>
-__global__ void expert_kernel(const __grid_constant__ ExpertArgs p);
+// The expert kernel of format fmt (kFmtMx / kFmtNv): the dynamic shared memory
+// attribute (once per process and format) and a launch of `ctas` CTAs.
+// Defined beside the kernel template, whose instantiations stay in that file.
+cudaError_t expert_kernel_configure(int fmt);
+cudaError_t expert_kernel_launch(int fmt, int ctas, const ExpertArgs &ea, void *stream);
 __global__ void repack_scales_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst,
                                      int n, int rows, int k, int gate_up, int inter, int block);
 __global__ void nv_alpha_kernel(const float *__restrict__ scale_2, float input_scale, float *__restrict__ alpha,

@@ -179,6 +179,18 @@ class RoutedMoE:
         self.route_words_max = int(info.route_words)
         self.expert_weight_bytes = int(info.weight_bytes)
 
+    @classmethod
+    def from_trtllm(cls, w13, w13_scale, w2, w2_scale, top_k: int, max_rows: int, *, halves: str = "w3_w1",
+                    **kwargs) -> "RoutedMoE":
+        """A layer from SGLang's processed TRT-LLM-gen MXFP4 weights (the layout
+        the reference's RoutedExpertGemm takes): re-laid once into canonical
+        copies (megamoe.layouts.trtllm_to_canonical); the processed tensors are
+        not read afterwards."""
+        from .layouts import trtllm_to_canonical
+
+        c13, c13s, c2, c2s = trtllm_to_canonical(w13, w13_scale, w2, w2_scale, halves=halves)
+        return cls(c13, c13s, c2, c2s, top_k, max_rows, **kwargs)
+
     def __del__(self):
         handle = getattr(self, "_handle", None)
         if handle is not None and handle.value:
