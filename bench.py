@@ -58,8 +58,8 @@ def parse_args():
     ap.add_argument("--config", choices=sorted(CONFIGS), default="2",
                     help="BASELINE config: 2 (MXFP4, hidden 7168, 384 + 1 experts) or 4 (NVFP4, hidden 6144, "
                          "256 + 1 experts; TP x EP2 at N > 1)")
-    ap.add_argument("--experts", type=int, default=384,
-                    help="routed experts (384 = config 2; fewer only for small profiling cases)")
+    ap.add_argument("--experts", type=int, default=None,
+                    help="routed experts (default: the config's; fewer only for small profiling cases)")
     ap.add_argument("--impl", choices=["mm", "reference"], default="mm")
     ap.add_argument("--combine", choices=["peer", "nccl"], default="peer",
                     help="N > 1: fused combine + peer all-reduce (default) or NCCL all-reduce of fp32 partials")
@@ -219,7 +219,7 @@ def run_mm(args):
 
     global H, I, E
     H, I, E, fmt = CONFIGS[args.config]
-    if args.config == "2":
+    if args.experts is not None:
         E = args.experts
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
