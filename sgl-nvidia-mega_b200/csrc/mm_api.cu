@@ -126,12 +126,26 @@ int64_t mm_route_words(int32_t tokens, int32_t top_k, int32_t experts) {
   return route_words(tokens, top_k, experts);
 }
 
+// The router launch's shared memory reaches 8 x H bf16 rows of x: raise the
+// kernel's dynamic shared memory limit once per device.
+static cudaError_t router_smem_attr() {
+  static bool done[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) return e;
+  if (done[dev]) return cudaSuccess;
+  e = cudaFuncSetAttribute(router_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(router_smem_bytes(kMaxRouterHidden)));
+  if (e == cudaSuccess) done[dev] = true;
+  return e;
+}
+
 int mm_router_gemv(const uint16_t *x, const uint16_t *w, float *logits, int32_t tokens,
                    int32_t experts, int32_t hidden, void *stream) {
   if (!x || !w || !logits) return fail(MM_ERR_INVALID, "mm_router_gemv: null pointer");
-  if (tokens < 1 || experts < 1 || hidden < 1024 || hidden % 1024 || hidden > 1024 * kMaxRouterParts)
+  if (tokens < 1 || experts < 1 || hidden < 1024 || hidden % 1024 || hidden > kMaxRouterHidden)
     return fail(MM_ERR_INVALID, "mm_router_gemv: tokens %d experts %d hidden %d (hidden %% 1024 == 0, <= %d)",
-                tokens, experts, hidden, 1024 * kMaxRouterParts);
+                tokens, experts, hidden, kMaxRouterHidden);
   if (!aligned(x, 16) || !aligned(w, 16)) return fail(MM_ERR_INVALID, "mm_router_gemv: x and w must be 16-byte aligned");
   RouterArgs a = {};
   a.x = x;
@@ -140,9 +154,10 @@ int mm_router_gemv(const uint16_t *x, const uint16_t *w, float *logits, int32_t 
   a.tokens = tokens;
   a.experts = experts;
   a.hidden = hidden;
-  a.gemv_ctas = experts;
-  dim3 grid(experts, (tokens + 7) / 8);
-  MM_CUDA(launch(router_quant_kernel, grid, dim3(256), 0, stream, a));
+  a.gemv_ctas = (experts + 3) / 4;
+  MM_CUDA(router_smem_attr());
+  dim3 grid(a.gemv_ctas, (tokens + 7) / 8);
+  MM_CUDA(launch(router_quant_kernel, grid, dim3(256), router_smem_bytes(hidden), stream, a));
   return MM_OK;
 }
 
@@ -495,8 +510,8 @@ static cudaError_t launch_experts(mm_layer *L, const ExpertArgs &ea, void *strea
 // of x into the layer's scratch (extra CTAs of the same grid).
 static int launch_router_quant(mm_layer *L, const uint16_t *x, const uint16_t *w, float *logits, int tokens,
                                void *stream) {
-  if (w && (L->H % 1024 || L->H > 1024 * kMaxRouterParts))
-    return fail(MM_ERR_INVALID, "router GEMV: hidden %d must be a multiple of 1024, <= %d", L->H, 1024 * kMaxRouterParts);
+  if (w && (L->H % 1024 || L->H > kMaxRouterHidden))
+    return fail(MM_ERR_INVALID, "router GEMV: hidden %d must be a multiple of 1024, <= %d", L->H, kMaxRouterHidden);
   if (w && !aligned(w, 16)) return fail(MM_ERR_INVALID, "router weight must be 16-byte aligned");
   RouterArgs a = {};
   a.x = x;
@@ -505,7 +520,7 @@ static int launch_router_quant(mm_layer *L, const uint16_t *x, const uint16_t *w
   a.tokens = tokens;
   a.experts = L->R;
   a.hidden = L->H;
-  a.gemv_ctas = w ? L->R : 0;
+  a.gemv_ctas = w ? (L->R + 3) / 4 : 0;
   a.xq = L->xq;
   a.xs = L->xs;
   a.max_tokens = L->Tmax;
@@ -515,7 +530,8 @@ static int launch_router_quant(mm_layer *L, const uint16_t *x, const uint16_t *w
   a.inv_gs = L->fmt == kFmtNv ? L->d.input_scale[0] : 1.0f;
   const int quant_ctas = (tokens * (L->H / 32) + 255) / 256;
   dim3 grid(a.gemv_ctas + quant_ctas, w ? (tokens + 7) / 8 : 1);
-  MM_CUDA(launch(router_quant_kernel, grid, dim3(256), 0, stream, a));
+  if (w) MM_CUDA(router_smem_attr());
+  MM_CUDA(launch(router_quant_kernel, grid, dim3(256), w ? router_smem_bytes(L->H) : 0, stream, a));
   return MM_OK;
 }
 

@@ -46,7 +46,8 @@ struct FrontArgs {
   RouteArgs route;
 };
 
-constexpr int kMaxRouterParts = 16;  // H <= 16384 for the router GEMV
+constexpr int kMaxRouterParts = 14;  // H <= 14336 for the router GEMV (x tile in shared memory)
+constexpr int kMaxRouterHidden = 1024 * kMaxRouterParts;
 
 struct RouterArgs {
   const uint16_t *x;         // bf16 [T, H]
@@ -185,6 +186,11 @@ cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
 
 // Host helpers shared by the .cu files (mm_api.cu defines them).
 int set_error(int code, const char *fmt, ...);
+// dynamic shared memory of the router launch for hidden size H: 8 token rows
+// of x (bf16) and the part sums of a 4-expert x 8-token tile
+inline size_t router_smem_bytes(int hidden) {
+  return static_cast<size_t>(8) * hidden * 2 + static_cast<size_t>(4) * kMaxRouterParts * 8 * 4;
+}
 // dynamic shared memory of the route build for (tokens, local experts)
 inline size_t route_smem_size(int tokens, int experts) {
   const int words = (tokens + 31) / 32;

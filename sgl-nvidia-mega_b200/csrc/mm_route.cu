@@ -24,14 +24,15 @@ namespace mm {
 // K0: router GEMV + routed-input quantization in one launch.
 //
 // CTAs [0, gemv_ctas) x grid.y: logits[t, e] = sum_h x[t, h] w[e, h] (fp32) for
-// expert e = blockIdx.x and the 8 tokens of chunk blockIdx.y. Summation order
-// (the CPU oracle replays it): H is cut in parts of 1024; part p belongs to warp
-// p % 8; lane l of a part accumulates, for j = 0..3 and i = 0..7, the element
+// experts [4 blockIdx.x, +4) and the 8 tokens of chunk blockIdx.y. Summation
+// order (the CPU oracle replays it): H is cut in parts of 1024; lane l of a
+// part accumulates, for j = 0..3 and i = 0..7, the element
 // h = 1024 p + 8 (l + 32 j) + i with acc = fma(x, w, acc) from acc = 0; the 32
 // lane sums are combined by the butterfly acc += shfl_xor(acc, 16, 8, 4, 2, 1);
 // the part sums in part order, s = ((p0 + p1) + p2) + ... bf16 x bf16 products
-// are exact in fp32. The weight row is static, so its loads are issued before
-// the grid-dependency wait.
+// are exact in fp32. The weight rows are static, so the first part's loads
+// are issued before the grid-dependency wait. Dynamic shared memory:
+// router_smem_bytes(H).
 //
 // CTAs [gemv_ctas, ...) (blockIdx.y == 0): the FP4 terms of x, one 32-element
 // chunk of one token per thread (one MXFP4 block or two NVFP4 blocks;
@@ -72,71 +73,104 @@ __global__ void __launch_bounds__(256) router_quant_kernel(RouterArgs a) {
     }
     return;
   }
-  __shared__ float part_sum[kMaxRouterParts][8];
-  const int e = blockIdx.x;
+  // GEMV tile: experts [4 blockIdx.x, +4) x tokens [8 blockIdx.y, +8). The 8
+  // token rows of x are staged once in shared memory (cp.async) and read by
+  // all four experts; warp w computes expert slot w % 4 over the parts of
+  // parity w / 4, keeping each part's sum; one thread per (expert, token)
+  // then adds the parts in part order.
+  extern __shared__ __align__(16) unsigned char router_smem[];
+  uint16_t *xs = reinterpret_cast<uint16_t *>(router_smem);                  // [8][H] bf16
+  float *part_val = reinterpret_cast<float *>(router_smem + 8 * a.hidden * 2);  // [4][kMaxRouterParts][8]
   const int t0 = blockIdx.y * 8;
   const int nt = min(8, a.tokens - t0);
   const int parts = a.hidden >> 10;
-  // the weight row first (static): four 16-byte vectors per lane and part
-  uint4 wv[kMaxRouterParts / 8][4];
+  const int es = warp & 3, pp = warp >> 2;
+  const int e = blockIdx.x * 4 + es;
+  const bool have_e = e < a.experts;
+  // the warp's weight parts are static: their loads go before the
+  // grid-dependency wait, the first kPreParts of them (all of them for
+  // H <= 8192) into registers; any further part is loaded when reached
+  constexpr int kPreParts = 4;
+  constexpr int kWarpParts = (kMaxRouterParts + 1) / 2;
+  uint4 wv[kPreParts][4];
 #pragma unroll
-  for (int pi = 0; pi < kMaxRouterParts / 8; ++pi) {
-    const int part = warp + 8 * pi;
+  for (int k = 0; k < kPreParts; ++k) {
+    const int part = pp + 2 * k;
 #pragma unroll
     for (int j = 0; j < 4; ++j)
-      wv[pi][j] = part < parts ? __ldg(reinterpret_cast<const uint4 *>(a.w + static_cast<size_t>(e) * a.hidden +
-                                                                       1024 * part) + lane + 32 * j)
-                               : make_uint4(0u, 0u, 0u, 0u);
+      wv[k][j] = have_e && part < parts
+                     ? __ldg(reinterpret_cast<const uint4 *>(a.w + static_cast<size_t>(e) * a.hidden + 1024 * part) +
+                             lane + 32 * j)
+                     : make_uint4(0u, 0u, 0u, 0u);
   }
   pdl_wait();
+  {
+    const int per_row = a.hidden >> 3;  // uint4 per token row
+    const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(xs));
+    for (int i = threadIdx.x; i < nt * per_row; i += blockDim.x) {
+      const int t = i / per_row, c = i - t * per_row;
+      cp_async_16(sbase + 16u * static_cast<uint32_t>(i),
+                  reinterpret_cast<const uint4 *>(a.x + static_cast<size_t>(t0 + t) * a.hidden) + c, 16u);
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();
+  }
+  if (have_e) {
 #pragma unroll
-  for (int pi = 0; pi < kMaxRouterParts / 8; ++pi) {
-    const int part = warp + 8 * pi;
-    if (part >= parts) break;
-    float acc[8];
-#pragma unroll
-    for (int tt = 0; tt < 8; tt += 2) {
-      uint4 xv[2][4];
-#pragma unroll
-      for (int u = 0; u < 2; ++u)
+    for (int k = 0; k < kWarpParts; ++k) {
+      const int part = pp + 2 * k;
+      if (part >= parts) break;
+      uint4 wlate[4];
+      if (k >= kPreParts) {
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-          xv[u][j] = (tt + u < nt) ? __ldg(reinterpret_cast<const uint4 *>(a.x + static_cast<size_t>(t0 + tt + u) * a.hidden +
-                                                                           1024 * part) + lane + 32 * j)
-                                   : make_uint4(0u, 0u, 0u, 0u);
+          wlate[j] = __ldg(reinterpret_cast<const uint4 *>(a.w + static_cast<size_t>(e) * a.hidden + 1024 * part) +
+                           lane + 32 * j);
+      }
+      const uint4 *wcur = k < kPreParts ? wv[k] : wlate;
+      // the 8 tokens' chains interleaved (independent accumulators; each token's
+      // own accumulation order is the one above); rows t >= nt are stale smem
+      // and never stored
+      const uint4 *xr = reinterpret_cast<const uint4 *>(xs + 1024 * part);
+      const int row_u4 = a.hidden >> 3;
+      float sacc[8];
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        float s = 0.0f;
+      for (int t = 0; t < 8; ++t) sacc[t] = 0.0f;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint32_t xq[4] = {xv[u][j].x, xv[u][j].y, xv[u][j].z, xv[u][j].w};
-          const uint32_t wq[4] = {wv[pi][j].x, wv[pi][j].y, wv[pi][j].z, wv[pi][j].w};
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t wq[4] = {wcur[j].x, wcur[j].y, wcur[j].z, wcur[j].w};
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          const uint4 xv = xr[t * row_u4 + lane + 32 * j];
+          const uint32_t xq[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            s = __fmaf_rn(__uint_as_float(xq[q] << 16), __uint_as_float(wq[q] << 16), s);
-            s = __fmaf_rn(__uint_as_float(xq[q] & 0xffff0000u), __uint_as_float(wq[q] & 0xffff0000u), s);
+            sacc[t] = __fmaf_rn(__uint_as_float(xq[q] << 16), __uint_as_float(wq[q] << 16), sacc[t]);
+            sacc[t] = __fmaf_rn(__uint_as_float(xq[q] & 0xffff0000u), __uint_as_float(wq[q] & 0xffff0000u), sacc[t]);
           }
         }
-        acc[tt + u] = s;
       }
-    }
-#pragma unroll
-    for (int tt = 0; tt < 8; ++tt) {
 #pragma unroll
       for (int off = 16; off >= 1; off >>= 1)
-        acc[tt] = __fadd_rn(acc[tt], __shfl_xor_sync(0xffffffffu, acc[tt], off));
-    }
-    if (lane == 0) {
 #pragma unroll
-      for (int tt = 0; tt < 8; ++tt) part_sum[part][tt] = acc[tt];
+        for (int t = 0; t < 8; ++t) sacc[t] = __fadd_rn(sacc[t], __shfl_xor_sync(0xffffffffu, sacc[t], off));
+      if (lane < nt) {
+        float v = sacc[0];
+#pragma unroll
+        for (int t = 1; t < 8; ++t) v = lane == t ? sacc[t] : v;
+        part_val[(es * kMaxRouterParts + part) * 8 + lane] = v;
+      }
     }
   }
   __syncthreads();
-  if (static_cast<int>(threadIdx.x) < nt) {
-    const int tt = threadIdx.x;
-    float s = part_sum[0][tt];
-    for (int p = 1; p < parts; ++p) s = __fadd_rn(s, part_sum[p][tt]);
-    a.logits[static_cast<size_t>(t0 + tt) * a.experts + e] = s;
+  if (static_cast<int>(threadIdx.x) < 4 * nt) {
+    const int es2 = threadIdx.x / nt, tt = threadIdx.x - es2 * nt;
+    const int e2 = blockIdx.x * 4 + es2;
+    if (e2 < a.experts) {
+      float sum = part_val[(es2 * kMaxRouterParts) * 8 + tt];
+      for (int p2 = 1; p2 < parts; ++p2) sum = __fadd_rn(sum, part_val[(es2 * kMaxRouterParts + p2) * 8 + tt]);
+      a.logits[static_cast<size_t>(t0 + tt) * a.experts + e2] = sum;
+    }
   }
 }
 
@@ -153,14 +187,6 @@ struct GateSmem {
 __device__ __forceinline__ unsigned long long pack_key(uint32_t key, int e) {
   return (static_cast<unsigned long long>(key) << 32) | static_cast<uint32_t>(0xffffffffu - e);
 }
-__device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long v) {
-#pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) {
-    const unsigned long long o = __shfl_xor_sync(0xffffffffu, v, off);
-    v = o > v ? o : v;
-  }
-  return v;
-}
 
 // Computes ids/weights of row `row` and writes them to ids_out/weights_out.
 __device__ void gate_row(const GateArgs &g, int row, int valid_rows, GateSmem &sm) {
@@ -175,11 +201,11 @@ __device__ void gate_row(const GateArgs &g, int row, int valid_rows, GateSmem &s
     alt = token == g.alt_token_id;
   }
   const float *bias = alt && g.bias_alt != nullptr ? g.bias_alt : g.bias;
-  unsigned long long pk[2];
+  uint32_t kv[2];  // routing key + 1 of experts tid, tid + 512; 0: none or taken
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     const int e = tid + 512 * h;
-    pk[h] = 0ull;
+    kv[h] = 0u;
     if (e < E) {
       const float l = lrow[e];
       const float b = bias != nullptr ? bias[e] : 0.0f;
@@ -189,37 +215,61 @@ __device__ void gate_row(const GateArgs &g, int row, int valid_rows, GateSmem &s
       else s = l;  // softmax: rank the (biased) logits
       sm.score[e] = s;
       sm.logit[e] = l;
-      pk[h] = pack_key(routing_key(__fadd_rn(s, b)), e);
+      kv[h] = routing_key(__fadd_rn(s, b)) + 1u;  // keys of real scores stay below 0xff800001
     }
   }
-  // per-warp top-K candidates (every global winner is in its warp's top-K)
+  // per-warp top-K candidates (every global winner is in its warp's top-K): the
+  // largest key by a warp reduction, the lowest expert id among its holders by
+  // ballot (experts tid < 512 precede tid + 512, and lanes ascend within each)
   for (int k = 0; k < K; ++k) {
-    const unsigned long long mine = pk[0] > pk[1] ? pk[0] : pk[1];
-    const unsigned long long top = warp_max_u64(mine);
+    const uint32_t m = __reduce_max_sync(0xffffffffu, kv[0] > kv[1] ? kv[0] : kv[1]);
+    unsigned long long top = 0ull;
+    if (m != 0u) {
+      const uint32_t b0 = __ballot_sync(0xffffffffu, kv[0] == m);
+      int win;
+      if (b0 != 0u) {
+        const int l = __ffs(b0) - 1;
+        win = warp * 32 + l;
+        if (lane == l) kv[0] = 0u;
+      } else {
+        const int l = __ffs(__ballot_sync(0xffffffffu, kv[1] == m)) - 1;
+        win = 512 + warp * 32 + l;
+        if (lane == l) kv[1] = 0u;
+      }
+      top = pack_key(m - 1u, win);
+    }
     if (lane == 0) sm.cand[warp][k] = top;
-    if (pk[0] == top) pk[0] = 0ull;
-    if (pk[1] == top) pk[1] = 0ull;
   }
   __syncthreads();
   if (warp == 0) {
     // merge 16 warps x K candidates: lane l holds warps' entries l, l+32, ...
+    // (a candidate is key + 1 and expert id; key 0: empty or taken). Each
+    // round: the largest key by a warp reduction, then the lowest expert id
+    // among its holders by a second one -- the same pick as the largest
+    // packed (key, ~id).
     constexpr int kPer = 16 * kMaxTopK / 32;
-    unsigned long long c[kPer];
+    uint32_t ckey[kPer], cid[kPer];
 #pragma unroll
     for (int j = 0; j < kPer; ++j) {
       const int idx = lane + 32 * j;  // idx = warp_id * kMaxTopK + k
       const int cw = idx / kMaxTopK, ck = idx % kMaxTopK;
-      c[j] = (ck < K) ? sm.cand[cw][ck] : 0ull;
+      const unsigned long long c = (ck < K) ? sm.cand[cw][ck] : 0ull;
+      ckey[j] = c == 0ull ? 0u : static_cast<uint32_t>(c >> 32) + 1u;
+      cid[j] = 0xffffffffu - static_cast<uint32_t>(c);
     }
     for (int k = 0; k < K; ++k) {
-      unsigned long long best = 0ull;
+      uint32_t lm = 0u;
 #pragma unroll
-      for (int j = 0; j < kPer; ++j) best = c[j] > best ? c[j] : best;
-      const unsigned long long top = warp_max_u64(best);
+      for (int j = 0; j < kPer; ++j) lm = ckey[j] > lm ? ckey[j] : lm;
+      const uint32_t m = __reduce_max_sync(0xffffffffu, lm);
+      uint32_t lid = 0xffffffffu;
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) lid = (m != 0u && ckey[j] == m && cid[j] < lid) ? cid[j] : lid;
+      const uint32_t wid = __reduce_min_sync(0xffffffffu, lid);
 #pragma unroll
       for (int j = 0; j < kPer; ++j)
-        if (c[j] == top) c[j] = 0ull;
-      if (lane == 0) sm.sel[k] = static_cast<int>(0xffffffffu - static_cast<uint32_t>(top));
+        if (ckey[j] == m && cid[j] == wid) ckey[j] = 0u;
+      if (lane == 0) sm.sel[k] = static_cast<int>(wid);  // 0xffffffff (-1) when nothing is left
     }
     __syncwarp();
     if (lane == 0) {
@@ -425,9 +475,9 @@ __global__ void __launch_bounds__(512) front_kernel(FrontArgs f) {
     const int valid = f.gate.num_valid != nullptr ? *f.gate.num_valid : f.route.tokens;
     gate_row(f.gate, row, valid, gsm);
   }
-  __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == 0) {  // thread 0 (warp 0, lane 0) wrote the row's ids and weights
+    __threadfence();
     const int ticket = atomicAdd(&f.route.ctrl[kCtrlTicket], 1);
     is_last = ticket == static_cast<int>(gridDim.x) - 1;
   }
