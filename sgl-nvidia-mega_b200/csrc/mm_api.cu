@@ -274,8 +274,8 @@ int mm_layer_create(const mm_layer_desc *desc, mm_layer **out) {
   *out = nullptr;
   const mm_layer_desc &d = *desc;
   if (d.hidden < 256 || d.hidden % 256) return fail(MM_ERR_INVALID, "hidden %d must be a positive multiple of 256", d.hidden);
-  if (d.intermediate < 256 || d.intermediate % 256)
-    return fail(MM_ERR_INVALID, "intermediate %d must be a positive multiple of 256", d.intermediate);
+  if (d.intermediate < 64 || d.intermediate % 64)
+    return fail(MM_ERR_INVALID, "intermediate %d must be a positive multiple of 64", d.intermediate);
   if (d.experts < 1 || d.experts > kMaxRouterExperts) return fail(MM_ERR_INVALID, "experts %d outside 1..%d", d.experts, kMaxRouterExperts);
   if (d.router_experts < d.experts || d.router_experts > kMaxRouterExperts)
     return fail(MM_ERR_INVALID, "router_experts %d outside experts..%d", d.router_experts, kMaxRouterExperts);
@@ -325,7 +325,7 @@ int mm_layer_create(const mm_layer_desc *desc, mm_layer **out) {
   L->m1 = L->I / 64;
   L->m2 = L->H / 128;
   L->ks1 = L->H / kStageK;
-  L->ks2 = L->I / kStageK;
+  L->ks2 = (L->I + kStageK - 1) / kStageK;  // the down GEMM's last stage may be partial
   L->max_ctas = route_max_ctas(L->Tmax, L->K, L->E);
   L->shared_row_base = kTile * L->max_ctas;
   L->rows_cap = L->shared_row_base + L->Tmax;
@@ -361,7 +361,10 @@ int mm_layer_create(const mm_layer_desc *desc, mm_layer **out) {
   if (nv) ALLOC(L->alpha, sizeof(float) * (2 * E + 2));
   const size_t xq_bytes = kMaxTerms * static_cast<size_t>(L->Tmax) * H / 2;
   const size_t hq_bytes = kMaxTerms * static_cast<size_t>(L->rows_cap) * I / 2;
-  const size_t xs_bytes = xq_bytes * 2 / L->block, hs_bytes = hq_bytes * 2 / L->block;
+  // h scale rows padded to 4 bytes so the 4-byte scale gathers stay aligned for any I % 64 == 0
+  const int hs_row = (L->I / L->block + 3) / 4 * 4;
+  const size_t xs_bytes = xq_bytes * 2 / L->block;
+  const size_t hs_bytes = kMaxTerms * static_cast<size_t>(L->rows_cap) * hs_row;
   ALLOC(L->xq, xq_bytes);
   ALLOC(L->xs, xs_bytes);
   ALLOC(L->hq, hq_bytes);
@@ -389,7 +392,7 @@ int mm_layer_create(const mm_layer_desc *desc, mm_layer **out) {
 
   // scale repack (once): canonical scales -> UMMA scale chunks
   auto repack = [&](const void *src, uint8_t *dst, int n, int rows, int k, int gate_up) -> int {
-    const size_t total = static_cast<size_t>(n) * (rows / 128) * (k / kStageK) * sfs;
+    const size_t total = static_cast<size_t>(n) * (rows / 128) * ((k + kStageK - 1) / kStageK) * sfs;
     const int blocks = static_cast<int>(total / 256 < 65536 ? (total + 255) / 256 : 65536);
     repack_scales_kernel<<<blocks, 256>>>(static_cast<const uint8_t *>(src), dst, n, rows, k, gate_up, L->I,
                                           L->block);
@@ -442,6 +445,7 @@ int mm_layer_create(const mm_layer_desc *desc, mm_layer **out) {
   ea.xs = L->xs;
   ea.hq = L->hq;
   ea.hs = L->hs;
+  ea.hs_row = hs_row;
   ea.segs = L->segs;
   ea.ctrl = L->ctrl;
   ea.flags = L->flags;

@@ -388,6 +388,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
     uint32_t soff[kPieces], doff[kPieces], sbytes[kPieces];
     uint32_t s_soff[2 * kC], s_doff[2 * kC], s_bytes[2 * kC];
     int nb = 0;
+    uint32_t k_bytes = 0, k_cols = 0;  // the unit's K in packed bytes and in scale columns
     const uint8_t *dq = nullptr, *dsc = nullptr;
 #pragma unroll 1
     while (true) {
@@ -430,8 +431,12 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
         dq = g2 ? p.hq : p.xq;
         dsc = g2 ? p.hs : p.xs;
         const uint32_t rowb = static_cast<uint32_t>(K) >> 1;  // packed bytes per row
+        k_bytes = rowb;
+        k_cols = static_cast<uint32_t>(K / L::kBlock);
         const uint32_t term_q = static_cast<uint32_t>(g2 ? p.rows_cap : p.max_tokens) * rowb;
-        const uint32_t term_s = term_q / (L::kBlock / 2);
+        // scale rows: x's are H / block bytes (a multiple of 8), h's padded to hs_row
+        const uint32_t srow = g2 ? static_cast<uint32_t>(p.hs_row) : static_cast<uint32_t>(K / L::kBlock);
+        const uint32_t term_s = static_cast<uint32_t>(g2 ? p.rows_cap : p.max_tokens) * srow;
 #pragma unroll
         for (int i = 0; i < kPieces; ++i) {
           const int rr = quarter + 4 * i;
@@ -452,7 +457,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
 #pragma unroll
           for (int c = 0; c < kC; ++c) {
             s_soff[kC * h + c] =
-                static_cast<uint32_t>(t) * term_s + static_cast<uint32_t>(sr) * (K / L::kBlock) + c * 4;
+                static_cast<uint32_t>(t) * term_s + static_cast<uint32_t>(sr) * srow + c * 4;
             s_doff[kC * h + c] = c * 512 + (rr & 31) * 16 + (rr >> 5) * 4;
             s_bytes[kC * h + c] = (rr < nb && r < rows) ? 4u : 0u;
           }
@@ -467,17 +472,34 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
         if (!oke) break;
         const uint32_t sb = base + L::kSmemB + stage * kBStageBytes;
         const uint8_t *gq = dq + ks * kRowBytes;
+        // a partial last stage (K not a multiple of 256): pieces past K zero-fill
+        const bool partial = static_cast<uint32_t>((ks + 1) * kRowBytes) > k_bytes;
+        const bool piece_in_k = !partial || static_cast<uint32_t>(ks * kRowBytes + pc * 16) < k_bytes;
 #pragma unroll
         for (int i = 0; i < kPieces; ++i) {
-          if (quarter + 4 * i < nb) cp_async_16(sb + doff[i], gq + soff[i], sbytes[i]);
+          if (quarter + 4 * i < nb) {
+            if (piece_in_k) cp_async_16(sb + doff[i], gq + soff[i], sbytes[i]);
+            else cp_async_16(sb + doff[i], dq, 0u);  // past K: zero-fill, nothing read
+          }
         }
         const uint32_t ssb = base + L::kSmemSfb + stage * L::kSfStageBytes;
         const uint8_t *gs = dsc + ks * L::kSfRow;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           if (lane + 32 * h < nb) {
+            if (!partial) {
 #pragma unroll
-            for (int c = 0; c < kC; ++c) cp_async_4(ssb + s_doff[kC * h + c], gs + s_soff[kC * h + c], s_bytes[kC * h + c]);
+              for (int c = 0; c < kC; ++c) cp_async_4(ssb + s_doff[kC * h + c], gs + s_soff[kC * h + c], s_bytes[kC * h + c]);
+            } else {
+#pragma unroll
+              for (int c = 0; c < kC; ++c) {
+                // scale columns past K zero-fill, a piece partly
+                const int left = static_cast<int>(k_cols) - (ks * L::kSfRow + 4 * c);
+                const uint32_t nbytes = left <= 0 ? 0u : (left >= 4 ? s_bytes[kC * h + c]
+                                                                    : (s_bytes[kC * h + c] ? static_cast<uint32_t>(left) : 0u));
+                cp_async_4(ssb + s_doff[kC * h + c], nbytes != 0u ? gs + s_soff[kC * h + c] : dsc, nbytes);
+              }
+            }
           }
         }
         cp_async_arrive_noinc(bar(kBarFull + stage));
@@ -570,7 +592,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
           const int f = 64 * m + 32 * q + lane;  // feature (column of h)
           const size_t rowb = static_cast<size_t>(p.inter) >> 1;
           const size_t tq = static_cast<size_t>(p.rows_cap) * rowb;  // term stride of hq
-          const size_t ts = tq / (L::kBlock / 2);                     // term stride of hs
+          const size_t ts = static_cast<size_t>(p.rows_cap) * p.hs_row;  // term stride of hs
 #pragma unroll
           for (int j = 0; j < kSegRows; ++j) {
             if (j >= rows) break;
@@ -603,7 +625,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
               const uint32_t up_nib = __shfl_down_sync(0xffffffffu, nib, 1);
               if ((lane & 1) == 0) p.hq[t * tq + prow * rowb + (f >> 1)] = static_cast<uint8_t>(nib | (up_nib << 4));
               if ((lane & (L::kBlock - 1)) == 0)
-                p.hs[t * ts + prow * (p.inter / L::kBlock) + f / L::kBlock] = static_cast<uint8_t>(code);
+                p.hs[t * ts + prow * p.hs_row + f / L::kBlock] = static_cast<uint8_t>(code);
             }
           }
           // publish this warp's 32 features of every row: two increments per unit
@@ -655,9 +677,10 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
 // ============================================================================
 __global__ void repack_scales_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst,
                                      int n, int rows, int k, int gate_up, int inter, int block) {
-  const int ks_n = k / kStageK;
+  const int ks_n = (k + kStageK - 1) / kStageK;  // a partial last stage gets zero scales past k
   const int tiles = rows / 128;
   const int per_row = kStageK / block;          // scale bytes of a row per stage
+  const int cols = k / block;                   // scale columns of a row
   const int stage_bytes = per_row * 128;        // = chunks * 512
   const size_t total = static_cast<size_t>(n) * tiles * ks_n * stage_bytes;
   for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
@@ -673,7 +696,7 @@ __global__ void repack_scales_kernel(const uint8_t *__restrict__ src, uint8_t *_
     const int r = m0 + 32 * m1;
     const int kb = ks * per_row + 4 * c + kk;
     const int srow = gate_up ? (r < 64 ? 64 * t + r : inter + 64 * t + (r - 64)) : 128 * t + r;
-    dst[idx] = src[(static_cast<size_t>(e) * rows + srow) * (k / block) + kb];
+    dst[idx] = kb < cols ? src[(static_cast<size_t>(e) * rows + srow) * cols + kb] : static_cast<uint8_t>(0);
   }
 }
 

@@ -305,6 +305,26 @@ def test_experts_balanced_dealing_groups_sum_to_the_layer():
     assert O.max_abs_rel(total.float().cpu().numpy(), ex.numpy()) <= OUT_TOL
 
 
+@pytest.mark.parametrize("fmt", ["mxfp4", "nvfp4"])
+@pytest.mark.parametrize("I", [576, 640])
+@pytest.mark.parametrize("T,distinct", [(8, None), (40, 6)])
+def test_experts_dsv41_geometry(fmt, I, T, distinct):
+    """DeepSeek-V4.1's own geometry (routed_expert_gemm.py:31-40): hidden 5120,
+    an intermediate slice of 576 (or its 640 padding), top-6; the down GEMM's K
+    is not a multiple of the 256-wide pipeline stage, so its last stage is
+    partial (zero-filled past K)."""
+    H, E, K = 5120, 32, 6
+    if fmt == "nvfp4":
+        layer = O.make_nvfp4_layer(H, I, E, shared=True, seed=I + T)
+    else:
+        layer = O.make_layer(H, I, E, shared=True, seed=I + T)
+    x, _, _ = O.make_inputs(T, H, E, seed=I + T)
+    g = torch.Generator().manual_seed(I + T)
+    ids = _random_ids(T, K, E, g, distinct)
+    w = torch.rand((T, K), generator=g)
+    _run_and_check(layer, x, ids, w, K, max_rows=64)
+
+
 def test_experts_expert_parallel_window():
     """EP: the rank holds experts [16, 32) of 32; other slots map to -1."""
     H, I, E, K, T = 1024, 256, 32, 4, 8
