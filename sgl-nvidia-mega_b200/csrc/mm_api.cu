@@ -360,9 +360,12 @@ int mm_layer_create(const mm_layer_desc *desc, mm_layer **out) {
   }
   if (nv) ALLOC(L->alpha, sizeof(float) * (2 * E + 2));
   const size_t xq_bytes = kMaxTerms * static_cast<size_t>(L->Tmax) * H / 2;
-  const size_t hq_bytes = kMaxTerms * static_cast<size_t>(L->rows_cap) * I / 2;
-  // h scale rows padded to 4 bytes so the 4-byte scale gathers stay aligned for any I % 64 == 0
-  const int hs_row = (L->I / L->block + 3) / 4 * 4;
+  // h rows are padded to whole K stages (256 features): the pad is zeroed here and never
+  // written, so the down GEMM's partial last stage (I % 256 != 0) reads zero codes and
+  // scales and its loader needs no K bound
+  const int hq_row = L->ks2 * (kStageK / 2);
+  const int hs_row = L->ks2 * (kStageK / L->block);
+  const size_t hq_bytes = kMaxTerms * static_cast<size_t>(L->rows_cap) * hq_row;
   const size_t xs_bytes = xq_bytes * 2 / L->block;
   const size_t hs_bytes = kMaxTerms * static_cast<size_t>(L->rows_cap) * hs_row;
   ALLOC(L->xq, xq_bytes);
@@ -445,6 +448,7 @@ int mm_layer_create(const mm_layer_desc *desc, mm_layer **out) {
   ea.xs = L->xs;
   ea.hq = L->hq;
   ea.hs = L->hs;
+  ea.hq_row = hq_row;
   ea.hs_row = hs_row;
   ea.segs = L->segs;
   ea.ctrl = L->ctrl;

@@ -388,7 +388,6 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
     uint32_t soff[kPieces], doff[kPieces], sbytes[kPieces];
     uint32_t s_soff[2 * kC], s_doff[2 * kC], s_bytes[2 * kC];
     int nb = 0;
-    uint32_t k_bytes = 0, k_cols = 0;  // the unit's K in packed bytes and in scale columns
     const uint8_t *dq = nullptr, *dsc = nullptr;
 #pragma unroll 1
     while (true) {
@@ -430,11 +429,10 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
         const int K = g2 ? p.inter : p.hidden;
         dq = g2 ? p.hq : p.xq;
         dsc = g2 ? p.hs : p.xs;
-        const uint32_t rowb = static_cast<uint32_t>(K) >> 1;  // packed bytes per row
-        k_bytes = rowb;
-        k_cols = static_cast<uint32_t>(K / L::kBlock);
+        // packed bytes and scale bytes per row: x's rows are exactly H (a multiple of 256);
+        // h's are padded to whole stages and zero past I
+        const uint32_t rowb = g2 ? static_cast<uint32_t>(p.hq_row) : static_cast<uint32_t>(K) >> 1;
         const uint32_t term_q = static_cast<uint32_t>(g2 ? p.rows_cap : p.max_tokens) * rowb;
-        // scale rows: x's are H / block bytes (a multiple of 8), h's padded to hs_row
         const uint32_t srow = g2 ? static_cast<uint32_t>(p.hs_row) : static_cast<uint32_t>(K / L::kBlock);
         const uint32_t term_s = static_cast<uint32_t>(g2 ? p.rows_cap : p.max_tokens) * srow;
 #pragma unroll
@@ -472,34 +470,17 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
         if (!oke) break;
         const uint32_t sb = base + L::kSmemB + stage * kBStageBytes;
         const uint8_t *gq = dq + ks * kRowBytes;
-        // a partial last stage (K not a multiple of 256): pieces past K zero-fill
-        const bool partial = static_cast<uint32_t>((ks + 1) * kRowBytes) > k_bytes;
-        const bool piece_in_k = !partial || static_cast<uint32_t>(ks * kRowBytes + pc * 16) < k_bytes;
 #pragma unroll
         for (int i = 0; i < kPieces; ++i) {
-          if (quarter + 4 * i < nb) {
-            if (piece_in_k) cp_async_16(sb + doff[i], gq + soff[i], sbytes[i]);
-            else cp_async_16(sb + doff[i], dq, 0u);  // past K: zero-fill, nothing read
-          }
+          if (quarter + 4 * i < nb) cp_async_16(sb + doff[i], gq + soff[i], sbytes[i]);
         }
         const uint32_t ssb = base + L::kSmemSfb + stage * L::kSfStageBytes;
         const uint8_t *gs = dsc + ks * L::kSfRow;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           if (lane + 32 * h < nb) {
-            if (!partial) {
 #pragma unroll
-              for (int c = 0; c < kC; ++c) cp_async_4(ssb + s_doff[kC * h + c], gs + s_soff[kC * h + c], s_bytes[kC * h + c]);
-            } else {
-#pragma unroll
-              for (int c = 0; c < kC; ++c) {
-                // scale columns past K zero-fill, a piece partly
-                const int left = static_cast<int>(k_cols) - (ks * L::kSfRow + 4 * c);
-                const uint32_t nbytes = left <= 0 ? 0u : (left >= 4 ? s_bytes[kC * h + c]
-                                                                    : (s_bytes[kC * h + c] ? static_cast<uint32_t>(left) : 0u));
-                cp_async_4(ssb + s_doff[kC * h + c], nbytes != 0u ? gs + s_soff[kC * h + c] : dsc, nbytes);
-              }
-            }
+            for (int c = 0; c < kC; ++c) cp_async_4(ssb + s_doff[kC * h + c], gs + s_soff[kC * h + c], s_bytes[kC * h + c]);
           }
         }
         cp_async_arrive_noinc(bar(kBarFull + stage));
@@ -590,7 +571,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
           const bool clamped = lim != nullptr;
           const float L = clamped ? lim[sg.x < 0 ? 0 : sg.x] : 0.0f;
           const int f = 64 * m + 32 * q + lane;  // feature (column of h)
-          const size_t rowb = static_cast<size_t>(p.inter) >> 1;
+          const size_t rowb = static_cast<size_t>(p.hq_row);
           const size_t tq = static_cast<size_t>(p.rows_cap) * rowb;  // term stride of hq
           const size_t ts = static_cast<size_t>(p.rows_cap) * p.hs_row;  // term stride of hs
 #pragma unroll

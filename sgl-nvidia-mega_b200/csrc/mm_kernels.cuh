@@ -74,7 +74,7 @@ struct alignas(64) ExpertArgs {
   const uint8_t *ssfa2;
   const uint8_t *xq;         // [kMaxTerms][max_tokens][H/2]
   const uint8_t *xs;         // [kMaxTerms][max_tokens][H/block]
-  uint8_t *hq;               // [kMaxTerms][rows_cap][I/2]
+  uint8_t *hq;               // [kMaxTerms][rows_cap][hq_row]
   uint8_t *hs;               // [kMaxTerms][rows_cap][hs_row]
   // NVFP4 only: accumulator multipliers per expert (weight scale_2 x the
   // GEMM's input scale) and the down GEMM's input quantization scale
@@ -92,7 +92,7 @@ struct alignas(64) ExpertArgs {
   const float *clamp;        // [E] or null
   const float *shared_clamp; // [1] or null
   int hidden, inter, max_tokens, rows_cap, terms, token_off;
-  int hs_row;                // bytes per h scale row: I / block rounded up to 4 (aligned gathers)
+  int hq_row, hs_row;        // bytes per h row / h scale row: I rounded up to 256 features, zero past I
   int m1, m2, ks1, ks2;
 };
 
