@@ -18,7 +18,7 @@ the next of 64 resident token batches (distinct routings); one step streams
 ~1.4 GB of expert weights, far above the 126 MB L2, so no flush is needed.
 The e2e figure goes through the public API call with host buffers.
 
-Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mm|reference]
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mm|reference|flashinfer]
 Under torchrun each rank drives one GPU; rank 0 prints one JSON line.
 """
 
@@ -60,7 +60,11 @@ def parse_args():
                          "256 + 1 experts; TP x EP2 at N > 1)")
     ap.add_argument("--experts", type=int, default=None,
                     help="routed experts (default: the config's; fewer only for small profiling cases)")
-    ap.add_argument("--impl", choices=["mm", "reference"], default="mm")
+    ap.add_argument("--impl", choices=["mm", "reference", "flashinfer"], default="mm",
+                    help="mm: this library; reference: the CPU oracle port; flashinfer: SGLang's stock GPU path "
+                         "(FlashInfer TRT-LLM-gen fused MoE, a library) on the same workload, N = 1")
+    ap.add_argument("--fi-act", choices=["bf16", "mxfp8"], default="bf16",
+                    help="--impl flashinfer: activations bf16, or MXFP8 quantized before the timed region")
     ap.add_argument("--combine", choices=["peer", "nccl"], default="peer",
                     help="N > 1: fused combine + peer all-reduce (default) or NCCL all-reduce of fp32 partials")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -755,10 +759,151 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------------------------- flashinfer
+def run_flashinfer(args):
+    """SGLang's stock GPU path for this layer, as a same-box comparison: torch's router
+    GEMM (bf16 in, fp32 logits), FlashInfer's TRT-LLM-gen fused MoE with its own
+    DeepSeekV3-style routing (sigmoid + bias, one group, top-8, renormalize, x 2.5) and
+    finalize over the same MXFP4 weights (bf16 activations), the shared expert as a
+    second FlashInfer call, the sum. FlashInfer's tactic is autotuned once for the shape
+    (as a server does at warm-up). Also reports how far its output is from this
+    library's on the same inputs. Config 2, one GPU."""
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1 or args.config != "2":
+        if rank == 0:
+            print(json.dumps({"impl": "flashinfer", "unavailable": "the FlashInfer comparison runs config 2 on one GPU"}),
+                  flush=True)
+        return
+    sys.path.insert(0, os.path.join(REPO, "baseline"))
+    import flashinfer_moe  # sets FlashInfer's cache directory before flashinfer is imported
+
+    global E
+    if args.experts is not None:
+        E = args.experts
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    T = args.tokens if args.tokens is not None else 8
+    moe, w, shared, router, bias, xs, info = build_layer(0, 1, T, dev)
+    fl = flashinfer_moe.FlashInferLayer(*w, shared, bias, K, SCALE, T)
+    router_t = router.t()
+    try:
+        torch.mm(xs[0], router_t, out_dtype=torch.float32)
+
+        def logits_of(x):
+            return torch.mm(x, router_t, out_dtype=torch.float32)
+        router_kind = "torch.mm bf16 -> fp32 out"
+    except Exception:
+        router_f = router.float().t().contiguous()
+
+        def logits_of(x):
+            return torch.mm(x.float(), router_f)
+        router_kind = "torch.mm fp32"
+
+    mx = args.fi_act == "mxfp8"
+    xq = [flashinfer_moe.mxfp8_quantize(xs[i]) for i in range(POOL)] if mx else None
+
+    def step(x, i=None):
+        if mx:
+            return fl.forward(x, logits_of(x), *xq[i])
+        return fl.forward(x, logits_of(x))
+
+    from flashinfer.autotuner import autotune
+
+    with autotune(True):
+        step(xs[0], 0)
+    torch.cuda.synchronize()
+
+    # agreement with this library (both are checked separately: this one against the oracle)
+    errs = []
+    for i in range(8):
+        a = step(xs[i], i).float()
+        b = moe.forward(xs[i], router_weight=router, bias=bias, routed_scaling_factor=SCALE).float()
+        errs.append(float((a - b).abs().max() / b.abs().max()))
+    torch.cuda.synchronize()
+
+    for i in range(max(args.warmup, 3)):
+        step(xs[i % POOL], i % POOL)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clocks:
+        start.record()
+        for i in range(args.steps):
+            step(xs[i % POOL], i % POOL)
+        end.record()
+        torch.cuda.synchronize()
+    ms_step = start.elapsed_time(end) / args.steps
+
+    host_x = torch.empty((POOL, T, H), dtype=torch.bfloat16).pin_memory()
+    host_x.copy_(xs.cpu())
+    host_out = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
+    xdev = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    e2e_steps = min(args.steps, 1000)
+    torch.cuda.synchronize()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for i in range(e2e_steps):
+        xdev.copy_(host_x[i % POOL], non_blocking=True)
+        host_out.copy_(step(xdev, i % POOL), non_blocking=True)
+    e2.record()
+    torch.cuda.synchronize()
+    e2e_value = T * e2e_steps / (s2.elapsed_time(e2) / 1e3)
+
+    distinct = []
+    bufs = {}
+    for i in range(POOL):
+        moe.forward(xs[i], router_weight=router, bias=bias, routed_scaling_factor=SCALE, buffers=bufs)
+        distinct.append(int(torch.unique(bufs["ids"]).numel()))
+    torch.cuda.synchronize()
+    d_mean = float(np.mean(distinct))
+    layer_bytes = (d_mean + 1) * expert_bytes(H, I) + E * H * 2
+    peak, peak_kind = peaks()
+    line = {
+        "impl": "flashinfer",
+        "metric": METRIC,
+        "value": T / (ms_step / 1e3),
+        "unit": "tokens/s",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_step,
+        "us_per_layer": ms_step * 1e3,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": ("mxfp4 weights x mxfp8 activations (FlashInfer MxE2m1 x MxE4m3; x quantized before the timed "
+                  "region, e2e reuses the pool's codes)" if mx else
+                  "mxfp4 weights x bf16 activations (FlashInfer MxE2m1 x Bfloat16)"),
+        "data": "synthetic (the mm arm's seeded weights and token batches)",
+        "config": {
+            "workload": f"BASELINE config 2: one routed-MoE layer, hidden {H}, {E} routed + 1 shared experts, "
+                        f"intermediate {I}, sigmoid+bias top-{K}, scale {SCALE}, MXFP4, {T} tokens",
+            "tokens": T,
+            "parallelism": "single",
+            "path": f"{router_kind}; flashinfer.fused_moe.trtllm_fp4_block_scale_moe (routing_method DeepSeekV3, "
+                    f"n_group 1, do_finalize); shared expert via trtllm_fp4_block_scale_routed_moe; add",
+            "flashinfer": __import__("flashinfer").__version__,
+            "distinct_experts_per_step": d_mean,
+            "layer_weight_bytes": layer_bytes,
+            "layer_roofline_frac": (layer_bytes / (ms_step / 1e3) / 1e9) / peak,
+            "peak": peak,
+            "peak_kind": peak_kind,
+            "max_abs_rel_vs_mm": {"max": max(errs), "median": float(np.median(errs)), "batches": len(errs)},
+        },
+        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
+                "d2h_bytes_per_step": T * H * 2, "steps": e2e_steps},
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    moe.check()
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.impl == "flashinfer":
+        run_flashinfer(args)
     elif args.stack:
         run_stack(args)
     else:

@@ -348,7 +348,7 @@ int mm_layer_create(const mm_layer_desc *desc, mm_layer **out) {
     }                                                                                    \
   } while (0)
 
-  const size_t E = L->E, H = L->H, I = L->I;
+  const size_t E = L->E, H = L->H;
   const size_t sfs = static_cast<size_t>(L->sf_stage);
   const size_t sfa13_bytes = E * L->m1 * L->ks1 * sfs;
   const size_t sfa2_bytes = E * L->m2 * L->ks2 * sfs;

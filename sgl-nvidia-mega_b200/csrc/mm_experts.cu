@@ -385,8 +385,9 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
     const int quarter = lane >> 3;
     constexpr int kPieces = kBRows / 4;  // rows per lane
     constexpr int kC = L::kChunks;
-    uint32_t soff[kPieces], doff[kPieces], sbytes[kPieces];
-    uint32_t s_soff[2 * kC], s_doff[2 * kC], s_bytes[2 * kC];
+    uint32_t soff[kPieces], doff[kPieces];
+    uint32_t s_base[2];  // scale bytes of B rows lane and lane + 32 at stage 0 (chunk c: + 4 c)
+    uint32_t pmask = 0, smask = 0;  // bit i: piece i / scale row half i holds a segment row (else zero-fill)
     int nb = 0;
     const uint8_t *dq = nullptr, *dsc = nullptr;
 #pragma unroll 1
@@ -443,7 +444,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
           const int sr = __shfl_sync(0xffffffffu, src, r & 31);
           soff[i] = static_cast<uint32_t>(t) * term_q + static_cast<uint32_t>(sr) * rowb + pc * 16;
           doff[i] = (rr >> 3) * 1024 + (rr & 7) * 128 + ((pc ^ (rr & 7)) << 4);
-          sbytes[i] = (rr < nb && r < rows) ? 16u : 0u;
+          pmask = (rr < nb && r < rows) ? (pmask | (1u << i)) : (pmask & ~(1u << i));
         }
         // scale pieces: B rows rr = lane and lane + 32, every chunk of the stage
 #pragma unroll
@@ -452,13 +453,8 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
           const int t = rr / n;
           const int r = rr - t * n;
           const int sr = __shfl_sync(0xffffffffu, src, r & 31);
-#pragma unroll
-          for (int c = 0; c < kC; ++c) {
-            s_soff[kC * h + c] =
-                static_cast<uint32_t>(t) * term_s + static_cast<uint32_t>(sr) * srow + c * 4;
-            s_doff[kC * h + c] = c * 512 + (rr & 31) * 16 + (rr >> 5) * 4;
-            s_bytes[kC * h + c] = (rr < nb && r < rows) ? 4u : 0u;
-          }
+          s_base[h] = static_cast<uint32_t>(t) * term_s + static_cast<uint32_t>(sr) * srow;
+          smask = (rr < nb && r < rows) ? (smask | (1u << h)) : (smask & ~(1u << h));
         }
       }
       const int ks_n = g2 ? p.ks2 : p.ks1;
@@ -472,7 +468,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
         const uint8_t *gq = dq + ks * kRowBytes;
 #pragma unroll
         for (int i = 0; i < kPieces; ++i) {
-          if (quarter + 4 * i < nb) cp_async_16(sb + doff[i], gq + soff[i], sbytes[i]);
+          if (quarter + 4 * i < nb) cp_async_16(sb + doff[i], gq + soff[i], ((pmask >> i) & 1u) * 16u);
         }
         const uint32_t ssb = base + L::kSmemSfb + stage * L::kSfStageBytes;
         const uint8_t *gs = dsc + ks * L::kSfRow;
@@ -480,7 +476,8 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
         for (int h = 0; h < 2; ++h) {
           if (lane + 32 * h < nb) {
 #pragma unroll
-            for (int c = 0; c < kC; ++c) cp_async_4(ssb + s_doff[kC * h + c], gs + s_soff[kC * h + c], s_bytes[kC * h + c]);
+            for (int c = 0; c < kC; ++c)  // chunk c, row lane + 32 h: byte 16 (row % 32) + 4 (row / 32)
+              cp_async_4(ssb + c * 512 + lane * 16 + h * 4, gs + s_base[h] + c * 4, ((smask >> h) & 1u) * 4u);
           }
         }
         cp_async_arrive_noinc(bar(kBarFull + stage));
