@@ -136,6 +136,20 @@ class FlashInferLayer:
                         do_finalize=True)
         return out + sh
 
+    def forward_routed(self, x, ids, weights):
+        """One step with given routing (ids int32 [T, k], weights fp32 [T, k], the
+        routed scale already in the weights): FlashInfer's routed MoE over the packed
+        (id, bf16 weight) words, finalized, plus the shared expert."""
+        out = self._call(self.routed, (pack_topk(ids, weights), None, x, None), self.w, self.E, self.k,
+                         n_group=None, topk_group=None, routed_scaling_factor=None, routing_method_type=5,
+                         do_finalize=True)
+        if self.sw is None:
+            return out
+        sh = self._call(self.routed, (self.shared_ids[: x.shape[0]], None, x, None), self.sw, 4, 1, local=1,
+                        n_group=None, topk_group=None, routed_scaling_factor=None, routing_method_type=5,
+                        do_finalize=True)
+        return out + sh
+
 
 def mxfp8_quantize(x):
     """MXFP8 codes (float8_e4m3fn [T, H]) and linear E8M0 scales ([T, H/32] viewed as

@@ -97,7 +97,7 @@ int set_error(int code, const char *fmt, ...) {
 struct mm_layer {
   mm_layer_desc d;
   int H, I, E, R, offset, K, Tmax, terms;
-  int m1, m2, ks1, ks2;
+  int m1, m2, ks1, ks2, tg2, u2;
   int max_ctas, rows_cap, shared_row_base, route_words_max, max_segs;
   int has_shared;
   int num_sms;
@@ -326,6 +326,13 @@ int mm_layer_create(const mm_layer_desc *desc, mm_layer **out) {
   L->m2 = L->H / 128;
   L->ks1 = L->H / kStageK;
   L->ks2 = (L->I + kStageK - 1) / kStageK;  // the down GEMM's last stage may be partial
+  // short down units (one or two K stages: narrow tensor-parallel slices) take two
+  // 128-row tiles each, so one accumulator hand-off serves two tiles; MXFP4 only
+  // (NVFP4's scale columns leave TMEM room for one tile per accumulator)
+  L->tg2 = (!nv && L->ks2 <= 2) ? 2 : 1;
+  static_assert(Fmt<kFmtMx>::kAccCols == 2 * kBRows && Fmt<kFmtNv>::kAccCols == kBRows,
+                "two-tile down units need MXFP4's double-width accumulator buffers");
+  L->u2 = (L->m2 + L->tg2 - 1) / L->tg2;
   L->max_ctas = route_max_ctas(L->Tmax, L->K, L->E);
   L->shared_row_base = kTile * L->max_ctas;
   L->rows_cap = L->shared_row_base + L->Tmax;
@@ -473,6 +480,8 @@ int mm_layer_create(const mm_layer_desc *desc, mm_layer **out) {
   ea.m2 = L->m2;
   ea.ks1 = L->ks1;
   ea.ks2 = L->ks2;
+  ea.tg2 = L->tg2;
+  ea.u2 = L->u2;
 
   ce = expert_kernel_configure(L->fmt);
   if (ce == cudaSuccess)
@@ -573,7 +582,7 @@ static int run_front_and_experts(mm_layer *L, const uint16_t *x, const mm_gate_a
   f.route.has_shared = L->has_shared;
   f.route.shared_row_base = L->shared_row_base;
   f.route.m1 = L->m1;
-  f.route.m2 = L->m2;
+  f.route.m2 = L->u2;
   MM_CUDA(cudaSetDevice(L->d.device));
   if (!quant_done) {
     int rc = launch_router_quant(L, x, nullptr, nullptr, tokens, stream);

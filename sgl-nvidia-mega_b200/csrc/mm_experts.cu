@@ -44,6 +44,8 @@ namespace {
 
 constexpr uint32_t kATxBytes = kAStageBytes;  // packed codes land as they are
 
+// Unit u: gate_up units [0, nseg m1) (segment, 128-row gate_up tile m), then
+// down units (segment, down unit m covering w2 tiles [m tg2, m tg2 + tg2)).
 __device__ __forceinline__ void decode_unit(int u, int nseg, int m1, int m2, bool &g2, int &seg,
                                             int &m) {
   const int n1 = nseg * m1;
@@ -153,9 +155,12 @@ __device__ __forceinline__ void mma_nvf4(uint32_t d_tmem, uint64_t adesc, uint64
 
 }  // namespace
 
-template <int F>
+// kTg2: down tiles per down unit (p.tg2; 2 only for MXFP4 layers with one or two K
+// stages per down tile), a template argument so single-tile layers run the plain loop.
+template <int F, int kTg2>
 __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(const __grid_constant__ ExpertArgs p) {
   using L = Fmt<F>;
+  static_assert(kTg2 == 1 || (kTg2 == 2 && L::kAccCols >= 2 * kBRows), "two-tile units need double-width accumulators");
   constexpr bool kNv = F == kFmtNv;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -232,6 +237,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
       int b_next = total, b_end = total;  // the next batch, once claimed
       bool b_claimed = false;
       bool ok = true;
+      int filled = 0;  // stages filled (the drain waits for the last ring's copies to land)
 #pragma unroll 1
       while (ok) {
         const int u = cur;
@@ -244,16 +250,21 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
         if (!have) break;
         bool g2;
         int seg, m;
-        decode_unit(u, nseg, p.m1, p.m2, g2, seg, m);
+        decode_unit(u, nseg, p.m1, p.u2, g2, seg, m);
         const int4 sg = seg_cache.get(p.segs, seg);
         const int e = sg.x < 0 ? 0 : sg.x;
         const bool sh = sg.x < 0;
         const CUtensorMap *map = g2 ? (sh ? &p.sw2_map : &p.w2_map) : (sh ? &p.sw13_map : &p.w13_map);
-        const int ks_n = g2 ? p.ks2 : p.ks1;
+        // a down unit's stages run over its tiles, K stages within a tile; the
+        // tiles' scale chunks are consecutive ([expert][tile][K stage])
+        const int ks_u = g2 ? p.ks2 : p.ks1;
+        const int t0 = g2 ? m * kTg2 : m;
+        const int ks_n = (g2 ? (kTg2 == 1 ? 1 : min(kTg2, p.m2 - t0)) : 1) * ks_u;
         const uint8_t *sfa = g2 ? (sh ? p.ssfa2 : p.sfa2) : (sh ? p.ssfa13 : p.sfa13);
-        sfa += (static_cast<size_t>(e) * (g2 ? p.m2 : p.m1) + m) * static_cast<size_t>(ks_n) * L::kSfStageBytes;
+        sfa += (static_cast<size_t>(e) * (g2 ? p.m2 : p.m1) + t0) * static_cast<size_t>(ks_u) * L::kSfStageBytes;
         const int claim_at = ks_n > 3 ? ks_n - 3 : 0;
         const bool refill = !b_claimed && a_end - a_next <= 1;
+        int tt = 0, kq = 0;  // tile of the unit (down units) and K stage within it
 #pragma unroll 1
         for (int ks = 0; ks < ks_n; ++ks) {
           if (refill && ks == claim_at) {
@@ -269,15 +280,17 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
           const uint32_t full = bar(kBarFull + stage);
           mbar_expect_tx(full, kATxBytes + L::kSfStageBytes);
           const uint32_t sa = base + L::kSmemA + stage * kAStageBytes;
-          const int x = ks * kRowBytes;  // byte offset along K
+          const int x = kq * kRowBytes;  // byte offset along K
           if (!g2) {
             tma_load_3d(sa, map, x, 64 * m, e, full, policy);
             tma_load_3d(sa + 64 * kRowBytes, map, x, p.inter + 64 * m, e, full, policy);
           } else {
-            tma_load_3d(sa, map, x, 128 * m, e, full, policy);
+            tma_load_3d(sa, map, x, 128 * (t0 + tt), e, full, policy);
           }
           bulk_load(base + L::kSmemSfa + stage * L::kSfStageBytes,
                     sfa + static_cast<size_t>(ks) * L::kSfStageBytes, L::kSfStageBytes, full, policy);
+          ++filled;
+          if (++kq == ks_u) { kq = 0; ++tt; }
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
         }
         if (a_next >= a_end && b_claimed) {
@@ -287,10 +300,16 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
         }
         if (a_next < a_end) cur = a_next++;
       }
-      // drain: every stage filled so far has been consumed, so no copy is in flight
-      for (int i = 0; i < kStages; ++i) {
-        mbar_wait(bar(kBarEmpty + stage), phase ^ 1u, err, kErrTimeoutEmpty);
-        if (++stage == kStages) { stage = 0; phase ^= 1u; }
+      // drain: the copies of the last ring's fills have landed (their full
+      // barriers completed), so no copy is in flight when the CTA exits
+      for (int i = 0; i < kStages && i < filled; ++i) {
+        if (stage == 0) {
+          stage = kStages - 1;
+          phase ^= 1u;
+        } else {
+          --stage;
+        }
+        mbar_wait(bar(kBarFull + stage), phase, err, kErrTimeoutFull);
       }
     }
   } else if (warp == 1) {
@@ -314,17 +333,21 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
         if (u < 0) break;
         bool g2;
         int seg, m;
-        decode_unit(u, nseg, p.m1, p.m2, g2, seg, m);
+        decode_unit(u, nseg, p.m1, p.u2, g2, seg, m);
         const int4 sg = seg_cache.get(p.segs, seg);
         const uint32_t n = static_cast<uint32_t>((sg.z + 7) & ~7);
         const uint32_t nmma = n * static_cast<uint32_t>(p.terms);  // term 0 rows, term 1 rows, ...
         const uint32_t id0 = idesc_base | ((nmma >> 3) << 17);
         const uint32_t id2 = id0 | (2u << 4) | (2u << 29);  // MXFP4: the chunk's second byte pair
-        const int ks_n = g2 ? p.ks2 : p.ks1;
+        const int ks_u = g2 ? p.ks2 : p.ks1;
+        const int ks_n = (g2 ? (kTg2 == 1 ? 1 : min(kTg2, p.m2 - m * kTg2)) : 1) * ks_u;
         if (!mbar_wait(bar(kBarAccEmpty + acc), acc_phase ^ 1u, err, kErrTimeoutAcc)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tbase + L::kTmemAcc + acc * kBRows;
+        // accumulator buffers tg2 x kBRows columns apart (single-tile layers keep them adjacent)
+        const uint32_t acc_tmem = tbase + L::kTmemAcc + acc * static_cast<uint32_t>(kTg2 * kBRows);
         bool ok = true;
+        uint32_t d_tmem = acc_tmem;  // the unit's current tile: its accumulator kBRows columns further
+        int kq = 0;                  // K stage within the tile
 #pragma unroll 1
         for (int ks = 0; ks < ks_n; ++ks) {
           if (!mbar_wait(bar(kBarFull + stage), phase, err, kErrTimeoutFull)) {
@@ -350,12 +373,13 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             if constexpr (kNv)
-              mma_nvf4(d_tmem, a_d + 2 * k, b_d + 2 * k, id0, sfa_t + 4 * k, sfb_t + 4 * k, (ks | k) != 0 ? 1u : 0u);
+              mma_nvf4(d_tmem, a_d + 2 * k, b_d + 2 * k, id0, sfa_t + 4 * k, sfb_t + 4 * k, (kq | k) != 0 ? 1u : 0u);
             else
               mma_mxf4(d_tmem, a_d + 2 * k, b_d + 2 * k, (k & 1) ? id2 : id0, sfa_t + 4 * (k >> 1),
-                       sfb_t + 4 * (k >> 1), (ks | k) != 0 ? 1u : 0u);
+                       sfb_t + 4 * (k >> 1), (kq | k) != 0 ? 1u : 0u);
           }
           tc_commit(bar(kBarEmpty + stage));
+          if (++kq == ks_u) { kq = 0; d_tmem += kBRows; }
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
@@ -406,7 +430,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
       if (!okw || u < 0) break;
       bool g2;
       int seg, m;
-      decode_unit(u, nseg, p.m1, p.m2, g2, seg, m);
+      decode_unit(u, nseg, p.m1, p.u2, g2, seg, m);
       if (g2 && seg != ready_seg) {  // once complete, a mailbox stays complete in this launch
         int okf = 1;
         if (lane == 0) okf = wait_flag(p.flags + seg, 2 * p.m1, err) ? 1 : 0;
@@ -457,21 +481,23 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
           smask = (rr < nb && r < rows) ? (smask | (1u << h)) : (smask & ~(1u << h));
         }
       }
-      const int ks_n = g2 ? p.ks2 : p.ks1;
+      // a down unit's tiles share their B: stage ks loads K stage ks % ks_u
+      const int ks_u = g2 ? p.ks2 : p.ks1;
+      const int ks_n = (g2 ? (kTg2 == 1 ? 1 : min(kTg2, p.m2 - m * kTg2)) : 1) * ks_u;
 #pragma unroll 1
-      for (int ks = 0; ks < ks_n; ++ks) {
+      for (int ks = 0, kq = 0; ks < ks_n; ++ks, kq = (kq + 1 == ks_u) ? 0 : kq + 1) {
         int oke = 1;
         if (lane == 0) oke = mbar_wait(bar(kBarEmpty + stage), phase ^ 1u, err, kErrTimeoutEmpty) ? 1 : 0;
         oke = __shfl_sync(0xffffffffu, oke, 0);
         if (!oke) break;
         const uint32_t sb = base + L::kSmemB + stage * kBStageBytes;
-        const uint8_t *gq = dq + ks * kRowBytes;
+        const uint8_t *gq = dq + kq * kRowBytes;
 #pragma unroll
         for (int i = 0; i < kPieces; ++i) {
           if (quarter + 4 * i < nb) cp_async_16(sb + doff[i], gq + soff[i], ((pmask >> i) & 1u) * 16u);
         }
         const uint32_t ssb = base + L::kSmemSfb + stage * L::kSfStageBytes;
-        const uint8_t *gs = dsc + ks * L::kSfRow;
+        const uint8_t *gs = dsc + kq * L::kSfRow;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           if (lane + 32 * h < nb) {
@@ -513,7 +539,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
       if (!okw || u < 0) break;
       bool g2;
       int seg, m;
-      decode_unit(u, nseg, p.m1, p.m2, g2, seg, m);
+      decode_unit(u, nseg, p.m1, p.u2, g2, seg, m);
       const int4 sg = seg_cache.get(p.segs, seg);
       const int rows = sg.z;
       const int n = (rows + 7) & ~7;
@@ -522,105 +548,115 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       tc_fence_after();
-      uint32_t ra[32], rb[16];
-      const uint32_t taddr = tbase + (static_cast<uint32_t>(32 * q) << 16) + L::kTmemAcc + acc * kBRows;
-      tc_ld_32x32b_x32(taddr, ra);
-      tc_ld_32x32b_x16(taddr + 32, rb);
-      tc_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(kBarAccEmpty + acc));
-      if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
-      // columns [t n, (t+1) n) hold term t's products; row j's value = sum of terms
-      float v[kSegRows];
-#pragma unroll
-      for (int j = 0; j < kSegRows; ++j) {
-        float a = __uint_as_float(ra[j]);
-        if (p.terms > 1) a = __fadd_rn(a, __uint_as_float(n == 8 ? ra[8 + j] : ra[16 + j]));
-        if (p.terms > 2) a = __fadd_rn(a, __uint_as_float(n == 8 ? ra[16 + j] : rb[j]));
-        v[j] = a;
-      }
-      if constexpr (kNv) {  // the product of the two second-level scales
-        const float al = sg.x < 0 ? (g2 ? p.salpha2[0] : p.salpha13[0]) : (g2 ? p.alpha2[sg.x] : p.alpha13[sg.x]);
-#pragma unroll
-        for (int j = 0; j < kSegRows; ++j) v[j] = __fmul_rn(v[j], al);
-      }
-      if (!g2) {
-        // rows 0..63: gate of features 64m + row; rows 64..127: up of the same features
-        if (q >= 2) {
-          if (lane == 0) ok = mbar_wait(bar(kBarExFree), ex_phase ^ 1u, err, kErrTimeoutAcc) ? 1 : 0;
-          ok = __shfl_sync(0xffffffffu, ok, 0);
-          if (!ok) break;
-#pragma unroll
-          for (int j = 0; j < kSegRows; ++j) ex[(row - 64) * kSegRows + j] = v[j];
+      // a down unit holds tg2 tiles: tile tt's accumulator at tt x kBRows columns
+      const int tiles = g2 ? (kTg2 == 1 ? 1 : min(kTg2, p.m2 - m * kTg2)) : 1;
+      const uint32_t acc_addr =
+          tbase + (static_cast<uint32_t>(32 * q) << 16) + L::kTmemAcc + acc * static_cast<uint32_t>(kTg2 * kBRows);
+#pragma unroll 1
+      for (int tt = 0; tt < tiles; ++tt) {
+        uint32_t ra[32], rb[16];
+        const uint32_t taddr = acc_addr + static_cast<uint32_t>(tt * kBRows);
+        tc_ld_32x32b_x32(taddr, ra);
+        tc_ld_32x32b_x16(taddr + 32, rb);
+        tc_wait_ld();
+        if (tt == tiles - 1) {  // every tile read: the accumulator buffer is free
+          tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(bar(kBarExFull));
+          if (lane == 0) mbar_arrive(bar(kBarAccEmpty + acc));
+          if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+        }
+        // columns [t n, (t+1) n) hold term t's products; row j's value = sum of terms
+        float v[kSegRows];
+#pragma unroll
+        for (int j = 0; j < kSegRows; ++j) {
+          float a = __uint_as_float(ra[j]);
+          if (p.terms > 1) a = __fadd_rn(a, __uint_as_float(n == 8 ? ra[8 + j] : ra[16 + j]));
+          if (p.terms > 2) a = __fadd_rn(a, __uint_as_float(n == 8 ? ra[16 + j] : rb[j]));
+          v[j] = a;
+        }
+        if constexpr (kNv) {  // the product of the two second-level scales
+          const float al = sg.x < 0 ? (g2 ? p.salpha2[0] : p.salpha13[0]) : (g2 ? p.alpha2[sg.x] : p.alpha13[sg.x]);
+#pragma unroll
+          for (int j = 0; j < kSegRows; ++j) v[j] = __fmul_rn(v[j], al);
+        }
+        if (!g2) {
+          // rows 0..63: gate of features 64m + row; rows 64..127: up of the same features
+          if (q >= 2) {
+            if (lane == 0) ok = mbar_wait(bar(kBarExFree), ex_phase ^ 1u, err, kErrTimeoutAcc) ? 1 : 0;
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+#pragma unroll
+            for (int j = 0; j < kSegRows; ++j) ex[(row - 64) * kSegRows + j] = v[j];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(kBarExFull));
+          } else {
+            if (lane == 0) ok = mbar_wait(bar(kBarExFull), ex_phase, err, kErrTimeoutAcc) ? 1 : 0;
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            float upv[kSegRows];
+#pragma unroll
+            for (int j = 0; j < kSegRows; ++j) upv[j] = ex[row * kSegRows + j];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(kBarExFree));
+            const float *lim = sg.x < 0 ? p.shared_clamp : p.clamp;
+            const bool clamped = lim != nullptr;
+            const float L = clamped ? lim[sg.x < 0 ? 0 : sg.x] : 0.0f;
+            const int f = 64 * m + 32 * q + lane;  // feature (column of h)
+            const size_t rowb = static_cast<size_t>(p.hq_row);
+            const size_t tq = static_cast<size_t>(p.rows_cap) * rowb;  // term stride of hq
+            const size_t ts = static_cast<size_t>(p.rows_cap) * p.hs_row;  // term stride of hs
+#pragma unroll
+            for (int j = 0; j < kSegRows; ++j) {
+              if (j >= rows) break;
+              float g = v[j];
+              float up = upv[j];
+              if (clamped) {
+                up = fminf(fmaxf(up, -L), L);
+                g = fminf(g, L);
+              }
+              float r = __fmul_rn(up, __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
+              const size_t prow = static_cast<size_t>(sg.y + j);
+              // FP4 terms of the 32 features of this warp for token row j: one
+              // MXFP4 block of 32, or two NVFP4 blocks of 16 (lane halves)
+              for (int t = 0; t < p.terms; ++t) {
+                uint32_t nib, code;
+                if constexpr (kNv) {
+                  float amax = fabsf(r);
+#pragma unroll
+                  for (int off = 8; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+                  code = nv4_scale_code(amax, p.gs2);
+                  const float sv = e4m3_value(static_cast<uint8_t>(code));
+                  nib = e2m1x2(__fmul_rn(r, nv4_multiplier(sv, p.gs2)), 0.0f) & 15u;
+                  r = __fsub_rn(r, __fmul_rn(__fmul_rn(e2m1_value(nib), sv), p.inv_gs2));
+                } else {
+                  const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(r))));
+                  code = mx4_scale_code(amax);
+                  nib = e2m1x2(__fmul_rn(r, mx_inverse(code)), 0.0f) & 15u;
+                  r = __fsub_rn(r, __fmul_rn(e2m1_value(nib), mx_scale_value(code)));
+                }
+                const uint32_t up_nib = __shfl_down_sync(0xffffffffu, nib, 1);
+                if ((lane & 1) == 0) p.hq[t * tq + prow * rowb + (f >> 1)] = static_cast<uint8_t>(nib | (up_nib << 4));
+                if ((lane & (L::kBlock - 1)) == 0)
+                  p.hs[t * ts + prow * p.hs_row + f / L::kBlock] = static_cast<uint8_t>(code);
+              }
+            }
+            // publish this warp's 32 features of every row: two increments per unit
+            __threadfence();
+            __syncwarp();
+            if (lane == 0) asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(p.flags + seg) : "memory");
+          }
+          ex_phase ^= 1u;
         } else {
-          if (lane == 0) ok = mbar_wait(bar(kBarExFull), ex_phase, err, kErrTimeoutAcc) ? 1 : 0;
-          ok = __shfl_sync(0xffffffffu, ok, 0);
-          if (!ok) break;
-          float upv[kSegRows];
-#pragma unroll
-          for (int j = 0; j < kSegRows; ++j) upv[j] = ex[row * kSegRows + j];
-          __syncwarp();
-          if (lane == 0) mbar_arrive(bar(kBarExFree));
-          const float *lim = sg.x < 0 ? p.shared_clamp : p.clamp;
-          const bool clamped = lim != nullptr;
-          const float L = clamped ? lim[sg.x < 0 ? 0 : sg.x] : 0.0f;
-          const int f = 64 * m + 32 * q + lane;  // feature (column of h)
-          const size_t rowb = static_cast<size_t>(p.hq_row);
-          const size_t tq = static_cast<size_t>(p.rows_cap) * rowb;  // term stride of hq
-          const size_t ts = static_cast<size_t>(p.rows_cap) * p.hs_row;  // term stride of hs
+          // features 128 (m tg2 + tt) + row of the segment's rows, bf16
+          const size_t col = static_cast<size_t>(128 * (m * kTg2 + tt) + row);
 #pragma unroll
           for (int j = 0; j < kSegRows; ++j) {
             if (j >= rows) break;
-            float g = v[j];
-            float up = upv[j];
-            if (clamped) {
-              up = fminf(fmaxf(up, -L), L);
-              g = fminf(g, L);
-            }
-            float r = __fmul_rn(up, __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
-            const size_t prow = static_cast<size_t>(sg.y + j);
-            // FP4 terms of the 32 features of this warp for token row j: one
-            // MXFP4 block of 32, or two NVFP4 blocks of 16 (lane halves)
-            for (int t = 0; t < p.terms; ++t) {
-              uint32_t nib, code;
-              if constexpr (kNv) {
-                float amax = fabsf(r);
-#pragma unroll
-                for (int off = 8; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-                code = nv4_scale_code(amax, p.gs2);
-                const float sv = e4m3_value(static_cast<uint8_t>(code));
-                nib = e2m1x2(__fmul_rn(r, nv4_multiplier(sv, p.gs2)), 0.0f) & 15u;
-                r = __fsub_rn(r, __fmul_rn(__fmul_rn(e2m1_value(nib), sv), p.inv_gs2));
-              } else {
-                const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(r))));
-                code = mx4_scale_code(amax);
-                nib = e2m1x2(__fmul_rn(r, mx_inverse(code)), 0.0f) & 15u;
-                r = __fsub_rn(r, __fmul_rn(e2m1_value(nib), mx_scale_value(code)));
-              }
-              const uint32_t up_nib = __shfl_down_sync(0xffffffffu, nib, 1);
-              if ((lane & 1) == 0) p.hq[t * tq + prow * rowb + (f >> 1)] = static_cast<uint8_t>(nib | (up_nib << 4));
-              if ((lane & (L::kBlock - 1)) == 0)
-                p.hs[t * ts + prow * p.hs_row + f / L::kBlock] = static_cast<uint8_t>(code);
-            }
+            p.rows_out[static_cast<size_t>(sg.y + j) * p.hidden + col] = float_to_bf16_bits(v[j]);
           }
-          // publish this warp's 32 features of every row: two increments per unit
-          __threadfence();
-          __syncwarp();
-          if (lane == 0) asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(p.flags + seg) : "memory");
-        }
-        ex_phase ^= 1u;
-      } else {
-        // features 128m + row of the segment's rows, bf16
-        const size_t col = static_cast<size_t>(128 * m + row);
-#pragma unroll
-        for (int j = 0; j < kSegRows; ++j) {
-          if (j >= rows) break;
-          p.rows_out[static_cast<size_t>(sg.y + j) * p.hidden + col] = float_to_bf16_bits(v[j]);
         }
       }
+      if (!ok) break;
     }
   }
 
@@ -687,16 +723,26 @@ __global__ void nv_alpha_kernel(const float *__restrict__ scale_2, float input_s
 }
 
 cudaError_t expert_kernel_configure(int fmt) {
-  return fmt == kFmtNv ? cudaFuncSetAttribute(expert_kernel<kFmtNv>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              Fmt<kFmtNv>::kSmemAlloc)
-                       : cudaFuncSetAttribute(expert_kernel<kFmtMx>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              Fmt<kFmtMx>::kSmemAlloc);
+  if (fmt == kFmtNv)
+    return cudaFuncSetAttribute(expert_kernel<kFmtNv, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                Fmt<kFmtNv>::kSmemAlloc);
+  cudaError_t e = cudaFuncSetAttribute(expert_kernel<kFmtMx, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       Fmt<kFmtMx>::kSmemAlloc);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(expert_kernel<kFmtMx, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Fmt<kFmtMx>::kSmemAlloc);
+  return e;
 }
 
 cudaError_t expert_kernel_launch(int fmt, int ctas, const ExpertArgs &ea, void *stream) {
   const dim3 grid(ctas), block(kExpertThreads);
-  return fmt == kFmtNv ? launch(expert_kernel<kFmtNv>, grid, block, Fmt<kFmtNv>::kSmemAlloc, stream, ea)
-                       : launch(expert_kernel<kFmtMx>, grid, block, Fmt<kFmtMx>::kSmemAlloc, stream, ea);
+  if (fmt == kFmtNv) {
+    if (ea.tg2 != 1) return cudaErrorInvalidValue;
+    return launch(expert_kernel<kFmtNv, 1>, grid, block, Fmt<kFmtNv>::kSmemAlloc, stream, ea);
+  }
+  if (ea.tg2 == 2) return launch(expert_kernel<kFmtMx, 2>, grid, block, Fmt<kFmtMx>::kSmemAlloc, stream, ea);
+  if (ea.tg2 != 1) return cudaErrorInvalidValue;
+  return launch(expert_kernel<kFmtMx, 1>, grid, block, Fmt<kFmtMx>::kSmemAlloc, stream, ea);
 }
 
 }  // namespace mm

@@ -93,7 +93,8 @@ struct alignas(64) ExpertArgs {
   const float *shared_clamp; // [1] or null
   int hidden, inter, max_tokens, rows_cap, terms, token_off;
   int hq_row, hs_row;        // bytes per h row / h scale row: I rounded up to 256 features, zero past I
-  int m1, m2, ks1, ks2;
+  int m1, m2, ks1, ks2;      // gate_up units / down tiles per segment; K stages of each
+  int tg2, u2;               // down tiles per down unit; down units per segment (ceil(m2 / tg2))
 };
 
 struct FinalizeArgs {

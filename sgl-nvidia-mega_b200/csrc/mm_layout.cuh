@@ -118,11 +118,15 @@ struct Fmt {
   static constexpr int kSmemTmemBase = kSmemWorkIds + 4 * kWorkSlots;
   static constexpr int kSmemTotal = kSmemTmemBase + 16;
   static constexpr int kSmemAlloc = kSmemTotal + 1024;  // room to align the base to 1 KB
-  // TMEM columns: 2 accumulators of kBRows fp32 columns, then per stage the A
-  // scale chunks and the B scale chunks (4 columns per chunk)
+  // TMEM columns: 2 accumulator buffers of kAccCols fp32 columns, then per stage
+  // the A scale chunks and the B scale chunks (4 columns per chunk). An MXFP4
+  // buffer holds two weight tiles' accumulators (2 x kBRows: two-tile down
+  // units, 2 x 96 + 2 x 4 x 8 = 256 columns); NVFP4's larger scale chunks leave
+  // room for one (2 x 48 + 2 x 4 x 16 = 224)
+  static constexpr int kAccCols = F == kFmtNv ? kBRows : 2 * kBRows;
   static constexpr int kTmemAcc = 0;
   static constexpr int kTmemSfCols = 4 * kChunks;
-  static constexpr int kTmemSfa = 2 * kBRows;
+  static constexpr int kTmemSfa = 2 * kAccCols;
   static constexpr int kTmemSfb = kTmemSfa + kStages * kTmemSfCols;
   static constexpr int kTmemEnd = kTmemSfb + kStages * kTmemSfCols;
   static_assert(kSmemAlloc <= 232448, "expert kernel shared memory over the 227 KB limit");
