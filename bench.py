@@ -68,6 +68,9 @@ def parse_args():
     ap.add_argument("--combine", choices=["peer", "nccl"], default="peer",
                     help="N > 1: fused combine + peer all-reduce (default) or NCCL all-reduce of fp32 partials")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--slice", type=int, default=0,
+                    help="one GPU only: run rank 0's share of an N-way sharded layer (TP-N for config 2) with no "
+                         "exchange, to measure and profile narrow slices")
     ap.add_argument("--stack", action="store_true",
                     help="BASELINE config 5: a step of --layers EP8 MoE layers chained through the fused hop")
     ap.add_argument("--layers", type=int, default=60)
@@ -238,7 +241,10 @@ def run_mm(args):
 
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     T = args.tokens if args.tokens is not None else (80 if args.config == "4" else 8)
-    moe, w, shared, router, bias, xs, info = build_layer(rank, world, T, dev, fmt)
+    if args.slice > 1 and world > 1:
+        raise SystemExit("--slice runs on one GPU")
+    shards = args.slice if args.slice > 1 else world  # ranks the layer is sharded over
+    moe, w, shared, router, bias, xs, info = build_layer(rank, shards, T, dev, fmt)
     bufs = {}
     out_buf = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
     peer = world > 1 and args.combine == "peer"
@@ -362,12 +368,14 @@ def run_mm(args):
                            max_experts=None if args.config == "2" else 6)
     fmt_name = "MXFP4" if fmt == "mxfp4" else "NVFP4"
     if args.config == "2":
-        par = f"tp{world}" if world > 1 else "single"
-        split = f" (TP{world}: {I // world} per rank)" if world > 1 else ""
+        par = f"tp{shards}" if shards > 1 else "single"
+        split = f" (TP{shards}: {I // shards} per rank)" if shards > 1 else ""
     else:
-        par = f"tp{info['tp']}xep{info['ep']}" if world > 1 else "single"
+        par = f"tp{info['tp']}xep{info['ep']}" if shards > 1 else "single"
         split = (f" (TP{info['tp']} x EP{info['ep']}: {info['local']} experts x {info['ir']} per rank)"
-                 if world > 1 else "")
+                 if shards > 1 else "")
+    if shards != world:
+        par = f"slice of {par} (rank 0's share on one GPU, no exchange)"
 
     line = {
         "metric": METRIC,
