@@ -28,8 +28,10 @@ namespace mm {
 // order (the CPU oracle replays it): H is cut in parts of 1024; lane l of a
 // part accumulates, for j = 0..3 and i = 0..7, the element
 // h = 1024 p + 8 (l + 32 j) + i with acc = fma(x, w, acc) from acc = 0; the 32
-// lane sums are combined by the butterfly acc += shfl_xor(acc, 16, 8, 4, 2, 1);
-// the part sums in part order, s = ((p0 + p1) + p2) + ... bf16 x bf16 products
+// lane sums are combined pairwise by lane bit 4, then 3, 2, 1, 0 (the pairing
+// of the butterfly acc += shfl_xor(acc, 16, 8, 4, 2, 1), computed here as a
+// reduce-scatter over a warp's 4 experts x 8 tokens); the part sums in part
+// order, s = ((p0 + p1) + p2) + ... bf16 x bf16 products
 // are exact in fp32. The weight rows are static, so the first part's loads
 // are issued before the grid-dependency wait. Dynamic shared memory:
 // router_smem_bytes(H).
@@ -74,35 +76,35 @@ __global__ void __launch_bounds__(256) router_quant_kernel(RouterArgs a) {
     return;
   }
   // GEMV tile: experts [4 blockIdx.x, +4) x tokens [8 blockIdx.y, +8). The 8
-  // token rows of x are staged once in shared memory (cp.async) and read by
-  // all four experts; warp w computes expert slot w % 4 over the parts of
-  // parity w / 4, keeping each part's sum; one thread per (expert, token)
-  // then adds the parts in part order.
+  // token rows of x are staged once in shared memory (cp.async). Warp w takes
+  // the 1024-wide K parts w, w + 8 for all four experts, so each x load feeds
+  // four experts; lane l sums elements 8 (l + 32 j) .. + 8 of the part for every
+  // (expert, token), and a reduce-scatter butterfly over the 32 (expert, token)
+  // sums leaves lane l with the part sum of expert l / 8, token l % 8 (the same
+  // pairing of lanes as an xor all-reduce: 16, 8, 4, 2, 1). One thread per
+  // (expert, token) then adds the parts in part order.
   extern __shared__ __align__(16) unsigned char router_smem[];
   uint16_t *xs = reinterpret_cast<uint16_t *>(router_smem);                  // [8][H] bf16
   float *part_val = reinterpret_cast<float *>(router_smem + 8 * a.hidden * 2);  // [4][kMaxRouterParts][8]
   const int t0 = blockIdx.y * 8;
   const int nt = min(8, a.tokens - t0);
   const int parts = a.hidden >> 10;
-  const int es = warp & 3, pp = warp >> 2;
-  const int e = blockIdx.x * 4 + es;
-  const bool have_e = e < a.experts;
-  // the warp's weight parts are static: their loads go before the
-  // grid-dependency wait, the first kPreParts of them (all of them for
-  // H <= 8192) into registers; any further part is loaded when reached
-  constexpr int kPreParts = 4;
-  constexpr int kWarpParts = (kMaxRouterParts + 1) / 2;
-  uint4 wv[kPreParts][4];
+  const int e0 = blockIdx.x * 4;
+  // the warp's first part's weights (4 experts x 32 elements per lane) are
+  // loaded before the grid-dependency wait; a second part (H > 8192) when reached
+  auto load_w = [&](int part, uint4 (&wv)[4][4]) {
 #pragma unroll
-  for (int k = 0; k < kPreParts; ++k) {
-    const int part = pp + 2 * k;
+    for (int es = 0; es < 4; ++es)
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
-      wv[k][j] = have_e && part < parts
-                     ? __ldg(reinterpret_cast<const uint4 *>(a.w + static_cast<size_t>(e) * a.hidden + 1024 * part) +
-                             lane + 32 * j)
-                     : make_uint4(0u, 0u, 0u, 0u);
-  }
+      for (int j = 0; j < 4; ++j)
+        wv[es][j] = e0 + es < a.experts && part < parts
+                        ? __ldg(reinterpret_cast<const uint4 *>(a.w + static_cast<size_t>(e0 + es) * a.hidden +
+                                                                1024 * part) +
+                                lane + 32 * j)
+                        : make_uint4(0u, 0u, 0u, 0u);
+  };
+  uint4 wv[4][4];
+  load_w(warp, wv);
   pdl_wait();
   {
     const int per_row = a.hidden >> 3;  // uint4 per token row
@@ -115,52 +117,49 @@ __global__ void __launch_bounds__(256) router_quant_kernel(RouterArgs a) {
     asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
   }
-  if (have_e) {
+#pragma unroll 1
+  for (int part = warp; part < parts; part += 8) {
+    if (part != warp) load_w(part, wv);
+    // per lane: 4 experts x 8 tokens chains, each in the element order above;
+    // rows t >= nt are stale smem and never stored
+    const uint4 *xr = reinterpret_cast<const uint4 *>(xs + 1024 * part);
+    const int row_u4 = a.hidden >> 3;
+    float v[32];  // v[8 es + t]
 #pragma unroll
-    for (int k = 0; k < kWarpParts; ++k) {
-      const int part = pp + 2 * k;
-      if (part >= parts) break;
-      uint4 wlate[4];
-      if (k >= kPreParts) {
+    for (int i = 0; i < 32; ++i) v[i] = 0.0f;
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-          wlate[j] = __ldg(reinterpret_cast<const uint4 *>(a.w + static_cast<size_t>(e) * a.hidden + 1024 * part) +
-                           lane + 32 * j);
-      }
-      const uint4 *wcur = k < kPreParts ? wv[k] : wlate;
-      // the 8 tokens' chains interleaved (independent accumulators; each token's
-      // own accumulation order is the one above); rows t >= nt are stale smem
-      // and never stored
-      const uint4 *xr = reinterpret_cast<const uint4 *>(xs + 1024 * part);
-      const int row_u4 = a.hidden >> 3;
-      float sacc[8];
+    for (int j = 0; j < 4; ++j) {
 #pragma unroll
-      for (int t = 0; t < 8; ++t) sacc[t] = 0.0f;
+      for (int t = 0; t < 8; ++t) {
+        const uint4 xv = xr[t * row_u4 + lane + 32 * j];
+        const uint32_t xq[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint32_t wq[4] = {wcur[j].x, wcur[j].y, wcur[j].z, wcur[j].w};
-#pragma unroll
-        for (int t = 0; t < 8; ++t) {
-          const uint4 xv = xr[t * row_u4 + lane + 32 * j];
-          const uint32_t xq[4] = {xv.x, xv.y, xv.z, xv.w};
+        for (int es = 0; es < 4; ++es) {
+          const uint32_t wq[4] = {wv[es][j].x, wv[es][j].y, wv[es][j].z, wv[es][j].w};
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            sacc[t] = __fmaf_rn(__uint_as_float(xq[q] << 16), __uint_as_float(wq[q] << 16), sacc[t]);
-            sacc[t] = __fmaf_rn(__uint_as_float(xq[q] & 0xffff0000u), __uint_as_float(wq[q] & 0xffff0000u), sacc[t]);
+            v[8 * es + t] = __fmaf_rn(__uint_as_float(xq[q] << 16), __uint_as_float(wq[q] << 16), v[8 * es + t]);
+            v[8 * es + t] =
+                __fmaf_rn(__uint_as_float(xq[q] & 0xffff0000u), __uint_as_float(wq[q] & 0xffff0000u), v[8 * es + t]);
           }
         }
       }
+    }
+    // reduce-scatter: at offset o a lane keeps the half of its current window
+    // selected by its lane bit o and adds its partner's copy of that half
 #pragma unroll
-      for (int off = 16; off >= 1; off >>= 1)
+    for (int lvl = 0; lvl < 5; ++lvl) {
+      const int off = 16 >> lvl;
+      const bool upper = (lane & off) != 0;
 #pragma unroll
-        for (int t = 0; t < 8; ++t) sacc[t] = __fadd_rn(sacc[t], __shfl_xor_sync(0xffffffffu, sacc[t], off));
-      if (lane < nt) {
-        float v = sacc[0];
-#pragma unroll
-        for (int t = 1; t < 8; ++t) v = lane == t ? sacc[t] : v;
-        part_val[(es * kMaxRouterParts + part) * 8 + lane] = v;
+      for (int i = 0; i < off; ++i) {
+        const float send = upper ? v[i] : v[i + off];
+        const float keep = upper ? v[i + off] : v[i];
+        v[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, off));
       }
     }
+    const int es = lane >> 3, t = lane & 7;
+    if (t < nt && e0 + es < a.experts) part_val[(es * kMaxRouterParts + part) * 8 + t] = v[0];
   }
   __syncthreads();
   if (static_cast<int>(threadIdx.x) < 4 * nt) {
