@@ -544,3 +544,60 @@ def test_stack_matches_layer_loop_oracle_and_graph():
     stack.check()
     del graph
     comm.close()
+
+
+@pytest.mark.parametrize("score", ["sigmoid", "softmax", "sqrtsoftplus"])
+@pytest.mark.parametrize("kind", ["normal", "ties", "nan_rows", "tie_cutoff"])
+@pytest.mark.parametrize("E,K", [(16, 2), (384, 8), (512, 10)])
+def test_front_rank_and_route_bitexact(score, kind, E, K):
+    """The layer's front launch (one CTA per row ranks it; the last builds the
+    record) against the oracle: ids and weights bit for bit, the slot -> row
+    map equal, padded rows included."""
+    mm = _mm()
+    H, I = 1024, 256
+    layer = O.make_layer(H, I, E, shared=False, seed=81)
+    moe = to_gpu_layer(layer, K, 64)
+    g = torch.Generator().manual_seed(4321)
+    for T in (1, 5, 8, 9, 16, 32):
+        for trial in range(2):
+            logits = _logits(kind, T, E, g).float().contiguous()
+            bias = None if trial == 0 and kind != "ties" else (torch.randn(E, generator=g) * 0.05).float()
+            valid = T if trial == 0 else max(1, T - 2)
+            nv = torch.tensor([valid], dtype=torch.int32, device="cuda")
+            x = torch.randn((T, H), generator=g).to(torch.bfloat16)
+            _, w, perm, ids = moe.gate_topk_and_gemms(x.cuda(), logits.cuda(),
+                                                     None if bias is None else bias.cuda(), 2.5, nv, score=score)
+            torch.cuda.synchronize()
+            ow, oids = O.gate_topk(logits.numpy(), None if bias is None else bias.numpy(), K, score=score,
+                                   scale=2.5, num_valid=valid)
+            assert np.array_equal(ids.cpu().numpy(), oids), (kind, T, trial)
+            assert _same_bits(w.cpu().numpy(), ow), (kind, T, trial)
+            operm, _ = O.route(oids, E)
+            assert np.array_equal(perm.cpu().numpy(), operm), (kind, T, trial)
+    moe.check()
+
+
+@pytest.mark.parametrize("T", [3, 8, 16])
+def test_front_vision_alt_bias_and_ep(T):
+    """The front launch with the vision alt-bias on an EP window: ids and
+    weights equal the oracle's, non-local slots map to -1."""
+    mm = _mm()
+    H, I, E, K = 1024, 256, 384, 8
+    layer = O.make_layer(H, I, E, shared=False, seed=91)
+    moe = to_gpu_layer(layer, K, 64, router_experts=E, expert_offset=192, window=slice(192, 384))
+    g = torch.Generator().manual_seed(92)
+    logits = torch.randn((T, E), generator=g).float()
+    bias = (torch.randn(E, generator=g) * 0.05).float()
+    bias_alt = (torch.randn(E, generator=g) * 0.5).float()
+    input_ids = torch.randint(0, 3, (T,), generator=g, dtype=torch.int32)
+    x = torch.randn((T, H), generator=g).to(torch.bfloat16)
+    _, w, perm, ids = moe.gate_topk_and_gemms(x.cuda(), logits.cuda(), bias.cuda(), 2.5,
+                                             alt=(bias_alt.cuda(), input_ids.cuda(), 1))
+    torch.cuda.synchronize()
+    ow, oids = O.gate_topk(logits.numpy(), bias.numpy(), K, scale=2.5, bias_alt=bias_alt.numpy(),
+                           input_ids=input_ids.numpy(), alt_token_id=1)
+    assert np.array_equal(ids.cpu().numpy(), oids)
+    assert _same_bits(w.cpu().numpy(), ow)
+    operm, _ = O.route(oids, 192, 192)
+    assert np.array_equal(perm.cpu().numpy(), operm)
+    moe.check()
