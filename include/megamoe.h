@@ -291,12 +291,18 @@ int mm_layer_gate_experts(mm_layer *layer, const uint16_t *x, const mm_gate_args
                           uint16_t *rows, void *stream);
 
 /* Launches the expert kernel again on the work tables of this layer's last
- * front pass (same tokens, routing and input): re-computes the same rows. A
- * benchmark hook that times the dominant kernel alone; no reference
- * counterpart (the reference launches its GEMM pair once per route record,
- * routed_expert_gemm.py:964-999). */
+ * front pass (same tokens, routing and input): re-computes the same rows. The
+ * tables must be re-armed first (mm_layer_rearm_experts) each time: a launch
+ * consumes them. A benchmark hook that times the dominant kernel alone; no
+ * reference counterpart (the reference launches its GEMM pair once per route
+ * record, routed_expert_gemm.py:964-999). */
 int mm_layer_rerun_experts(mm_layer *layer, int32_t tokens, const int32_t *record,
                            uint16_t *rows, void *stream);
+
+/* Re-arms the expert kernel's work tables of the last front pass (zeroes the
+ * segment mailboxes and the claim counter, stream-ordered) so that
+ * mm_layer_rerun_experts can launch on them again. */
+int mm_layer_rearm_experts(mm_layer *layer, void *stream);
 
 /* The whole MoE step: [router GEMV] -> top-k -> route -> experts -> combine. */
 int mm_layer_forward(mm_layer *layer, const mm_forward_args *args, void *stream);

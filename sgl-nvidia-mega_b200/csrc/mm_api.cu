@@ -597,6 +597,15 @@ static int run_front_and_experts(mm_layer *L, const uint16_t *x, const mm_gate_a
   return MM_OK;
 }
 
+int mm_layer_rearm_experts(mm_layer *L, void *stream) {
+  if (!L) return fail(MM_ERR_INVALID, "mm_layer_rearm_experts: null layer");
+  MM_CUDA(cudaSetDevice(L->d.device));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  MM_CUDA(cudaMemsetAsync(L->flags, 0, sizeof(int) * L->max_segs, s));
+  MM_CUDA(cudaMemsetAsync(L->ctrl + kCtrlClaim, 0, sizeof(int), s));
+  return MM_OK;
+}
+
 int mm_layer_rerun_experts(mm_layer *L, int32_t tokens, const int32_t *record, uint16_t *rows, void *stream) {
   if (!L || !record || !rows) return fail(MM_ERR_INVALID, "mm_layer_rerun_experts: null pointer");
   if (tokens < 1 || tokens > L->Tmax) return fail(MM_ERR_INVALID, "tokens %d outside 1..%d", tokens, L->Tmax);

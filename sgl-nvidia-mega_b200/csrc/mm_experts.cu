@@ -667,19 +667,9 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
     tc_fence_after();
     tmem_dealloc(tbase, kTmemCols);
   }
-  // The last CTA to finish re-arms the work tables (claim counter, mailboxes),
-  // so the kernel can be launched again on the same front-kernel output.
-  if (threadIdx.x == 0) {
-    __threadfence();
-    const int done = atomicAdd(&p.ctrl[kCtrlDone], 1);
-    if (done == static_cast<int>(gridDim.x) - 1) {
-      __threadfence();
-      const int nseg = *reinterpret_cast<volatile int *>(&p.ctrl[kCtrlSegments]);
-      for (int s = 0; s < nseg; ++s) p.flags[s] = 0;
-      p.ctrl[kCtrlClaim] = 0;
-      p.ctrl[kCtrlDone] = 0;
-    }
-  }
+  // The work tables (claim counter, mailboxes) are re-armed by the next front
+  // pass (build_route), or by mm_layer_rearm_experts before a relaunch on the
+  // same tables: no end-of-kernel fence and ticket.
 }
 
 // ============================================================================

@@ -156,6 +156,7 @@ SIGNATURES = {
         [c_void_p, c_void_p, POINTER(MMGateArgs), c_int32, c_void_p, c_void_p, c_void_p, c_void_p],
     ),
     "mm_layer_rerun_experts": (c_int32, [c_void_p, c_int32, c_void_p, c_void_p, c_void_p]),
+    "mm_layer_rearm_experts": (c_int32, [c_void_p, c_void_p]),
     "mm_layer_forward": (c_int32, [c_void_p, POINTER(MMForwardArgs), c_void_p]),
     "mm_layer_check": (c_int32, [c_void_p]),
     "mm_stack_forward": (c_int32, [POINTER(MMStackLayer), c_int32, c_void_p]),

@@ -382,9 +382,16 @@ class RoutedMoE:
             return out, res_out
         return part if partial else out
 
-    def rerun_experts(self, tokens: int, record: torch.Tensor, rows: torch.Tensor) -> None:
+    def rearm_experts(self) -> None:
+        """Re-arm the last front pass's work tables for another rerun_experts."""
+        check(lib().mm_layer_rearm_experts(self._handle, _stream(self.device)), "mm_layer_rearm_experts")
+
+    def rerun_experts(self, tokens: int, record: torch.Tensor, rows: torch.Tensor, rearm: bool = True) -> None:
         """Launch the expert kernel again on the last front pass's work tables
-        (benchmark hook: times the dominant kernel alone)."""
+        (benchmark hook: times the dominant kernel alone). ``rearm=False``
+        when rearm_experts was called since the last launch."""
+        if rearm:
+            self.rearm_experts()
         check(lib().mm_layer_rerun_experts(self._handle, tokens, record.data_ptr(), rows.data_ptr(),
                                             _stream(self.device)), "mm_layer_rerun_experts")
 

@@ -601,3 +601,25 @@ def test_front_vision_alt_bias_and_ep(T):
     operm, _ = O.route(oids, 192, 192)
     assert np.array_equal(perm.cpu().numpy(), operm)
     moe.check()
+
+
+def test_rerun_experts_after_rearm_reproduces_rows():
+    """The benchmark hook: re-arming the work tables and relaunching the expert
+    kernel on the last front pass recomputes the same rows, bit for bit, as
+    often as it is repeated."""
+    H, I, E, K, T = 2048, 512, 64, 8, 8
+    layer = O.make_layer(H, I, E, shared=True, seed=101)
+    x, wr, bias = O.make_inputs(T, H, E, seed=102)
+    moe = to_gpu_layer(layer, K, 16)
+    bufs = {}
+    moe.forward(x.cuda(), router_weight=wr.cuda(), bias=bias.cuda(), routed_scaling_factor=2.5, buffers=bufs)
+    torch.cuda.synchronize()
+    want = bufs["rows"].clone()
+    for _ in range(3):
+        bufs["rows"].zero_()
+        moe.rerun_experts(T, bufs["record"], bufs["rows"])
+        torch.cuda.synchronize()
+        moe.check()
+        perm = bufs["permuted"].cpu().numpy()
+        used = sorted({int(p) for p in perm.flatten() if p >= 0})
+        assert torch.equal(bufs["rows"][used], want[used])
