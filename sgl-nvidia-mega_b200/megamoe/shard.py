@@ -1,6 +1,6 @@
 """Partitions of one MoE layer's canonical MXFP4 weights across ranks.
 
-Tensor parallel on the expert intermediate (SURVEY's MoE TP, the reference's
+Tensor parallel on the expert intermediate (the reference's MoE TP,
 ``routed_expert_gemm.py:37-40`` slices): rank r of n holds, of every expert, the
 gate rows [r I/n, (r+1) I/n) and the matching up rows of w13, and the same K
 columns of w2; the partial outputs of the ranks sum to the full output (the
