@@ -52,7 +52,6 @@ constexpr int kCtrlSegments = 0;  // number of segments
 constexpr int kCtrlUnits = 1;     // gate_up units + down units
 constexpr int kCtrlClaim = 2;     // units claimed after the first wave (reset to 0 by the front kernel)
 constexpr int kCtrlTicket = 3;    // front kernel's last-CTA ticket (reset by the last CTA)
-constexpr int kCtrlSpare = 4;     // unused
 constexpr int kCtrlWords = 8;
 
 // ---- the persistent expert kernel's shared memory -----------------------------------
