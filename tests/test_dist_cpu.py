@@ -1,7 +1,7 @@
-"""The multi-GPU partitions on CPU ranks (gloo, world size 2): each rank runs the
-oracle on its tensor-parallel slice (intermediate split) or its expert-parallel
-window, the partial outputs meet in an all-reduce, and the sum equals the
-unpartitioned layer. This checks the partition arithmetic the GPU path uses
+"""The multi-GPU partitions on CPU ranks (gloo, world size 2 or 4): each rank runs
+the oracle on its tensor-parallel slice (intermediate split), its expert-parallel
+window, or both (bench.py's TP x EP2 map for config 4), the partial outputs meet
+in an all-reduce, and the sum equals the unpartitioned layer. This checks the partition arithmetic the GPU path uses
 (megamoe.shard, forward(partial=True) + all_reduce + finalize_partial) with no
 GPU involved."""
 
@@ -42,7 +42,20 @@ def _worker(rank, world, port, mode, queue):
         ids = np.stack([torch.randperm(E, generator=g)[:K].numpy() for _ in range(T)]).astype(np.int32)
         w = torch.rand((T, K), generator=g).numpy()
         full, _, _ = O.moe_layer(x, ids, w, layer)
-        if mode == "tp":
+        if mode == "tpxep":  # bench.partition for 4 ranks: TP2 x EP2 (config 4's 2-D split)
+            import bench
+
+            tp, ep = bench.partition(world, "nvfp4")
+            assert (tp, ep) == (2, 2)
+            ep_rank, tp_rank = rank // tp, rank % tp
+            offset, local = shard.ep_window(E, ep_rank, ep)
+            win = [t[offset:offset + local] for t in (layer["w13"], layer["w13_scale"], layer["w2"], layer["w2_scale"])]
+            part = dict(layer)
+            part["w13"], part["w13_scale"], part["w2"], part["w2_scale"] = shard.tp_slice(*win, tp_rank, tp)
+            # the shared expert lives in EP group 0, TP-split across its ranks
+            part["shared"] = shard.tp_slice(*layer["shared"], tp_rank, tp) if ep_rank == 0 else None
+            out, _, _ = O.moe_layer(x, ids, w, part, expert_offset=offset, local_experts=local)
+        elif mode == "tp":
             part = dict(layer)
             part["w13"], part["w13_scale"], part["w2"], part["w2_scale"] = shard.tp_slice(
                 layer["w13"], layer["w13_scale"], layer["w2"], layer["w2_scale"], rank, world)
@@ -64,15 +77,15 @@ def _worker(rank, world, port, mode, queue):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["tp", "ep"])
-def test_partitions_sum_to_the_full_layer(mode):
+@pytest.mark.parametrize("mode,world", [("tp", 2), ("ep", 2), ("tpxep", 4)])
+def test_partitions_sum_to_the_full_layer(mode, world):
     from oracle import oracle as O
 
     O.build()  # compile the C oracle once, before the ranks import it
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, queue)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, mode, queue)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
