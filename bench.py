@@ -785,6 +785,12 @@ def run_flashinfer(args):
             print(json.dumps({"impl": "flashinfer", "unavailable": "the FlashInfer comparison runs config 2 on one GPU"}),
                   flush=True)
         return
+    if args.tokens is not None and args.tokens < 8:
+        # FlashInfer 0.6.11's autotuner crashed on the host (a segfault in
+        # cuModuleGetFunction) at 1 token on this B200; the case is not run
+        print(json.dumps({"impl": "flashinfer", "unavailable": "FlashInfer's autotuner crashed on the host below 8 "
+                                                               "tokens (segfault in cuModuleGetFunction)"}), flush=True)
+        return
     sys.path.insert(0, os.path.join(REPO, "baseline"))
     import flashinfer_moe  # sets FlashInfer's cache directory before flashinfer is imported
 
