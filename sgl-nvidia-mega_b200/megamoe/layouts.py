@@ -1,5 +1,5 @@
-"""Weight-layout adapters: SGLang's processed FlashInfer / TRT-LLM-gen MXFP4
-layout -> the canonical layout this library reads.
+"""Weight-layout adapters: SGLang's processed FlashInfer / TRT-LLM-gen MXFP4 and
+NVFP4 layouts -> the canonical layout this library reads.
 
 SGLang's ``Mxfp4FlashinferTrtllmMoEMethod`` hands the TRT-LLM-gen MoE (and the
 reference's ``RoutedExpertGemm``, whose test builds the same layout:
@@ -13,6 +13,9 @@ reference's ``RoutedExpertGemm``, whose test builds the same layout:
   * w2 and its scales: ``get_w2_permute_indices_with_cache`` rows, then the
     same swizzle for the scales.
 
+The NVFP4 processing (the TRT-LLM NVFP4 tensors of GLM-5.3's engine,
+``glm5_3/sm103/moe/weights.py:1-30``: the same row maps, E4M3 scales per 16
+elements in the same 128 x 4 interleave) differs only in the scale block.
 ``trtllm_to_canonical`` inverts all of it once, at build time, into the
 canonical [w1; w3] rows with row-major scales; the row permutations come from
 FlashInfer's own index helpers (host code, evaluated on the CPU), the swizzle is
@@ -46,28 +49,41 @@ def deinterleave_scales(flat: torch.Tensor, rows: int, cols: int) -> torch.Tenso
     return t.contiguous().view(Rp, Cp)[:rows, :cols]
 
 
-def _perms(two_i: int, half_h: int, hidden: int, half_i: int):
+def _perms(two_i: int, half_h: int, hidden: int, half_i: int, block: int = 32):
+    """Row permutations of the processed w13 / w13 scales / w2 / w2 scales
+    (FlashInfer's host-side index helpers; the scale matrices have 2 K / block
+    columns: block 32 for MXFP4, 16 for NVFP4)."""
     from flashinfer.fused_moe.core import (  # host-side index helpers
         _maybe_get_cached_w3_w1_permute_indices,
         get_w2_permute_indices_with_cache,
     )
 
     cache: dict = {}
+    per_byte = block // 2  # packed code bytes per scale
     p13 = _maybe_get_cached_w3_w1_permute_indices(cache, torch.empty((two_i, half_h), dtype=torch.uint8), 128)
-    p13s = _maybe_get_cached_w3_w1_permute_indices(cache, torch.empty((two_i, half_h // 16), dtype=torch.uint8),
-                                                   128, num_elts_per_sf=16)
+    p13s = _maybe_get_cached_w3_w1_permute_indices(
+        cache, torch.empty((two_i, half_h // per_byte), dtype=torch.uint8), 128, num_elts_per_sf=16)
     p2 = get_w2_permute_indices_with_cache(cache, torch.empty((hidden, half_i), dtype=torch.uint8), 128)
-    p2s = get_w2_permute_indices_with_cache(cache, torch.empty((hidden, half_i // 16), dtype=torch.uint8), 128,
+    p2s = get_w2_permute_indices_with_cache(cache, torch.empty((hidden, half_i // per_byte), dtype=torch.uint8), 128,
                                             num_elts_per_sf=16)
     return p13.cpu(), p13s.cpu(), p2.cpu(), p2s.cpu()
 
 
+def _block(weight_format: str) -> int:
+    if weight_format not in ("mxfp4", "nvfp4"):
+        raise ValueError(f"weight_format must be 'mxfp4' or 'nvfp4', not {weight_format!r}")
+    return 32 if weight_format == "mxfp4" else 16
+
+
 def trtllm_to_canonical(w13: torch.Tensor, w13_scale: torch.Tensor, w2: torch.Tensor, w2_scale: torch.Tensor,
-                        *, halves: str = "w3_w1") -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
-    """Canonical (w13 u8 [E, 2I, H/2] as [w1; w3], w13_scale u8 [E, 2I, H/32],
-    w2 u8 [E, H, I/2], w2_scale u8 [E, H, I/32]) copies of processed
-    TRT-LLM-gen MXFP4 weights. ``halves``: the order of the processed w13's two
-    halves, "w3_w1" (TRT-LLM's, up first) or "w1_w3"."""
+                        *, halves: str = "w3_w1",
+                        weight_format: str = "mxfp4") -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Canonical (w13 u8 [E, 2I, H/2] as [w1; w3], w13_scale u8 [E, 2I, H/block],
+    w2 u8 [E, H, I/2], w2_scale u8 [E, H, I/block]) copies of processed
+    TRT-LLM-gen weights; block 32 (MXFP4, E8M0 scales) or 16 (NVFP4, E4M3
+    scales). ``halves``: the order of the processed w13's two halves, "w3_w1"
+    (TRT-LLM's, up first) or "w1_w3"."""
+    block = _block(weight_format)
     if halves not in ("w3_w1", "w1_w3"):
         raise ValueError(f"halves must be 'w3_w1' or 'w1_w3', not {halves!r}")
     w13, w2 = (t.view(torch.uint8) for t in (w13, w2))
@@ -76,15 +92,15 @@ def trtllm_to_canonical(w13: torch.Tensor, w13_scale: torch.Tensor, w2: torch.Te
     inter, H = two_i // 2, 2 * half_h
     if tuple(w2.shape) != (E, H, inter // 2):
         raise ValueError(f"w2: expected [{E}, {H}, {inter // 2}], got {tuple(w2.shape)}")
-    p13, p13s, p2, p2s = _perms(two_i, half_h, hidden, half_i)
+    p13, p13s, p2, p2s = _perms(two_i, half_h, hidden, half_i, block)
     dev = w13.device
     inv13, inv13s = torch.argsort(p13).to(dev), torch.argsort(p13s).to(dev)
     inv2, inv2s = torch.argsort(p2).to(dev), torch.argsort(p2s).to(dev)
     c13 = w13[:, inv13].contiguous()
     c2 = w2[:, inv2].contiguous()
     s13f, s2f = w13_scale.reshape(E, -1).view(torch.uint8), w2_scale.reshape(E, -1).view(torch.uint8)
-    c13s = torch.stack([deinterleave_scales(s13f[e], two_i, H // 32)[inv13s] for e in range(E)]).contiguous()
-    c2s = torch.stack([deinterleave_scales(s2f[e], hidden, inter // 32)[inv2s] for e in range(E)]).contiguous()
+    c13s = torch.stack([deinterleave_scales(s13f[e], two_i, H // block)[inv13s] for e in range(E)]).contiguous()
+    c2s = torch.stack([deinterleave_scales(s2f[e], hidden, inter // block)[inv2s] for e in range(E)]).contiguous()
     if halves == "w3_w1":  # canonical is [w1 (gate); w3 (up)]
         c13 = torch.cat([c13[:, inter:], c13[:, :inter]], dim=1).contiguous()
         c13s = torch.cat([c13s[:, inter:], c13s[:, :inter]], dim=1).contiguous()
@@ -92,9 +108,10 @@ def trtllm_to_canonical(w13: torch.Tensor, w13_scale: torch.Tensor, w2: torch.Te
 
 
 def canonical_to_trtllm(w13: torch.Tensor, w13_scale: torch.Tensor, w2: torch.Tensor, w2_scale: torch.Tensor,
-                        *, halves: str = "w3_w1"):
+                        *, halves: str = "w3_w1", weight_format: str = "mxfp4"):
     """The processing ``trtllm_to_canonical`` inverts (for tests and tools):
-    canonical [w1; w3] MXFP4 weights -> processed TRT-LLM-gen layout."""
+    canonical [w1; w3] MXFP4 / NVFP4 weights -> processed TRT-LLM-gen layout."""
+    block = _block(weight_format)
     w13, w2, w13_scale, w2_scale = (t.view(torch.uint8) for t in (w13, w2, w13_scale, w2_scale))
     E, two_i, half_h = w13.shape
     hidden, half_i = w2.shape[1], w2.shape[2]
@@ -102,7 +119,7 @@ def canonical_to_trtllm(w13: torch.Tensor, w13_scale: torch.Tensor, w2: torch.Te
     if halves == "w3_w1":
         w13 = torch.cat([w13[:, inter:], w13[:, :inter]], dim=1)
         w13_scale = torch.cat([w13_scale[:, inter:], w13_scale[:, :inter]], dim=1)
-    p13, p13s, p2, p2s = (p.to(w13.device) for p in _perms(two_i, half_h, hidden, half_i))
+    p13, p13s, p2, p2s = (p.to(w13.device) for p in _perms(two_i, half_h, hidden, half_i, block))
     g13 = w13[:, p13].contiguous()
     g2 = w2[:, p2].contiguous()
     g13s = torch.stack([interleave_scales(w13_scale[e][p13s]) for e in range(E)]).reshape(E, two_i, -1)

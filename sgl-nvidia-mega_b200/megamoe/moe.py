@@ -183,12 +183,14 @@ class RoutedMoE:
     def from_trtllm(cls, w13, w13_scale, w2, w2_scale, top_k: int, max_rows: int, *, halves: str = "w3_w1",
                     **kwargs) -> "RoutedMoE":
         """A layer from SGLang's processed TRT-LLM-gen MXFP4 weights (the layout
-        the reference's RoutedExpertGemm takes): re-laid once into canonical
-        copies (megamoe.layouts.trtllm_to_canonical); the processed tensors are
-        not read afterwards."""
+        the reference's RoutedExpertGemm takes), or NVFP4 ones with
+        weight_format="nvfp4" (plus its scale_2 / input_scale arguments):
+        re-laid once into canonical copies (megamoe.layouts.trtllm_to_canonical);
+        the processed tensors are not read afterwards."""
         from .layouts import trtllm_to_canonical
 
-        c13, c13s, c2, c2s = trtllm_to_canonical(w13, w13_scale, w2, w2_scale, halves=halves)
+        c13, c13s, c2, c2s = trtllm_to_canonical(w13, w13_scale, w2, w2_scale, halves=halves,
+                                                 weight_format=kwargs.get("weight_format", "mxfp4"))
         return cls(c13, c13s, c2, c2s, top_k, max_rows, **kwargs)
 
     def __del__(self):

@@ -1,4 +1,5 @@
-"""The TRT-LLM-gen / FlashInfer processed-weight adapter (megamoe.layouts):
+"""The TRT-LLM-gen / FlashInfer processed-weight adapter (megamoe.layouts), MXFP4
+and NVFP4:
 exact round trips on the CPU; on the GPU, the restated scale swizzle against
 FlashInfer's own block_scale_interleave and a layer built from processed
 weights against the canonical one."""
@@ -39,6 +40,22 @@ def test_trtllm_layout_round_trip(halves):
     back = L.trtllm_to_canonical(*processed, halves=halves)
     for a, b in zip(back, w):
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("halves", ["w3_w1", "w1_w3"])
+def test_trtllm_nvfp4_layout_round_trip(halves):
+    """NVFP4 (E4M3 scale per 16): the same row maps, a scale block of 16."""
+    L = _layouts()
+    layer = O.make_nvfp4_layer(512, 256, 3, shared=False, seed=5)
+    w = [layer[k] for k in ("w13", "w13_scale", "w2", "w2_scale")]
+    assert w[1].shape[-1] == 512 // 16 and w[3].shape[-1] == 256 // 16
+    processed = L.canonical_to_trtllm(*w, halves=halves, weight_format="nvfp4")
+    assert not torch.equal(processed[0], w[0])
+    back = L.trtllm_to_canonical(*processed, halves=halves, weight_format="nvfp4")
+    for a, b in zip(back, w):
+        assert torch.equal(a, b)
+    with pytest.raises(ValueError):
+        L.trtllm_to_canonical(*processed, weight_format="fp8")
 
 
 def test_trtllm_w13_tile_holds_one_gate_up_feature_block():
@@ -83,4 +100,28 @@ def test_layer_from_trtllm_weights_equals_canonical_layer():
     rb, _, pb = b(x.to(dev), ids, wts)
     assert torch.equal(pa, pb)
     sel = pa.flatten().long()  # the rows the slots point to (padding rows are never written)
+    assert torch.equal(ra[sel], rb[sel])
+
+
+@pytest.mark.gpu
+def test_nvfp4_layer_from_trtllm_weights_equals_canonical_layer():
+    import megamoe
+
+    H, I, E, K, T = 1024, 512, 8, 4, 6
+    layer = O.make_nvfp4_layer(H, I, E, shared=False, seed=9)
+    dev = torch.device("cuda", 0)
+    w = [layer[k].to(dev) for k in ("w13", "w13_scale", "w2", "w2_scale")]
+    nv = dict(weight_format="nvfp4", w13_scale_2=layer["w13_scale_2"].to(dev), w2_scale_2=layer["w2_scale_2"].to(dev),
+              input_scale=layer["input_scale"])
+    processed = _layouts().canonical_to_trtllm(*w, weight_format="nvfp4")
+    a = megamoe.RoutedMoE(*w, K, 8, **nv)
+    b = megamoe.RoutedMoE.from_trtllm(*processed, K, 8, **nv)
+    x, _, _ = O.make_inputs(T, H, E, seed=9)
+    g = torch.Generator().manual_seed(9)
+    ids = torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(T)]).int().to(dev)
+    wts = torch.rand((T, K), generator=g).to(dev)
+    ra, _, pa = a(x.to(dev), ids, wts)
+    rb, _, pb = b(x.to(dev), ids, wts)
+    assert torch.equal(pa, pb)
+    sel = pa.flatten().long()
     assert torch.equal(ra[sel], rb[sel])
