@@ -306,13 +306,14 @@ def test_experts_balanced_dealing_groups_sum_to_the_layer():
 
 
 @pytest.mark.parametrize("fmt", ["mxfp4", "nvfp4"])
-@pytest.mark.parametrize("I", [576, 640])
+@pytest.mark.parametrize("I", [320, 384, 576, 640])
 @pytest.mark.parametrize("T,distinct", [(8, None), (40, 6)])
 def test_experts_dsv41_geometry(fmt, I, T, distinct):
     """DeepSeek-V4.1's own geometry (routed_expert_gemm.py:31-40): hidden 5120,
     an intermediate slice of 576 (or its 640 padding), top-6; the down GEMM's K
     is not a multiple of the 256-wide pipeline stage, so its last stage is
-    partial (zero-filled past K)."""
+    partial (zero-filled past K). I = 320 / 384 give two K stages per down tile,
+    so MXFP4 takes two tiles per down unit with a partial second stage."""
     H, E, K = 5120, 32, 6
     if fmt == "nvfp4":
         layer = O.make_nvfp4_layer(H, I, E, shared=True, seed=I + T)
