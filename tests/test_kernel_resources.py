@@ -1,0 +1,56 @@
+"""Resource guard for the CUDA kernels (CPU: nvcc cross-compiles for sm_100a):
+no kernel spills registers to local memory, and the expert kernel fits the
+register budget its two-CTAs-per-SM launch relies on (224 threads x 2 CTAs).
+
+One known exception: the combine + all-reduce + RMSNorm hop keeps one 4-byte
+value in local memory across its cluster barrier (8 bytes of spill traffic in a
+latency-bound kernel that runs once per layer)."""
+
+import os
+import re
+import shutil
+import subprocess
+
+import pytest
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+CSRC = os.path.join(REPO, "sgl-nvidia-mega_b200", "csrc")
+NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
+
+
+def _ptxas_info(source):
+    res = subprocess.run([NVCC, "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++17",
+                          "-I", os.path.join(REPO, "include"), "-I", CSRC, "-Xptxas", "-v", "-c",
+                          os.path.join(CSRC, source), "-o", os.devnull], capture_output=True, text=True, timeout=300)
+    assert res.returncode == 0, res.stderr[-2000:]
+    kernels, current = {}, None
+    for line in res.stderr.splitlines():
+        m = re.search(r"Compiling entry function '([^']+)'", line)
+        if m:
+            current = m.group(1)
+            kernels[current] = {}
+            continue
+        if current is None:
+            continue
+        m = re.search(r"(\d+) bytes spill stores, (\d+) bytes spill loads", line)
+        if m:
+            kernels[current]["spill"] = int(m.group(1)) + int(m.group(2))
+        m = re.search(r"Used (\d+) registers", line)
+        if m:
+            kernels[current]["regs"] = int(m.group(1))
+    return kernels
+
+
+@pytest.mark.skipif(not os.path.exists(NVCC) and shutil.which("nvcc") is None, reason="nvcc not found")
+ALLOWED_SPILL = {"_ZN2mm25finalize_allreduce_kernelILb1EEEvNS_8CommArgsE": 8}
+
+
+@pytest.mark.parametrize("source", ["mm_experts.cu", "mm_route.cu", "mm_finalize.cu", "mm_comm.cu"])
+def test_no_kernel_spills(source):
+    kernels = _ptxas_info(source)
+    assert kernels, "ptxas reported no kernels"
+    for name, info in kernels.items():
+        assert info.get("spill", 0) <= ALLOWED_SPILL.get(name, 0), (name, info)
+        if "expert_kernel" in name:
+            # 2 CTAs x 224 threads per SM within 65,536 registers: <= 146, allocated in steps of 8
+            assert info["regs"] <= 144, (name, info)
