@@ -41,10 +41,10 @@ def _ptxas_info(source):
     return kernels
 
 
-@pytest.mark.skipif(not os.path.exists(NVCC) and shutil.which("nvcc") is None, reason="nvcc not found")
 ALLOWED_SPILL = {"_ZN2mm25finalize_allreduce_kernelILb1EEEvNS_8CommArgsE": 8}
 
 
+@pytest.mark.skipif(not os.path.exists(NVCC) and shutil.which("nvcc") is None, reason="nvcc not found")
 @pytest.mark.parametrize("source", ["mm_experts.cu", "mm_route.cu", "mm_finalize.cu", "mm_comm.cu"])
 def test_no_kernel_spills(source):
     kernels = _ptxas_info(source)
