@@ -357,9 +357,11 @@ def run_mm(args):
     if os.path.exists(tpath):
         try:
             with open(tpath) as f:
-                tj = json.load(f)
-            if int(tj["world"]) == world and int(tj["hidden"]) == H and int(tj["intermediate"]) == I:
-                traffic = float(tj["traffic_bytes_per_expert"]) * (last_d + 1)
+                entries = json.load(f)
+            for tj in entries if isinstance(entries, list) else [entries]:
+                if (int(tj["world"]) == shards and int(tj["hidden"]) == H and int(tj["intermediate"]) == I
+                        and tj.get("format", "mxfp4") == fmt):
+                    traffic = float(tj["traffic_bytes_per_expert"]) * (last_d + n_shared)
         except Exception:
             traffic = None
 
