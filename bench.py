@@ -77,6 +77,28 @@ def parse_args():
     return ap.parse_args()
 
 
+def routing_rule(config):
+    """(renormalize, eps) of a BASELINE config's routing weights: config 4 follows
+    GLM-5.3 (bf16(scale * s / (sum + 1e-20)), glm5_3/sm103/moe/routing.py:3-11);
+    the others renormalize by the plain sum."""
+    return ("scaled_bf16", 1e-20) if config == "4" else (True, 0.0)
+
+
+def workload_name(config, T, shards, hidden, inter, experts):
+    """The workload string both arms report for one layer of BASELINE `config`."""
+    tp, ep = partition(shards, CONFIGS[config][3])
+    fmt_name = "MXFP4" if CONFIGS[config][3] == "mxfp4" else "NVFP4"
+    if shards <= 1:
+        split = ""
+    elif config == "2":
+        split = f" (TP{shards}: {inter // shards} per rank)"
+    else:
+        split = f" (TP{tp} x EP{ep}: {experts // ep} experts x {inter // tp} per rank)"
+    rule = ", GLM-5.3 bf16 weights" if config == "4" else ""
+    return (f"BASELINE config {config}: one routed-MoE layer, hidden {hidden}, {experts} routed + 1 shared experts, "
+            f"intermediate {inter}{split}, sigmoid+bias top-{K}{rule}, scale {SCALE}, {fmt_name}, {T} tokens")
+
+
 def peaks():
     path = os.path.join(REPO, "MEASURED_PEAKS.json")
     try:
@@ -246,19 +268,22 @@ def run_mm(args):
     shards = args.slice if args.slice > 1 else world  # ranks the layer is sharded over
     moe, w, shared, router, bias, xs, info = build_layer(rank, shards, T, dev, fmt)
     bufs = {}
-    out_buf = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
     peer = world > 1 and args.combine == "peer"
     comm = megamoe.PeerAllReduce(T, H) if peer else None
 
-    def step(x):
+    renorm, eps = routing_rule(args.config)
+
+    def step(x, b=None):
+        b = bufs if b is None else b
         if world == 1 or peer:
-            return moe.forward(x, router_weight=router, bias=bias, routed_scaling_factor=SCALE, buffers=bufs,
-                               comm=comm)
+            return moe.forward(x, router_weight=router, bias=bias, routed_scaling_factor=SCALE, buffers=b,
+                               comm=comm, renormalize=renorm, renormalize_epsilon=eps)
         part = moe.forward(x, router_weight=router, bias=bias, routed_scaling_factor=SCALE, partial=True,
-                           buffers=bufs)
+                           buffers=b, renormalize=renorm, renormalize_epsilon=eps)
         dist.all_reduce(part)
-        megamoe.finalize_partial(part, out=out_buf)
-        return out_buf
+        out = b.setdefault("final", torch.empty((T, H), dtype=torch.bfloat16, device=dev))
+        megamoe.finalize_partial(part, out=out)
+        return out
 
     def barrier():
         torch.cuda.synchronize()
@@ -327,22 +352,13 @@ def run_mm(args):
     peak, peak_kind = peaks()
     achieved = k_bytes / (k_ms / 1e3) / 1e9
 
-    # end to end through the public API with host buffers
+    # end to end through the public API with host buffers: every step copies its
+    # x from pinned host memory and its output back, pipelined on a copy stream
     host_x = torch.empty((POOL, T, H), dtype=torch.bfloat16).pin_memory()
     host_x.copy_(xs.cpu())
-    host_out = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
-    xdev = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
     e2e_steps = min(args.steps, 1000)
     barrier()
-    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s2.record()
-    for i in range(e2e_steps):
-        xdev.copy_(host_x[i % POOL], non_blocking=True)
-        out = step(xdev)
-        host_out.copy_(out, non_blocking=True)
-    e2.record()
-    torch.cuda.synchronize()
-    e2e_ms = s2.elapsed_time(e2)
+    e2e_ms = e2e_pipelined(step, host_x, e2e_steps, dev)
     if dist is not None:
         t = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -368,15 +384,12 @@ def run_mm(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(w, shared, router, bias, xs, T, moe if fmt == "nvfp4" else None,
-                           max_experts=None if args.config == "2" else 6)
+                           max_experts=None if args.config == "2" else 6, renorm=(renorm, eps))
     fmt_name = "MXFP4" if fmt == "mxfp4" else "NVFP4"
     if args.config == "2":
         par = f"tp{shards}" if shards > 1 else "single"
-        split = f" (TP{shards}: {I // shards} per rank)" if shards > 1 else ""
     else:
         par = f"tp{info['tp']}xep{info['ep']}" if shards > 1 else "single"
-        split = (f" (TP{info['tp']} x EP{info['ep']}: {info['local']} experts x {info['ir']} per rank)"
-                 if shards > 1 else "")
     if shards != world:
         par = f"slice of {par} (rank 0's share on one GPU, no exchange)"
 
@@ -395,9 +408,7 @@ def run_mm(args):
         "dtype": f"{fmt} weights x {fmt}(3-term) activations, fp32 accumulate",
         "data": f"synthetic (seeded random {fmt_name} weights, bf16 x ~ N(0,1))",
         "config": {
-            "workload": f"BASELINE config {args.config}: one routed-MoE layer, hidden {H}, {E} routed + 1 shared "
-                        f"experts, intermediate {I}{split}, sigmoid+bias top-{K}, scale {SCALE}, {fmt_name}, "
-                        f"{T} tokens",
+            "workload": workload_name(args.config, T, shards, H, I, E),
             "tokens": T,
             "parallelism": par,
             "l2": f"inputs larger than L2 (~{layer_bytes / 1e9:.2f} GB of expert weights per step, "
@@ -422,7 +433,9 @@ def run_mm(args):
             "launch_ms": k_ms,
         },
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
-                "d2h_bytes_per_step": T * H * 2, "steps": e2e_steps},
+                "d2h_bytes_per_step": T * H * 2, "steps": e2e_steps,
+                "copies": "per step: x H2D from pinned memory and the output D2H, on a copy stream overlapping the "
+                          "neighbouring steps (double-buffered)"},
         "gpu_launches": args.steps * (4 if world == 1 or peer else 5),
         "clocks": clocks.summary(),
         "cpu_baseline": cpu,
@@ -436,6 +449,54 @@ def run_mm(args):
             comm.close()
         dist.barrier()
         dist.destroy_process_group()
+
+
+def e2e_pipelined(step, host_x, n, dev):
+    """Device time (ms, CUDA events on the compute stream) of n steps through the
+    public API with host buffers. Step i copies x from pinned host memory
+    (host_x[i % pool]) and its output back to pinned host memory; the copies
+    run on a copy stream, double-buffered, so that step i's output copy and
+    step i+1's input copy overlap the neighbouring steps' kernels. The region
+    opens before the first input copy and closes after the last output copy."""
+    comp = torch.cuda.current_stream(dev)
+    copy = torch.cuda.Stream(device=dev)
+    T, Hh = host_x.shape[1], host_x.shape[2]
+    xdev = [torch.zeros((T, Hh), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    host_out = torch.empty((2, T, Hh), dtype=torch.bfloat16).pin_memory()
+    bufs = [{}, {}]
+    step(xdev[0], bufs[0])  # allocate each slot's buffers outside the timed region
+    step(xdev[1], bufs[1])
+    torch.cuda.synchronize()
+    ev = lambda: torch.cuda.Event()  # noqa: E731
+    h2d, done, d2h = [ev(), ev()], [ev(), ev()], [ev(), ev()]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    pool = host_x.shape[0]
+    start.record(comp)
+    copy.wait_event(start)
+    with torch.cuda.stream(copy):
+        xdev[0].copy_(host_x[0], non_blocking=True)
+        h2d[0].record(copy)
+    for i in range(n):
+        slot = i & 1
+        if i + 1 < n:  # the next step's input, once step i - 1 has consumed that slot
+            with torch.cuda.stream(copy):
+                if i >= 1:
+                    copy.wait_event(done[slot ^ 1])
+                xdev[slot ^ 1].copy_(host_x[(i + 1) % pool], non_blocking=True)
+                h2d[slot ^ 1].record(copy)
+        comp.wait_event(h2d[slot])
+        if i >= 2:
+            comp.wait_event(d2h[slot])  # step i - 2's output has left this slot's buffer
+        out = step(xdev[slot], bufs[slot])
+        done[slot].record(comp)
+        with torch.cuda.stream(copy):
+            copy.wait_event(done[slot])
+            host_out[slot].copy_(out, non_blocking=True)
+            d2h[slot].record(copy)
+    comp.wait_event(d2h[(n - 1) & 1])
+    end.record(comp)
+    torch.cuda.synchronize()
+    return start.elapsed_time(end)
 
 
 # --------------------------------------------------------------------------- config 5
@@ -638,13 +699,14 @@ def run_stack(args):
 
 
 # --------------------------------------------------------------------------- CPU legs
-def _cpu_layer_step(x_bf16, router_bf16, bias, experts_w, shared_w, oracle, max_experts=None):
+def _cpu_layer_step(x_bf16, router_bf16, bias, experts_w, shared_w, oracle, max_experts=None,
+                    renorm=(True, 0.0)):
     """One layer on the CPU oracle: routing, then the activated experts (all of
     them, or the first max_experts) and the shared expert. Returns (seconds of
     routing, seconds per expert MLP, distinct experts)."""
     t0 = time.perf_counter()
     logits = oracle.router_gemv(oracle.bf16_bits(x_bf16), oracle.bf16_bits(router_bf16))
-    w, ids = oracle.gate_topk(logits, bias.numpy(), K, scale=SCALE)
+    w, ids = oracle.gate_topk(logits, bias.numpy(), K, scale=SCALE, renormalize=renorm[0], eps=renorm[1])
     t1 = time.perf_counter()
     x = x_bf16.float()
     out = torch.zeros_like(x)
@@ -661,7 +723,7 @@ def _cpu_layer_step(x_bf16, router_bf16, bias, experts_w, shared_w, oracle, max_
     return t1 - t0, (t2 - t1) / (len(ran) + 1), len(experts)
 
 
-def cpu_baseline(w, shared, router, bias, xs, T, nv_moe=None, max_experts=None):
+def cpu_baseline(w, shared, router, bias, xs, T, nv_moe=None, max_experts=None, renorm=(True, 0.0)):
     """The oracle port timed on this host's cores on the same workload, after
     one warm-up step: a full layer step (every activated expert + shared), or
     with max_experts a bounded sample whose layer time is routing + (distinct
@@ -674,7 +736,7 @@ def cpu_baseline(w, shared, router, bias, xs, T, nv_moe=None, max_experts=None):
     needed = set()
     for xi in xc:
         logits = oracle.router_gemv(oracle.bf16_bits(xi), oracle.bf16_bits(router_c))
-        _, ids = oracle.gate_topk(logits, bias_c.numpy(), K, scale=SCALE)
+        _, ids = oracle.gate_topk(logits, bias_c.numpy(), K, scale=SCALE, renormalize=renorm[0], eps=renorm[1])
         ex = sorted(set(ids.flatten().tolist()))
         needed |= set(ex if max_experts is None else ex[:max_experts])
     if nv_moe is None:
@@ -687,9 +749,9 @@ def cpu_baseline(w, shared, router, bias, xs, T, nv_moe=None, max_experts=None):
                  for e in needed}
         sh = tuple(t[0].cpu() for t in shared[:4]) + (None, "exact", 3,
                                                        (float(shared[4][0]), float(shared[5][0]), ins))
-    _cpu_layer_step(xc[0], router_c, bias_c, lambda e: cache[e], sh, oracle, max_experts)  # warm-up
+    _cpu_layer_step(xc[0], router_c, bias_c, lambda e: cache[e], sh, oracle, max_experts, renorm)  # warm-up
     route_s, per_expert_s, d = _cpu_layer_step(xc[1], router_c, bias_c, lambda e: cache[e], sh, oracle,
-                                               max_experts)
+                                               max_experts, renorm)
     layer_s = route_s + (d + 1) * per_expert_s
     sample = (f"1 full layer step ({T} tokens, every activated expert + shared) after 1 warm-up"
               if max_experts is None else
@@ -701,51 +763,71 @@ def cpu_baseline(w, shared, router, bias, xs, T, nv_moe=None, max_experts=None):
 
 def run_reference(args):
     """The reference path's CPU implementation (the oracle port: the reference
-    itself has no CPU MoE path) on all host threads, on this arm's workload.
-    Each step is a bounded sample: the routing of one token batch plus one of
-    its activated experts' MLP; the layer time is the routing time plus (distinct
-    + 1) times the mean expert time. Steps stop after a ~150 s budget."""
+    itself has no CPU MoE path) on all host threads, on this arm's workload
+    (or 4 with --config 4): every step is one full layer
+    step, router GEMV -> top-k -> every activated expert's MLP (dequantized
+    FP4 weights, fp32) -> weighted combine + the shared expert, on the next of 4
+    seeded token batches. Each expert's weights are generated once (seeded by
+    its id) and kept resident, as on the GPU. The run stops early, with the
+    steps it completed reported, when it would outlast a few minutes."""
     from oracle import oracle
 
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    global H, I, E
+    H, I, E, fmt = CONFIGS[args.config]
     torch.set_num_threads(os.cpu_count() or 1)
     threads = torch.get_num_threads()
-    T = args.tokens if args.tokens is not None else 8
-    g = torch.Generator().manual_seed(1000)
+    T = args.tokens if args.tokens is not None else (80 if args.config == "4" else 8)
+    renorm = routing_rule(args.config)
+    nv = fmt == "nvfp4"
+    ins = (8.0 / (6.0 * 448.0), 2.0 ** -4)  # NVFP4 static input scales (FC1 for |x| <= 8)
 
-    def rnd(shape, lo, hi):
-        return torch.randint(lo, hi + 1, shape, dtype=torch.uint8, generator=g)
+    def expert(seed):
+        g = torch.Generator().manual_seed(seed)
+        codes = lambda shape: torch.randint(0, 256, shape, dtype=torch.uint8, generator=g)  # noqa: E731
+        if not nv:
+            sc = lambda shape: torch.randint(117, 122, shape, dtype=torch.uint8, generator=g)  # noqa: E731
+            return (codes((2 * I, H // 2)), sc((2 * I, H // 32)), codes((H, I // 2)), sc((H, I // 32)), None,
+                    "exact")
+        sf = lambda shape: (0.5 + 3.5 * torch.rand(shape, generator=g)).to(torch.float8_e4m3fn).view(  # noqa: E731
+            torch.uint8)
+        s2 = 2.0 ** -8 * (1.0 + 0.25 * float(torch.rand((), generator=g)))
+        return (codes((2 * I, H // 2)), sf((2 * I, H // 16)), codes((H, I // 2)), sf((H, I // 16)), None, "exact",
+                3, (s2, s2, ins))
 
+    cache = {}
+
+    def weights_of(e):
+        if e not in cache:
+            cache[e] = expert(1000 + e)
+        return cache[e]
+
+    shared_w = expert(999)
     gx = torch.Generator().manual_seed(7)
     router = (torch.randn((E, H), generator=gx) * 0.02).to(torch.bfloat16)
     bias = (torch.randn((E,), generator=gx) * 0.01).float()
-    x = torch.randn((T, H), generator=gx).to(torch.bfloat16)
-    expert = (rnd((2 * I, H // 2), 0, 255), rnd((2 * I, H // 32), 117, 121), rnd((H, I // 2), 0, 255),
-              rnd((H, I // 32), 117, 121))
-    budget = 150.0
-    route_t, exp_t, distinct = [], [], []
+    xs = [torch.randn((T, H), generator=gx).to(torch.bfloat16) for _ in range(4)]
+    for xb in xs:  # every batch's experts resident before the timed steps (set-up)
+        logits = oracle.router_gemv(oracle.bf16_bits(xb), oracle.bf16_bits(router))
+        _, ids = oracle.gate_topk(logits, bias.numpy(), K, scale=SCALE, renormalize=renorm[0], eps=renorm[1])
+        for e in set(ids.flatten().tolist()):
+            weights_of(e)
+    budget = 240.0
+    step_s, distinct = [], []
     t_begin = time.perf_counter()
-    done = 0
     for i in range(args.warmup + args.steps):
-        t0 = time.perf_counter()
-        logits = oracle.router_gemv(oracle.bf16_bits(x), oracle.bf16_bits(router))
-        w, ids = oracle.gate_topk(logits, bias.numpy(), K, scale=SCALE)
+        r_s, e_s, d = _cpu_layer_step(xs[i % 4], router, bias, weights_of, shared_w, oracle, None, renorm)
         t1 = time.perf_counter()
-        e = int(ids.flatten()[i % ids.size])
-        toks = [t for t in range(T) if e in ids[t]]
-        oracle.expert_mlp(x[toks].float(), *expert, None, "exact")
-        t2 = time.perf_counter()
         if i >= args.warmup:
-            route_t.append(t1 - t0)
-            exp_t.append(t2 - t1)
-            distinct.append(len(set(ids.flatten().tolist())))
-            done += 1
-        if time.perf_counter() - t_begin > budget and done >= 3:
+            step_s.append(r_s + e_s * (d + 1))
+            distinct.append(d)
+        if t1 - t_begin > budget and len(step_s) >= 1:
             break
-    layer_s = float(np.mean(route_t)) + (float(np.mean(distinct)) + 1) * float(np.mean(exp_t))
-    value = T / layer_s
+    done = len(step_s)
+    ms = float(np.mean(step_s)) * 1e3
+    value = T / (ms / 1e3)
     line = {
         "impl": "reference",
         "metric": METRIC,
@@ -754,18 +836,20 @@ def run_reference(args):
         "n_gpus": args.gpus,
         "steps": done,
         "warmup": args.warmup,
-        "ms_per_step": layer_s * 1e3,
+        "ms_per_step": ms,
+        "us_per_layer": ms * 1e3,
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
-        "dtype": "fp32 (dequantized MXFP4)",
+        "dtype": f"fp32 (dequantized {fmt.upper()} weights, bf16 x)",
         "data": "synthetic (seeded)",
-        "config": {"workload": f"BASELINE config 2 layer (hidden {H}, {E}+1 experts, intermediate {I}, top-{K}, "
-                               f"{T} tokens) on the CPU oracle port",
-                   "tokens": T},
+        "config": {"workload": workload_name(args.config, T, args.gpus, H, I, E), "tokens": T,
+                   "parallelism": "single" if args.gpus <= 1 else f"the whole layer on rank 0's host cores",
+                   "distinct_experts_per_step": float(np.mean(distinct)) if distinct else None},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": f"{done} steps of (routing + 1 activated expert MLP), layer time = routing + "
-                                   f"(distinct + 1) x mean expert time; steps capped by a {budget:.0f} s budget"},
+                         "sample": f"{done} full layer steps of {T} tokens (router GEMV, top-k, every activated "
+                                   f"expert's MLP + the shared expert, combine) after {args.warmup} warm-up; "
+                                   f"at most {budget:.0f} s"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

@@ -55,6 +55,15 @@ extern "C" {
 #define MM_SCORE_SQRTSOFTPLUS 2 /* s = sqrt(log1p(exp(x))) (x above 20: sqrt x),
                                    key = s + bias, w = s / sum (DeepSeek-V4.1) */
 
+/* ---- routing weight rules (mm_gate_args.renormalize) ------------------- */
+#define MM_RENORM_NONE 0        /* w = s * scale                                  */
+#define MM_RENORM_SUM 1         /* w = (s / sum) * scale (sum + eps when eps > 0;
+                                   a zero sum counts as 1); the sum in slot order */
+#define MM_RENORM_SCALED_BF16 2 /* GLM-5.3 (glm5_3/sm103/moe/routing.py:3-11):
+                                   w = bf16(scale * s / (sum + eps)), the sum in
+                                   the order of a warp xor-butterfly over the
+                                   slots; sigmoid or sqrtsoftplus scores        */
+
 /* ---- expert weight formats ---------------------------------------------- */
 #define MM_WEIGHT_MXFP4 0 /* E2M1 codes + one E8M0 scale per 32 along K      */
 #define MM_WEIGHT_NVFP4 1 /* E2M1 codes + one E4M3 scale per 16 along K and
@@ -116,7 +125,7 @@ typedef struct mm_gate_args {
   const int32_t *num_valid;  /* device int32 [1] or NULL: rows >= *num_valid get
                                 id -1 and weight 0 (padded graph rows)            */
   int32_t score_func;        /* MM_SCORE_*                                        */
-  int32_t renormalize;       /* 1: w = s / sum(selected s) (always for softmax)   */
+  int32_t renormalize;       /* MM_RENORM_* (softmax always renormalizes)         */
   float routed_scaling;      /* multiplies every weight                           */
   float renorm_eps;          /* > 0: divide by sum + eps; else by the guarded sum */
   float *weights;            /* out [T, top_k] fp32                               */
@@ -138,7 +147,22 @@ typedef struct mm_layer_info {
   int64_t shared_row_base; /* first rows_out row of the shared expert's T rows    */
   int64_t route_words;     /* int32 words of the route record at max_tokens       */
   int64_t weight_bytes;    /* algorithmic FP4 + scale bytes of one expert         */
+  int32_t act_terms;       /* FP4 terms per activation                            */
+  int32_t h_row_bytes;     /* bytes of one h code row (I padded to 256 features)  */
+  int64_t h_scale_row_bytes; /* bytes of one h scale row                          */
 } mm_layer_info;
+
+/* The layer's quantized activations (mm_layer_read_scratch): the routed input
+ * as FP4 terms, codes [3][max_tokens][H/2] (two E2M1 per byte, low nibble =
+ * even element) and scales [3][max_tokens][H/block] (E8M0 per 32, or E4M3 per
+ * 16 for NVFP4), rows = tokens; the SwiGLU output h likewise, codes
+ * [3][rows_capacity][h_row_bytes] and scales [3][rows_capacity]
+ * [h_scale_row_bytes], rows in the permuted order of the deferred rows. Terms
+ * past act_terms are unused. */
+#define MM_SCRATCH_X_CODES 0
+#define MM_SCRATCH_X_SCALES 1
+#define MM_SCRATCH_H_CODES 2
+#define MM_SCRATCH_H_SCALES 3
 
 /* Whole-step arguments (mm_layer_forward). */
 typedef struct mm_comm mm_comm; /* opaque handle: see mm_comm_create */
@@ -208,8 +232,9 @@ int mm_route(const int32_t *ids, int32_t *permuted, int32_t *record, int32_t tok
  * Outputs equal mm_gate_topk followed by mm_route. gate->ids may be NULL (ids
  * not returned). Scratch: 8.25 KB of the library's static device memory per
  * GPU, held until exit; tokens * top_k <= 2048, larger requests are rejected
- * with MM_ERR_INVALID. The first call on a device sets the scratch up (symbol lookup,
- * a cudaMemset of its counter) and should come before any stream capture. All
+ * with MM_ERR_INVALID. The first call on a device sets the scratch up (the symbol's
+ * device address, the kernel's shared-memory limit) and should come before any
+ * stream capture. All
  * calls on a device share the scratch: calls that overlap on the GPU (other
  * streams) race; consecutive calls on one stream do not. */
 int mm_gate_route_noalloc(const mm_gate_args *gate, int32_t tokens, int32_t router_experts,
@@ -243,10 +268,22 @@ int mm_comm_handle(const mm_comm *comm, void *handle);
  * rank order; this rank's own entry is ignored). Once per comm. */
 int mm_comm_open(mm_comm *comm, const void *handles);
 int mm_comm_destroy(mm_comm *comm);
+/* Opens a group whose members all live in this process (one process driving
+ * several GPUs, or several ranks of one GPU): members[q] is rank q's comm
+ * (members[rank] == comm), every member of the same world, max_tokens and
+ * hidden. Peer access is enabled from this comm's device to each member's.
+ * Instead of mm_comm_open; once per comm. No reference counterpart (the
+ * reference's groups are one process per GPU, all_reduce_mhc.py:1194). */
+int mm_comm_open_local(mm_comm *comm, mm_comm *const *members);
 /* Synchronizes and reads (then clears) the comm's device error word:
- * MM_OK or MM_ERR_DEVICE_TIMEOUT (a peer's partial never arrived within 1.5 s;
- * the group's comms must then be rebuilt). */
+ * MM_OK or MM_ERR_DEVICE_TIMEOUT (a peer's partial never arrived within the
+ * wait budget; the group's comms must then be rebuilt). */
 int mm_comm_check(mm_comm *comm);
+/* The budget of the mailbox poll of this comm's launches, 1 us .. 60 s
+ * (default 1.5 s). A poll that runs out sets the comm's error word and the
+ * launch ends. The reference's remote waits carry deadlines too
+ * (common/sync.py:157-185, all_reduce_mhc.py:917-924); there they trap. */
+int mm_comm_set_wait_budget(mm_comm *comm, int64_t microseconds);
 
 /* out[t] = bf16( sum_{r = 0..world-1} y_r[t] ) in fp32, rank order, where
  * y_r = bf16(bf16(sum_k w * rows_r[perm_r]) + shared_r) is rank r's partial
@@ -290,6 +327,30 @@ int mm_layer_gate_experts(mm_layer *layer, const uint16_t *x, const mm_gate_args
                           int32_t tokens, int32_t *permuted, int32_t *record,
                           uint16_t *rows, void *stream);
 
+/* mm_layer_experts and mm_layer_gate_experts with the routed input already
+ * MXFP8-quantized, as SGLang hands it to the reference
+ * (Mxfp4FlashinferTrtllmMoEMethod.quantize_routed_input; the reference's
+ * RoutedExpertGemm.__call__(x_quant, x_scale, topk_ids, topk_weights),
+ * routed_expert_gemm.py:703, and gate_topk_and_gemms(x_quant, x_scale, ...),
+ * :776): x_quant u8 [T, H] E4M3 codes, x_scale u8 [T, H/32] E8M0 scales
+ * (row-major, unswizzled), both 16-byte aligned. Each element enters the
+ * chain as e4m3 * 2^(scale - 127) (exact, one fp32 rounding for subnormal
+ * results), then as the layer's FP4 terms. */
+int mm_layer_experts_mxfp8(mm_layer *layer, const uint8_t *x_quant, const uint8_t *x_scale,
+                           const int32_t *ids, int32_t tokens, int32_t *permuted,
+                           int32_t *record, uint16_t *rows, void *stream);
+int mm_layer_gate_experts_mxfp8(mm_layer *layer, const uint8_t *x_quant, const uint8_t *x_scale,
+                                const mm_gate_args *gate, int32_t tokens, int32_t *permuted,
+                                int32_t *record, uint16_t *rows, void *stream);
+
+/* Bytes of one of the layer's activation buffers (MM_SCRATCH_*), -1 for an
+ * unknown one; and a stream-ordered device-to-device copy of it into dst
+ * (exactly that many bytes). For inspecting the quantization bytes the chain
+ * multiplies; no reference counterpart. */
+int64_t mm_layer_scratch_bytes(const mm_layer *layer, int32_t which);
+int mm_layer_read_scratch(const mm_layer *layer, int32_t which, void *dst, int64_t bytes,
+                          void *stream);
+
 /* Launches the expert kernel again on the work tables of this layer's last
  * front pass (same tokens, routing and input): re-computes the same rows. The
  * tables must be re-armed first (mm_layer_rearm_experts) each time: a launch
@@ -303,6 +364,20 @@ int mm_layer_rerun_experts(mm_layer *layer, int32_t tokens, const int32_t *recor
  * segment mailboxes and the claim counter, stream-ordered) so that
  * mm_layer_rerun_experts can launch on them again. */
 int mm_layer_rearm_experts(mm_layer *layer, void *stream);
+
+/* Re-arms the work tables like mm_layer_rearm_experts, but with every segment's
+ * gate_up -> down mailbox set far below reach, so that the next
+ * mm_layer_rerun_experts cannot finish: its down units' bounded waits run out,
+ * the launch ends and mm_layer_check reports MM_ERR_DEVICE_TIMEOUT. A test
+ * hook for the timeout path (a flag that nothing sets); the next front pass
+ * (any layer call) re-arms the tables normally. No reference counterpart. */
+int mm_layer_block_downs(mm_layer *layer, void *stream);
+
+/* The budget of every bounded device wait of this layer's expert launches,
+ * 1 us .. 60 s (default 1.5 s). A wait that runs out sets the layer's error
+ * word, every later wait of the launch gives up at once, and the launch ends
+ * (its copies and MMAs in flight drained first). */
+int mm_layer_set_wait_budget(mm_layer *layer, int64_t microseconds);
 
 /* The whole MoE step: [router GEMV] -> top-k -> route -> experts -> combine. */
 int mm_layer_forward(mm_layer *layer, const mm_forward_args *args, void *stream);

@@ -187,7 +187,19 @@ void or_gate_topk(const float *logits, const float *bias_main, int num_valid, in
     } else {
       float sum = 0.0f;
       for (int k = 0; k < K; ++k) { w[k] = or_score(score_func, l[sel[k]]); sum = sum + w[k]; }
-      if (renormalize) {
+      if (renormalize == 2) {
+        /* GLM-5.3 (glm5_3/sm103/moe/routing.py:3-11; routing_weight in
+         * glm5_3/sm103/primitives/ptx_tc.py): the selected scores summed in the
+         * order of a warp xor-butterfly with slot k in lane k (lane 0's order is
+         * the halving t[i] += t[i + off], off = 8, 4, 2, 1), then
+         * w = bf16(scale * s / (sum + eps)) with the scale multiplied first */
+        float t[16];
+        for (int k = 0; k < 16; ++k) t[k] = k < K ? w[k] : 0.0f;
+        for (int off = 8; off >= 1; off >>= 1)
+          for (int i = 0; i < off; ++i) t[i] = t[i] + t[i + off];
+        const float d = t[0] + eps;
+        for (int k = 0; k < K; ++k) w[k] = bf16_to_f(f_to_bf16((scale * w[k]) / d));
+      } else if (renormalize) {
         const float norm = eps > 0.0f ? sum + eps : (sum > 0.0f ? sum : 1.0f);
         for (int k = 0; k < K; ++k) w[k] = (w[k] / norm) * scale;
       } else {

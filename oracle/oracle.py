@@ -39,12 +39,20 @@ E2M1 = np.array([0, 0.5, 1, 1.5, 2, 3, 4, 6, -0.0, -0.5, -1, -1.5, -2, -3, -4, -
 _lib = None
 
 
+def reference_root() -> Optional[str]:
+    """The reference checkout named by MM_REFERENCE_ROOT (the directory holding
+    sgl_nvidia_mega/), or None when unset or absent."""
+    root = os.environ.get("MM_REFERENCE_ROOT", "")
+    return root if root and os.path.isdir(os.path.join(root, "sgl_nvidia_mega")) else None
+
+
 def build(ref: bool = False) -> None:
-    """Compile the C oracle (and, with ``ref`` and the reference tree present,
-    the reference's route kernels for the CPU)."""
+    """Compile the C oracle (and, with ``ref`` and MM_REFERENCE_ROOT naming a
+    reference checkout, the reference's route kernels for the CPU)."""
     subprocess.run(["make", "-s", "-C", HERE], check=True)
-    if ref and os.path.isdir("/root/reference"):
-        subprocess.run(["make", "-s", "-C", HERE, "ref"], check=True)
+    root = reference_root()
+    if ref and root is not None:
+        subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={root}"], check=True)
 
 
 def lib() -> ctypes.CDLL:
@@ -84,8 +92,13 @@ def router_gemv(x_bf16: np.ndarray, w_bf16: np.ndarray) -> np.ndarray:
     return out
 
 
+# routing weight rules: "scaled_bf16" is GLM-5.3's bf16(scale * s / (sum + eps))
+# with the butterfly-order sum (glm5_3/sm103/moe/routing.py:3-11)
+RENORM = {"none": 0, "sum": 1, "scaled_bf16": 2}
+
+
 def gate_topk(logits: np.ndarray, bias: Optional[np.ndarray], top_k: int, *, score: str = "sigmoid",
-              renormalize: bool = True, scale: float = 1.0, eps: float = 0.0, num_valid: Optional[int] = None,
+              renormalize=True, scale: float = 1.0, eps: float = 0.0, num_valid: Optional[int] = None,
               bias_alt: Optional[np.ndarray] = None, input_ids: Optional[np.ndarray] = None,
               alt_token_id: int = -1):
     logits = np.ascontiguousarray(logits, dtype=np.float32)
@@ -96,7 +109,8 @@ def gate_topk(logits: np.ndarray, bias: Optional[np.ndarray], top_k: int, *, sco
     w = np.empty((T, top_k), dtype=np.float32)
     ids = np.empty((T, top_k), dtype=np.int32)
     sf = {"sigmoid": 0, "softmax": 1, "sqrtsoftplus": 2}[score]
-    lib().or_gate_topk(_p(logits), _p(b), T if num_valid is None else int(num_valid), sf, int(renormalize),
+    rn = RENORM[renormalize] if isinstance(renormalize, str) else int(bool(renormalize))
+    lib().or_gate_topk(_p(logits), _p(b), T if num_valid is None else int(num_valid), sf, rn,
                        c_float(scale), c_float(eps), T, E, top_k, _p(w), _p(ids), _p(ba), _p(tok),
                        ctypes.c_int64(alt_token_id))
     return w, ids
@@ -224,14 +238,16 @@ def nvfp4_dequant(q: np.ndarray, s: np.ndarray, input_scale: float) -> np.ndarra
 
 def dequant_nvfp4(codes: torch.Tensor, scales: torch.Tensor, scale_2: float) -> torch.Tensor:
     """u8 [..., K/2] codes + u8 [..., K/16] E4M3 + fp32 second-level scale ->
-    fp32 [..., K] (ModelOpt NVFP4: w = e2m1 * e4m3 * scale_2)."""
+    fp32 [..., K] (ModelOpt NVFP4: w = e2m1 * e4m3 * scale_2). e2m1 * e4m3 is
+    exact in fp32 (at most 5 significant bits), so the one rounding is that of
+    the product with scale_2, as in an exact evaluation rounded to fp32."""
     lut = torch.from_numpy(E2M1)
     lo = lut[(codes & 0x0F).long()]
     hi = lut[(codes >> 4).long()]
-    vals = torch.stack([lo, hi], dim=-1).reshape(*codes.shape[:-1], codes.shape[-1] * 2).double()
-    sc = torch.from_numpy(e4m3_lut())[scales.long()].double()
-    out = (vals.reshape(*scales.shape, 16) * sc[..., None]).reshape(vals.shape) * float(scale_2)
-    return out.float()
+    vals = torch.stack([lo, hi], dim=-1).reshape(*codes.shape[:-1], codes.shape[-1] * 2)
+    sc = torch.from_numpy(e4m3_lut())[scales.long()]
+    out = (vals.reshape(*scales.shape, 16) * sc[..., None]).reshape(vals.shape)
+    return out * torch.tensor(float(scale_2), dtype=torch.float32)
 
 
 def finalize(rows_bf16: np.ndarray, weights: np.ndarray, permuted: np.ndarray,

@@ -170,6 +170,10 @@ static int check_gate(const mm_gate_args *a, int tokens, int E, int K) {
       a->score_func != MM_SCORE_SQRTSOFTPLUS)
     return fail(MM_ERR_UNSUPPORTED, "gate: score function %d is not built (sigmoid, softmax, sqrtsoftplus)",
                 a->score_func);
+  if (a->renormalize < 0 || a->renormalize > MM_RENORM_SCALED_BF16)
+    return fail(MM_ERR_INVALID, "gate: renormalize %d (0, 1 or MM_RENORM_SCALED_BF16)", a->renormalize);
+  if (a->renormalize == MM_RENORM_SCALED_BF16 && a->score_func == MM_SCORE_SOFTMAX)
+    return fail(MM_ERR_UNSUPPORTED, "gate: the scaled-bf16 rule takes sigmoid or sqrtsoftplus scores");
   return MM_OK;
 }
 
@@ -482,6 +486,7 @@ int mm_layer_create(const mm_layer_desc *desc, mm_layer **out) {
   ea.ks2 = L->ks2;
   ea.tg2 = L->tg2;
   ea.u2 = L->u2;
+  ea.wait_ns = kWaitBudgetNs;
 
   ce = expert_kernel_configure(L->fmt);
   if (ce == cudaSuccess)
@@ -516,6 +521,9 @@ int mm_layer_get_info(const mm_layer *L, mm_layer_info *info) {
   info->shared_row_base = L->shared_row_base;
   info->route_words = L->route_words_max;
   info->weight_bytes = 3LL * L->H * L->I / 2 + 3LL * L->H * L->I / L->block;
+  info->act_terms = L->terms;
+  info->h_row_bytes = L->ea.hq_row;
+  info->h_scale_row_bytes = L->ea.hs_row;
   return MM_OK;
 }
 
@@ -524,14 +532,17 @@ static cudaError_t launch_experts(mm_layer *L, const ExpertArgs &ea, void *strea
 }
 
 // One launch of the router GEMV (w non-null) and the MXFP4-terms quantization
-// of x into the layer's scratch (extra CTAs of the same grid).
+// of x (bf16, or MXFP8 codes x8 with scales s8) into the layer's scratch
+// (extra CTAs of the same grid).
 static int launch_router_quant(mm_layer *L, const uint16_t *x, const uint16_t *w, float *logits, int tokens,
-                               void *stream) {
+                               void *stream, const uint8_t *x8 = nullptr, const uint8_t *s8 = nullptr) {
   if (w && (L->H % 1024 || L->H > kMaxRouterHidden))
     return fail(MM_ERR_INVALID, "router GEMV: hidden %d must be a multiple of 1024, <= %d", L->H, kMaxRouterHidden);
   if (w && !aligned(w, 16)) return fail(MM_ERR_INVALID, "router weight must be 16-byte aligned");
   RouterArgs a = {};
   a.x = x;
+  a.x8 = x8;
+  a.s8 = s8;
   a.w = w;
   a.logits = logits;
   a.tokens = tokens;
@@ -552,13 +563,16 @@ static int launch_router_quant(mm_layer *L, const uint16_t *x, const uint16_t *w
   return MM_OK;
 }
 
-// [quantization] + front (gate or given ids) + experts
+// [quantization] + front (gate or given ids) + experts. The routed input is bf16
+// x, or MXFP8 (x8 codes [T, H], s8 E8M0 scales [T, H/32]) when x is null.
 static int run_front_and_experts(mm_layer *L, const uint16_t *x, const mm_gate_args *gate,
                                  const int32_t *ids, int tokens, int32_t *permuted, int32_t *record,
-                                 uint16_t *rows, void *stream, bool quant_done = false) {
-  if (!x || !permuted || !record || !rows) return fail(MM_ERR_INVALID, "layer call: null pointer");
+                                 uint16_t *rows, void *stream, bool quant_done = false,
+                                 const uint8_t *x8 = nullptr, const uint8_t *s8 = nullptr) {
+  if ((!x && !(x8 && s8)) || !permuted || !record || !rows) return fail(MM_ERR_INVALID, "layer call: null pointer");
   if (tokens < 1 || tokens > L->Tmax) return fail(MM_ERR_INVALID, "tokens %d outside 1..%d", tokens, L->Tmax);
-  if (!aligned(x, 16) || !aligned(rows, 16)) return fail(MM_ERR_INVALID, "x and rows must be 16-byte aligned");
+  if ((x && !aligned(x, 16)) || (x8 && !aligned(x8, 16)) || !aligned(rows, 16))
+    return fail(MM_ERR_INVALID, "x (or x_quant) and rows must be 16-byte aligned");
   FrontArgs f = {};
   if (gate) {
     int rc = check_gate(gate, tokens, L->R, L->K);
@@ -585,7 +599,7 @@ static int run_front_and_experts(mm_layer *L, const uint16_t *x, const mm_gate_a
   f.route.m2 = L->u2;
   MM_CUDA(cudaSetDevice(L->d.device));
   if (!quant_done) {
-    int rc = launch_router_quant(L, x, nullptr, nullptr, tokens, stream);
+    int rc = launch_router_quant(L, x, nullptr, nullptr, tokens, stream, x ? nullptr : x8, x ? nullptr : s8);
     if (rc) return rc;
   }
   MM_CUDA(launch(front_kernel, dim3(tokens), dim3(512), route_smem_bytes(tokens, L->E), stream, f));
@@ -603,6 +617,26 @@ int mm_layer_rearm_experts(mm_layer *L, void *stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   MM_CUDA(cudaMemsetAsync(L->flags, 0, sizeof(int) * L->max_segs, s));
   MM_CUDA(cudaMemsetAsync(L->ctrl + kCtrlClaim, 0, sizeof(int), s));
+  return MM_OK;
+}
+
+int mm_layer_block_downs(mm_layer *L, void *stream) {
+  if (!L) return fail(MM_ERR_INVALID, "mm_layer_block_downs: null layer");
+  MM_CUDA(cudaSetDevice(L->d.device));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // every mailbox starts near INT_MIN: the gate_up units' increments never bring it
+  // to the down units' target, so their bounded waits run out
+  MM_CUDA(cudaMemsetAsync(L->flags, 0xc0, sizeof(int) * L->max_segs, s));
+  MM_CUDA(cudaMemsetAsync(L->ctrl + kCtrlClaim, 0, sizeof(int), s));
+  return MM_OK;
+}
+
+int mm_layer_set_wait_budget(mm_layer *L, int64_t microseconds) {
+  if (!L) return fail(MM_ERR_INVALID, "mm_layer_set_wait_budget: null layer");
+  if (microseconds < 1 || microseconds > 60000000)
+    return fail(MM_ERR_INVALID, "mm_layer_set_wait_budget: %lld us outside 1..60000000",
+                static_cast<long long>(microseconds));
+  L->ea.wait_ns = static_cast<unsigned long long>(microseconds) * 1000ull;
   return MM_OK;
 }
 
@@ -627,7 +661,54 @@ int mm_layer_experts(mm_layer *L, const uint16_t *x, const int32_t *ids, int32_t
 int mm_layer_gate_experts(mm_layer *L, const uint16_t *x, const mm_gate_args *gate, int32_t tokens,
                           int32_t *permuted, int32_t *record, uint16_t *rows, void *stream) {
   if (!L || !gate) return fail(MM_ERR_INVALID, "null layer or gate arguments");
+  if (!x) return fail(MM_ERR_INVALID, "mm_layer_gate_experts: null x");
   return run_front_and_experts(L, x, gate, nullptr, tokens, permuted, record, rows, stream);
+}
+
+int mm_layer_experts_mxfp8(mm_layer *L, const uint8_t *x_quant, const uint8_t *x_scale, const int32_t *ids,
+                           int32_t tokens, int32_t *permuted, int32_t *record, uint16_t *rows, void *stream) {
+  if (!L) return fail(MM_ERR_INVALID, "null layer");
+  if (!x_quant || !x_scale) return fail(MM_ERR_INVALID, "mm_layer_experts_mxfp8: null x_quant or x_scale");
+  return run_front_and_experts(L, nullptr, nullptr, ids, tokens, permuted, record, rows, stream, false, x_quant,
+                               x_scale);
+}
+
+int mm_layer_gate_experts_mxfp8(mm_layer *L, const uint8_t *x_quant, const uint8_t *x_scale,
+                                const mm_gate_args *gate, int32_t tokens, int32_t *permuted, int32_t *record,
+                                uint16_t *rows, void *stream) {
+  if (!L || !gate) return fail(MM_ERR_INVALID, "null layer or gate arguments");
+  if (!x_quant || !x_scale) return fail(MM_ERR_INVALID, "mm_layer_gate_experts_mxfp8: null x_quant or x_scale");
+  return run_front_and_experts(L, nullptr, gate, nullptr, tokens, permuted, record, rows, stream, false, x_quant,
+                               x_scale);
+}
+
+int64_t mm_layer_scratch_bytes(const mm_layer *L, int32_t which) {
+  if (!L) return -1;
+  const int64_t terms = kMaxTerms;
+  switch (which) {
+    case MM_SCRATCH_X_CODES: return terms * L->Tmax * (L->H / 2);
+    case MM_SCRATCH_X_SCALES: return terms * L->Tmax * (L->H / L->block);
+    case MM_SCRATCH_H_CODES: return terms * L->rows_cap * static_cast<int64_t>(L->ea.hq_row);
+    case MM_SCRATCH_H_SCALES: return terms * L->rows_cap * static_cast<int64_t>(L->ea.hs_row);
+    default: return -1;
+  }
+}
+
+int mm_layer_read_scratch(const mm_layer *L, int32_t which, void *dst, int64_t bytes, void *stream) {
+  if (!L || !dst) return fail(MM_ERR_INVALID, "mm_layer_read_scratch: null pointer");
+  const int64_t size = mm_layer_scratch_bytes(L, which);
+  if (size < 0) return fail(MM_ERR_INVALID, "mm_layer_read_scratch: unknown buffer %d", which);
+  if (bytes != size)
+    return fail(MM_ERR_INVALID, "mm_layer_read_scratch: buffer %d holds %lld bytes, not %lld", which,
+                static_cast<long long>(size), static_cast<long long>(bytes));
+  const void *src = which == MM_SCRATCH_X_CODES ? static_cast<const void *>(L->xq)
+                    : which == MM_SCRATCH_X_SCALES ? static_cast<const void *>(L->xs)
+                    : which == MM_SCRATCH_H_CODES ? static_cast<const void *>(L->hq)
+                                                  : static_cast<const void *>(L->hs);
+  MM_CUDA(cudaSetDevice(L->d.device));
+  MM_CUDA(cudaMemcpyAsync(dst, src, static_cast<size_t>(bytes), cudaMemcpyDeviceToDevice,
+                          static_cast<cudaStream_t>(stream)));
+  return MM_OK;
 }
 
 int mm_layer_forward(mm_layer *L, const mm_forward_args *a, void *stream) {

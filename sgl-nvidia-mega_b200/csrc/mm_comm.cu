@@ -53,6 +53,7 @@ struct CommArgs {
   const uint16_t *residual, *gamma;
   uint16_t *residual_out, *norm_out;
   float eps;
+  unsigned long long wait_ns;  // budget of the mailbox poll (mm_comm_set_wait_budget)
 };
 
 namespace {
@@ -163,7 +164,7 @@ __device__ __forceinline__ void combine_exchange(const CommArgs &c, int t, int h
     uint4 v = ld_volatile_v4(src);
 #pragma unroll 1
     for (uint32_t i = 0; has_empty(v.x) || has_empty(v.y) || has_empty(v.z) || has_empty(v.w); ++i) {
-      if ((i & 31u) == 31u && (error_set(c.err) || globaltimer() - t0 > kWaitBudgetNs)) {
+      if ((i & 31u) == 31u && (error_set(c.err) || globaltimer() - t0 > c.wait_ns)) {
         error_raise(c.err, kErrTimeoutFlag);
         break;
       }
@@ -287,6 +288,8 @@ using namespace mm;
 
 struct mm_comm {
   int rank, world, max_tokens, hidden, device, max_blocks;
+  unsigned long long wait_ns = kWaitBudgetNs;
+  bool ipc_opened = false;  // the peers' buffers are CUDA IPC mappings (closed at destroy)
   char *base = nullptr;
   size_t bytes = 0, off_counters = 0, off_err = 0, off_mbox = 0;
   char *peer[kMaxWorld] = {};
@@ -327,6 +330,7 @@ static int launch_comm(mm_comm *c, const char *what, const uint16_t *rows, const
   a.residual_out = residual_out;
   a.norm_out = norm_out;
   a.eps = eps;
+  a.wait_ns = c->wait_ns;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(tokens, ctas);
   cfg.blockDim = dim3(256);
@@ -423,9 +427,52 @@ int mm_comm_open(mm_comm *c, const void *handles) {
     }
     c->peer[q] = static_cast<char *>(p);
   }
+  c->ipc_opened = true;
   e = cudaMemcpy(c->peer_table, c->peer, sizeof(char *) * c->world, cudaMemcpyHostToDevice);
   if (e != cudaSuccess) return set_error(MM_ERR_CUDA, "mm_comm_open: %s", cudaGetErrorString(e));
   c->opened = true;
+  return MM_OK;
+}
+
+int mm_comm_open_local(mm_comm *c, mm_comm *const *members) {
+  if (!c || !members) return set_error(MM_ERR_INVALID, "mm_comm_open_local: null pointer");
+  if (c->opened) return set_error(MM_ERR_INVALID, "mm_comm_open_local: already open");
+  for (int q = 0; q < c->world; ++q) {
+    const mm_comm *m = members[q];
+    if (!m || m->rank != q || m->world != c->world || m->max_tokens != c->max_tokens || m->hidden != c->hidden)
+      return set_error(MM_ERR_INVALID, "mm_comm_open_local: member %d does not belong to this group", q);
+    if (q == c->rank && m != c) return set_error(MM_ERR_INVALID, "mm_comm_open_local: member %d is not this comm", q);
+  }
+  cudaError_t e = cudaSetDevice(c->device);
+  for (int q = 0; q < c->world && e == cudaSuccess; ++q) {
+    const int dev = members[q]->device;
+    if (dev == c->device) continue;
+    int can = 0;
+    e = cudaDeviceCanAccessPeer(&can, c->device, dev);
+    if (e == cudaSuccess && !can)
+      return set_error(MM_ERR_UNSUPPORTED, "mm_comm_open_local: device %d cannot reach device %d", c->device, dev);
+    if (e == cudaSuccess) {
+      e = cudaDeviceEnablePeerAccess(dev, 0);
+      if (e == cudaErrorPeerAccessAlreadyEnabled) {
+        cudaGetLastError();
+        e = cudaSuccess;
+      }
+    }
+  }
+  if (e != cudaSuccess) return set_error(MM_ERR_CUDA, "mm_comm_open_local: %s", cudaGetErrorString(e));
+  for (int q = 0; q < c->world; ++q) c->peer[q] = members[q]->base;
+  e = cudaMemcpy(c->peer_table, c->peer, sizeof(char *) * c->world, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return set_error(MM_ERR_CUDA, "mm_comm_open_local: %s", cudaGetErrorString(e));
+  c->opened = true;
+  return MM_OK;
+}
+
+int mm_comm_set_wait_budget(mm_comm *c, int64_t microseconds) {
+  if (!c) return set_error(MM_ERR_INVALID, "mm_comm_set_wait_budget: null comm");
+  if (microseconds < 1 || microseconds > 60000000)
+    return set_error(MM_ERR_INVALID, "mm_comm_set_wait_budget: %lld us outside 1..60000000",
+                     static_cast<long long>(microseconds));
+  c->wait_ns = static_cast<unsigned long long>(microseconds) * 1000ull;
   return MM_OK;
 }
 
@@ -434,7 +481,7 @@ int mm_comm_destroy(mm_comm *c) {
   cudaSetDevice(c->device);
   cudaDeviceSynchronize();
   for (int q = 0; q < c->world; ++q)
-    if (q != c->rank && c->peer[q]) cudaIpcCloseMemHandle(c->peer[q]);
+    if (c->ipc_opened && q != c->rank && c->peer[q]) cudaIpcCloseMemHandle(c->peer[q]);
   if (c->peer_table) cudaFree(c->peer_table);
   if (c->base) cudaFree(c->base);
   delete c;

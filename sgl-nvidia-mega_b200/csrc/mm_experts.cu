@@ -86,8 +86,9 @@ struct SegCache {
   }
 };
 
-// Wait until `flag` >= target; false (and the error word set) on timeout.
-__device__ bool wait_flag(const int *flag, int target, uint32_t *err) {
+// Wait until `flag` >= target; false (and the error word set) when `budget_ns`
+// runs out or another wait of the launch already failed.
+__device__ bool wait_flag(const int *flag, int target, uint32_t *err, uint64_t budget_ns) {
   if (ld_acquire(flag) >= target) return true;
   const uint64_t t0 = globaltimer();
 #pragma unroll 1
@@ -96,7 +97,7 @@ __device__ bool wait_flag(const int *flag, int target, uint32_t *err) {
     if (ld_acquire(flag) >= target) return true;
     if ((i & 15u) == 0u) {
       if (error_set(err)) return false;
-      if (globaltimer() - t0 > kWaitBudgetNs) {
+      if (globaltimer() - t0 > budget_ns) {
         error_raise(err, kErrTimeoutFlag);
         return false;
       }
@@ -172,6 +173,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
   int *work_ids = reinterpret_cast<int *>(sbase + L::kSmemWorkIds);
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sbase + L::kSmemTmemBase);
   uint32_t *err = p.err;
+  const uint64_t wb = p.wait_ns;  // budget of every bounded wait below
 
   pdl_launch_dependents();
 
@@ -243,7 +245,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
         const int u = cur;
         const bool have = u < total;
         cur = total;
-        if (!mbar_wait(bar(kBarWorkEmpty + ws), wphase ^ 1u, err, kErrTimeoutWork)) break;
+        if (!mbar_wait(bar(kBarWorkEmpty + ws), wphase ^ 1u, err, kErrTimeoutWork, wb)) break;
         work_ids[ws] = have ? u : -1;
         mbar_arrive(bar(kBarWorkFull + ws));
         if (++ws == kWorkSlots) { ws = 0; wphase ^= 1u; }
@@ -273,7 +275,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
             b_end = b_next + batch;
             b_claimed = true;
           }
-          if (!mbar_wait(bar(kBarEmpty + stage), phase ^ 1u, err, kErrTimeoutEmpty)) {
+          if (!mbar_wait(bar(kBarEmpty + stage), phase ^ 1u, err, kErrTimeoutEmpty, wb)) {
             ok = false;
             break;
           }
@@ -301,7 +303,9 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
         if (a_next < a_end) cur = a_next++;
       }
       // drain: the copies of the last ring's fills have landed (their full
-      // barriers completed), so no copy is in flight when the CTA exits
+      // barriers completed), so no copy is in flight when the CTA exits. After a
+      // failed wait too (the drain ignores the error word, with its own limit:
+      // a stage whose activation rows never arrived waits out the limit)
       for (int i = 0; i < kStages && i < filled; ++i) {
         if (stage == 0) {
           stage = kStages - 1;
@@ -309,7 +313,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
         } else {
           --stage;
         }
-        mbar_wait(bar(kBarFull + stage), phase, err, kErrTimeoutFull);
+        mbar_wait_drain(bar(kBarFull + stage), phase);
       }
     }
   } else if (warp == 1) {
@@ -326,7 +330,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
       SegCache seg_cache;
 #pragma unroll 1
       while (true) {
-        if (!mbar_wait(bar(kBarWorkFull + ws), wphase, err, kErrTimeoutWork)) break;
+        if (!mbar_wait(bar(kBarWorkFull + ws), wphase, err, kErrTimeoutWork, wb)) break;
         const int u = ld_shared_volatile(work_ids + ws);
         mbar_arrive(bar(kBarWorkEmpty + ws));
         if (++ws == kWorkSlots) { ws = 0; wphase ^= 1u; }
@@ -341,7 +345,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
         const uint32_t id2 = id0 | (2u << 4) | (2u << 29);  // MXFP4: the chunk's second byte pair
         const int ks_u = g2 ? p.ks2 : p.ks1;
         const int ks_n = (g2 ? (kTg2 == 1 ? 1 : min(kTg2, p.m2 - m * kTg2)) : 1) * ks_u;
-        if (!mbar_wait(bar(kBarAccEmpty + acc), acc_phase ^ 1u, err, kErrTimeoutAcc)) break;
+        if (!mbar_wait(bar(kBarAccEmpty + acc), acc_phase ^ 1u, err, kErrTimeoutAcc, wb)) break;
         tc_fence_after();
         // accumulator buffers tg2 x kBRows columns apart (single-tile layers keep them adjacent)
         const uint32_t acc_tmem = tbase + L::kTmemAcc + acc * static_cast<uint32_t>(kTg2 * kBRows);
@@ -350,7 +354,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
         int kq = 0;                  // K stage within the tile
 #pragma unroll 1
         for (int ks = 0; ks < ks_n; ++ks) {
-          if (!mbar_wait(bar(kBarFull + stage), phase, err, kErrTimeoutFull)) {
+          if (!mbar_wait(bar(kBarFull + stage), phase, err, kErrTimeoutFull, wb)) {
             ok = false;
             break;
           }
@@ -386,9 +390,10 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
         tc_commit(bar(kBarAccFull + acc));
         if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
       }
-      // every tcgen05 operation issued above has completed before teardown
+      // every tcgen05 operation issued above has completed before teardown (also
+      // after a failed wait: the drain ignores the error word)
       tc_commit(bar(kBarDrain));
-      mbar_wait(bar(kBarDrain), 0, err, kErrTimeoutAcc);
+      mbar_wait_drain(bar(kBarDrain), 0);
     }
   } else if (warp == 2) {
     // ============================ B loader ===================================
@@ -418,7 +423,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
     while (true) {
       int u = -1, okw = 1;
       if (lane == 0) {
-        okw = mbar_wait(bar(kBarWorkFull + ws), wphase, err, kErrTimeoutWork) ? 1 : 0;
+        okw = mbar_wait(bar(kBarWorkFull + ws), wphase, err, kErrTimeoutWork, wb) ? 1 : 0;
         if (okw) {
           u = ld_shared_volatile(work_ids + ws);
           mbar_arrive(bar(kBarWorkEmpty + ws));
@@ -433,7 +438,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
       decode_unit(u, nseg, p.m1, p.u2, g2, seg, m);
       if (g2 && seg != ready_seg) {  // once complete, a mailbox stays complete in this launch
         int okf = 1;
-        if (lane == 0) okf = wait_flag(p.flags + seg, 2 * p.m1, err) ? 1 : 0;
+        if (lane == 0) okf = wait_flag(p.flags + seg, 2 * p.m1, err, wb) ? 1 : 0;
         okf = __shfl_sync(0xffffffffu, okf, 0);
         if (!okf) break;
         ready_seg = seg;
@@ -487,7 +492,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
 #pragma unroll 1
       for (int ks = 0, kq = 0; ks < ks_n; ++ks, kq = (kq + 1 == ks_u) ? 0 : kq + 1) {
         int oke = 1;
-        if (lane == 0) oke = mbar_wait(bar(kBarEmpty + stage), phase ^ 1u, err, kErrTimeoutEmpty) ? 1 : 0;
+        if (lane == 0) oke = mbar_wait(bar(kBarEmpty + stage), phase ^ 1u, err, kErrTimeoutEmpty, wb) ? 1 : 0;
         oke = __shfl_sync(0xffffffffu, oke, 0);
         if (!oke) break;
         const uint32_t sb = base + L::kSmemB + stage * kBStageBytes;
@@ -527,7 +532,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
     while (true) {
       int u = -1, okw = 1;
       if (lane == 0) {
-        okw = mbar_wait(bar(kBarWorkFull + ws), wphase, err, kErrTimeoutWork) ? 1 : 0;
+        okw = mbar_wait(bar(kBarWorkFull + ws), wphase, err, kErrTimeoutWork, wb) ? 1 : 0;
         if (okw) {
           u = ld_shared_volatile(work_ids + ws);
           mbar_arrive(bar(kBarWorkEmpty + ws));
@@ -544,7 +549,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
       const int rows = sg.z;
       const int n = (rows + 7) & ~7;
       int ok = 1;
-      if (lane == 0) ok = mbar_wait(bar(kBarAccFull + acc), acc_phase, err, kErrTimeoutAcc) ? 1 : 0;
+      if (lane == 0) ok = mbar_wait(bar(kBarAccFull + acc), acc_phase, err, kErrTimeoutAcc, wb) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       tc_fence_after();
@@ -582,7 +587,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
         if (!g2) {
           // rows 0..63: gate of features 64m + row; rows 64..127: up of the same features
           if (q >= 2) {
-            if (lane == 0) ok = mbar_wait(bar(kBarExFree), ex_phase ^ 1u, err, kErrTimeoutAcc) ? 1 : 0;
+            if (lane == 0) ok = mbar_wait(bar(kBarExFree), ex_phase ^ 1u, err, kErrTimeoutAcc, wb) ? 1 : 0;
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
 #pragma unroll
@@ -590,7 +595,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(kBarExFull));
           } else {
-            if (lane == 0) ok = mbar_wait(bar(kBarExFull), ex_phase, err, kErrTimeoutAcc) ? 1 : 0;
+            if (lane == 0) ok = mbar_wait(bar(kBarExFull), ex_phase, err, kErrTimeoutAcc, wb) ? 1 : 0;
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
             float upv[kSegRows];

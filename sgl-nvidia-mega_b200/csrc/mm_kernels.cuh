@@ -50,7 +50,9 @@ constexpr int kMaxRouterParts = 14;  // H <= 14336 for the router GEMV (x tile i
 constexpr int kMaxRouterHidden = 1024 * kMaxRouterParts;
 
 struct RouterArgs {
-  const uint16_t *x;         // bf16 [T, H]
+  const uint16_t *x;         // bf16 [T, H] (GEMV input; quantized unless x8 is set)
+  const uint8_t *x8;         // or MXFP8 [T, H] E4M3 codes (quantization only), with
+  const uint8_t *s8;         //    [T, H/32] E8M0 block scales
   const uint16_t *w;         // bf16 [E, H] (null when gemv_ctas == 0)
   float *logits;             // [T, E]
   int tokens, experts, hidden;
@@ -95,6 +97,7 @@ struct alignas(64) ExpertArgs {
   int hq_row, hs_row;        // bytes per h row / h scale row: I rounded up to 256 features, zero past I
   int m1, m2, ks1, ks2;      // gate_up units / down tiles per segment; K stages of each
   int tg2, u2;               // down tiles per down unit; down units per segment (ceil(m2 / tg2))
+  unsigned long long wait_ns;  // budget of every bounded wait (mm_layer_set_wait_budget)
 };
 
 struct FinalizeArgs {

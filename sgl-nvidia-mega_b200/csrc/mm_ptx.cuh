@@ -20,8 +20,14 @@ constexpr uint32_t kErrTimeoutFlag = 1u << 4;    // gate_up segment never finish
 constexpr uint32_t kErrBadUnit = 1u << 8;        // a work item failed its checks
 constexpr uint32_t kErrTimeoutMask = 0xffu;
 
-// 1.5 s: far above any legitimate wait of one launch, far below any watchdog.
+// The default budget of one bounded wait, 1.5 s: far above any legitimate wait
+// of one launch, far below any watchdog. Layers and comms carry their own budget
+// (mm_layer_set_wait_budget / mm_comm_set_wait_budget), passed to every wait.
 constexpr uint64_t kWaitBudgetNs = 1500000000ull;
+// The limit of a teardown drain (copies and MMAs this CTA issued, which complete
+// in microseconds); a drain ignores the error word, so a launch that gave up
+// still lets its own in-flight work land before it frees shared memory and TMEM.
+constexpr uint64_t kDrainBudgetNs = 20000000ull;
 
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
@@ -78,9 +84,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0u;
 }
 // Wait for the phase with this parity to complete; false (and the error word
-// set) when the budget runs out or another wait of the launch already failed.
+// set) when `budget_ns` runs out or another wait of the launch already failed.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t *err,
-                                          uint32_t code) {
+                                          uint32_t code, uint64_t budget_ns = kWaitBudgetNs) {
 #pragma unroll 1
   for (int i = 0; i < 256; ++i)
     if (mbar_try_wait(bar, parity)) return true;
@@ -90,11 +96,21 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 63u) == 0u) {
       if (error_set(err)) return false;
-      if (globaltimer() - t0 > kWaitBudgetNs) {
+      if (globaltimer() - t0 > budget_ns) {
         error_raise(err, code);
         return false;
       }
     }
+  }
+}
+// A teardown drain: wait for the phase regardless of the error word, at most
+// kDrainBudgetNs; false when the limit ran out.
+__device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer();
+#pragma unroll 1
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63u) == 0u && globaltimer() - t0 > kDrainBudgetNs) return false;
   }
 }
 

@@ -38,7 +38,8 @@ namespace mm {
 //
 // CTAs [gemv_ctas, ...) (blockIdx.y == 0): the FP4 terms of x, one 32-element
 // chunk of one token per thread (one MXFP4 block or two NVFP4 blocks;
-// independent of the routing).
+// independent of the routing). x is bf16, or MXFP8 (x8 / s8: E4M3 codes and an
+// E8M0 scale per 32, the reference's pre-quantized routed input).
 // ============================================================================
 __global__ void __launch_bounds__(256) router_quant_kernel(RouterArgs a) {
   pdl_launch_dependents();
@@ -50,16 +51,31 @@ __global__ void __launch_bounds__(256) router_quant_kernel(RouterArgs a) {
     const int idx = (blockIdx.x - a.gemv_ctas) * blockDim.x + threadIdx.x;
     if (idx >= a.tokens * blocks) return;
     const int t = idx / blocks, b = idx - t * blocks;
-    const uint4 *src = reinterpret_cast<const uint4 *>(a.x + static_cast<size_t>(t) * a.hidden + 32 * b);
     float v[32];
+    if (a.x8 != nullptr) {
+      // MXFP8 input (the reference's x_quant / x_scale): the exact value of each
+      // E4M3 code times the block's E8M0 scale, one fp32 rounding (subnormals kept)
+      const uint4 *src = reinterpret_cast<const uint4 *>(a.x8 + static_cast<size_t>(t) * a.hidden + 32 * b);
+      const float sv = mx_scale_value(a.s8[static_cast<size_t>(t) * blocks + b]);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint4 u = src[i];
-      const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+      for (int i = 0; i < 2; ++i) {
+        const uint4 u = src[i];
+        const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        v[8 * i + 2 * j] = __uint_as_float(w4[j] << 16);
-        v[8 * i + 2 * j + 1] = __uint_as_float(w4[j] & 0xffff0000u);
+        for (int j = 0; j < 16; ++j)
+          v[16 * i + j] = __fmul_rn(e4m3_value(static_cast<uint8_t>(w4[j >> 2] >> (8 * (j & 3)))), sv);
+      }
+    } else {
+      const uint4 *src = reinterpret_cast<const uint4 *>(a.x + static_cast<size_t>(t) * a.hidden + 32 * b);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint4 u = src[i];
+        const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          v[8 * i + 2 * j] = __uint_as_float(w4[j] << 16);
+          v[8 * i + 2 * j + 1] = __uint_as_float(w4[j] & 0xffff0000u);
+        }
       }
     }
     const size_t q_stride = static_cast<size_t>(a.max_tokens) * (a.hidden >> 1);
@@ -289,7 +305,23 @@ __device__ void gate_row(const GateArgs &g, int row, int valid_rows, GateSmem &s
           w[k] = sm.score[sm.sel[k]];
           sum = __fadd_rn(sum, w[k]);
         }
-        if (g.renormalize) {
+        if (g.renormalize == 2) {
+          // GLM-5.3's rule (glm5_3/sm103/moe/routing.py:3-11, ptx_tc.py routing_weight):
+          // the selected scores summed in the order of a warp xor-butterfly whose
+          // lane k holds slot k (the halving [i] += [i + off], off = 8, 4, 2, 1, is
+          // lane 0's order), then w = bf16(scale * s / (sum + eps)), scale first;
+          // IEEE division where the reference divides approximately
+          float t[kMaxTopK];
+#pragma unroll
+          for (int k = 0; k < kMaxTopK; ++k) t[k] = k < K ? w[k] : 0.0f;
+#pragma unroll
+          for (int off = kMaxTopK / 2; off >= 1; off >>= 1)
+#pragma unroll
+            for (int i = 0; i < off; ++i) t[i] = __fadd_rn(t[i], t[i + off]);
+          const float d = __fadd_rn(t[0], g.renorm_eps);
+          for (int k = 0; k < K; ++k)
+            w[k] = bf16_bits_to_float(float_to_bf16_bits(__fdiv_rn(__fmul_rn(g.routed_scaling, w[k]), d)));
+        } else if (g.renormalize) {
           const float norm = g.renorm_eps > 0.0f ? __fadd_rn(sum, g.renorm_eps)
                                                  : (sum > 0.0f ? sum : 1.0f);
           for (int k = 0; k < K; ++k) w[k] = __fmul_rn(__fdiv_rn(w[k], norm), g.routed_scaling);
@@ -539,8 +571,11 @@ std::mutex g_noalloc_mutex;
 int *g_noalloc_ptr[kNoAllocMaxDevices] = {};
 
 // Once per device, with that device current: the device address of the scratch
-// array (in host code its name is only a stand-in), its ticket cleared, and the
-// kernel's shared-memory limit raised. Runs on the first call on a device.
+// array (in host code its name is only a stand-in) and the kernel's shared-memory
+// limit raised. Runs on the first call on a device. The ticket needs no clearing
+// here: a static device array is zero when the module loads, and every launch
+// re-arms the ticket before it ends (a memset here would also be unordered with
+// a launch on a non-blocking stream).
 int noalloc_setup(int device, int **out) {
   std::lock_guard<std::mutex> lock(g_noalloc_mutex);
   if (g_noalloc_ptr[device] == nullptr) {
@@ -548,10 +583,8 @@ int noalloc_setup(int device, int **out) {
     cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void **>(&ptr), g_noalloc_scratch);
     if (e != cudaSuccess)
       return set_error(MM_ERR_CUDA, "mm_gate_route_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
-    e = cudaMemset(ptr, 0, sizeof(int) * kNoAllocIdsWord);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(gate_route_noalloc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(route_smem_size(kMaxTokens, kMaxRouterExperts)));
+    e = cudaFuncSetAttribute(gate_route_noalloc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(route_smem_size(kMaxTokens, kMaxRouterExperts)));
     if (e != cudaSuccess)
       return set_error(MM_ERR_CUDA, "mm_gate_route_noalloc: set-up failed: %s", cudaGetErrorString(e));
     g_noalloc_ptr[device] = ptr;
@@ -583,6 +616,10 @@ extern "C" int mm_gate_route_noalloc(const mm_gate_args *gate, int32_t tokens, i
   if (gate->score_func != MM_SCORE_SIGMOID && gate->score_func != MM_SCORE_SOFTMAX &&
       gate->score_func != MM_SCORE_SQRTSOFTPLUS)
     return set_error(MM_ERR_UNSUPPORTED, "mm_gate_route_noalloc: score function %d is not built", gate->score_func);
+  if (gate->renormalize < 0 || gate->renormalize > MM_RENORM_SCALED_BF16 ||
+      (gate->renormalize == MM_RENORM_SCALED_BF16 && gate->score_func == MM_SCORE_SOFTMAX))
+    return set_error(MM_ERR_INVALID, "mm_gate_route_noalloc: renormalize %d with score function %d",
+                     gate->renormalize, gate->score_func);
   int device = 0;
   cudaError_t e = cudaGetDevice(&device);
   if (e != cudaSuccess || device < 0 || device >= kNoAllocMaxDevices)

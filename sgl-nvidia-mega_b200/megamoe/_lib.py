@@ -27,8 +27,28 @@ MM_SCORE_SOFTMAX = 1
 MM_SCORE_SQRTSOFTPLUS = 2
 SCORES = {"sigmoid": MM_SCORE_SIGMOID, "softmax": MM_SCORE_SOFTMAX, "sqrtsoftplus": MM_SCORE_SQRTSOFTPLUS}
 
+MM_RENORM_NONE = 0
+MM_RENORM_SUM = 1
+MM_RENORM_SCALED_BF16 = 2
+# renormalize= of the Python API: a bool (sum rule or none) or one of these names
+RENORMS = {"none": MM_RENORM_NONE, "sum": MM_RENORM_SUM, "scaled_bf16": MM_RENORM_SCALED_BF16}
+
 MM_WEIGHT_MXFP4 = 0
 MM_WEIGHT_NVFP4 = 1
+
+MM_SCRATCH_X_CODES = 0
+MM_SCRATCH_X_SCALES = 1
+MM_SCRATCH_H_CODES = 2
+MM_SCRATCH_H_SCALES = 3
+
+
+def renorm_code(renormalize) -> int:
+    """The C routing weight rule of a Python ``renormalize`` argument."""
+    if isinstance(renormalize, str):
+        if renormalize not in RENORMS:
+            raise ValueError(f"renormalize {renormalize!r}: True, False or one of {sorted(RENORMS)}")
+        return RENORMS[renormalize]
+    return MM_RENORM_SUM if renormalize else MM_RENORM_NONE
 
 
 class MMExpertWeights(ctypes.Structure):
@@ -88,6 +108,9 @@ class MMLayerInfo(ctypes.Structure):
         ("shared_row_base", c_int64),
         ("route_words", c_int64),
         ("weight_bytes", c_int64),
+        ("act_terms", c_int32),
+        ("h_row_bytes", c_int32),
+        ("h_scale_row_bytes", c_int64),
     ]
 
 
@@ -155,16 +178,30 @@ SIGNATURES = {
         c_int32,
         [c_void_p, c_void_p, POINTER(MMGateArgs), c_int32, c_void_p, c_void_p, c_void_p, c_void_p],
     ),
+    "mm_layer_experts_mxfp8": (
+        c_int32,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_void_p, c_void_p, c_void_p, c_void_p],
+    ),
+    "mm_layer_gate_experts_mxfp8": (
+        c_int32,
+        [c_void_p, c_void_p, c_void_p, POINTER(MMGateArgs), c_int32, c_void_p, c_void_p, c_void_p, c_void_p],
+    ),
+    "mm_layer_scratch_bytes": (c_int64, [c_void_p, c_int32]),
+    "mm_layer_read_scratch": (c_int32, [c_void_p, c_int32, c_void_p, c_int64, c_void_p]),
     "mm_layer_rerun_experts": (c_int32, [c_void_p, c_int32, c_void_p, c_void_p, c_void_p]),
     "mm_layer_rearm_experts": (c_int32, [c_void_p, c_void_p]),
+    "mm_layer_block_downs": (c_int32, [c_void_p, c_void_p]),
+    "mm_layer_set_wait_budget": (c_int32, [c_void_p, c_int64]),
     "mm_layer_forward": (c_int32, [c_void_p, POINTER(MMForwardArgs), c_void_p]),
     "mm_layer_check": (c_int32, [c_void_p]),
     "mm_stack_forward": (c_int32, [POINTER(MMStackLayer), c_int32, c_void_p]),
     "mm_comm_create": (c_int32, [c_int32, c_int32, c_int32, c_int32, c_int32, POINTER(c_void_p)]),
     "mm_comm_handle": (c_int32, [c_void_p, c_void_p]),
     "mm_comm_open": (c_int32, [c_void_p, c_void_p]),
+    "mm_comm_open_local": (c_int32, [c_void_p, POINTER(c_void_p)]),
     "mm_comm_destroy": (c_int32, [c_void_p]),
     "mm_comm_check": (c_int32, [c_void_p]),
+    "mm_comm_set_wait_budget": (c_int32, [c_void_p, c_int64]),
     "mm_finalize_allreduce_norm": (
         c_int32,
         [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_void_p,
@@ -197,12 +234,20 @@ def lib() -> ctypes.CDLL:
     return _lib
 
 
+class DeviceTimeoutError(RuntimeError):
+    """A bounded device wait gave up (MM_ERR_DEVICE_TIMEOUT): a producer, a peer
+    or a mailbox never arrived within the wait budget."""
+
+
 def check(rc: int, what: str) -> None:
     """Map a status code to the reference's exception types (ValueError for
-    shape/argument violations, RuntimeError for device/driver failures)."""
+    shape/argument violations, RuntimeError for device/driver failures;
+    DeviceTimeoutError, a RuntimeError, for a bounded wait that gave up)."""
     if rc == MM_OK:
         return
     msg = lib().mm_last_error().decode(errors="replace")
     if rc in (MM_ERR_INVALID, MM_ERR_UNSUPPORTED):
         raise ValueError(f"{what}: {msg}")
+    if rc == MM_ERR_DEVICE_TIMEOUT:
+        raise DeviceTimeoutError(f"{what}: {msg} (status {rc})")
     raise RuntimeError(f"{what}: {msg} (status {rc})")

@@ -64,6 +64,40 @@ class PeerAllReduce:
             self.handle = None
             raise
 
+    @classmethod
+    def local_group(cls, max_tokens: int, hidden: int, devices, eps: float = 1e-6) -> list:
+        """Every member of a group driven by this one process: rank q on
+        ``devices[q]`` (devices may repeat). Each member reaches the others'
+        buffers directly (peer access between distinct devices), with no IPC
+        and no process group. Returns the members in rank order."""
+        world = len(devices)
+        members = []
+        try:
+            for q, dev in enumerate(devices):
+                m = cls.__new__(cls)
+                m.rank, m.world = q, world
+                m.max_tokens, m.hidden, m.eps = int(max_tokens), int(hidden), float(eps)
+                m.device = torch.device(dev)
+                m.handle = None
+                h = ctypes.c_void_p()
+                check(lib().mm_comm_create(q, world, m.max_tokens, m.hidden, m.device.index, ctypes.byref(h)),
+                      "mm_comm_create")
+                m.handle = h.value
+                members.append(m)
+            table = (ctypes.c_void_p * world)(*(m.handle for m in members))
+            for m in members:
+                check(lib().mm_comm_open_local(m.handle, table), "mm_comm_open_local")
+        except BaseException:
+            for m in members:
+                m.close()
+            raise
+        return members
+
+    def set_wait_budget(self, microseconds: int) -> None:
+        """Budget of this rank's mailbox polls (default 1.5 s); a poll that runs
+        out ends the launch and makes ``check`` raise DeviceTimeoutError."""
+        check(lib().mm_comm_set_wait_budget(self.handle, int(microseconds)), "mm_comm_set_wait_budget")
+
     def _check(self, rows, weights, permuted, shared_output):
         if self.handle is None:
             raise RuntimeError("PeerAllReduce is closed")

@@ -5,17 +5,23 @@ RoutedMoE keeps the shape of sgl-nvidia-mega's RoutedExpertGemm
 finalize that consumes its output (deepseek_v41/sm103/all_reduce_mhc.py:1484,
 glm5_3/sm103/moe/finalize.py):
 
-  * ``__call__(x, topk_ids, topk_weights)`` -> the deferred-finalize triple
-    (gemm2 rows, weights, slot -> row), like RoutedExpertGemm.__call__;
-  * ``gate_topk_and_gemms(x, logits, bias, routed_scaling_factor, num_valid, ...)``
-    -> (rows, weights, permuted, ids), like RoutedExpertGemm.gate_topk_and_gemms;
+  * ``__call__(x_quant, x_scale, topk_ids, topk_weights)`` -> the
+    deferred-finalize triple (gemm2 rows, weights, slot -> row), positionally
+    like RoutedExpertGemm.__call__ (routed_expert_gemm.py:703);
+  * ``gate_topk_and_gemms(x_quant, x_scale, logits, bias, routed_scaling_factor,
+    num_valid, alt=None, renormalize_epsilon=0.0, ids_out=None, x=None,
+    early=False)`` -> (rows, weights, permuted, ids), like
+    RoutedExpertGemm.gate_topk_and_gemms (:776);
   * ``finalize(rows, weights, permuted)`` -> the combined bf16 MoE output;
   * ``forward(x, router_weight=..., bias=...)`` -> one whole MoE step.
 
-Differences from the reference's interface: the routed input is passed as bf16
-(the chain quantizes it itself, as gate_route_quant does), weights are the
-canonical MXFP4 layout (not FlashInfer-shuffled), and errors raise ValueError
-(shape/argument) or RuntimeError (device), as the reference's do.
+The routed input is MXFP8 (x_quant E4M3 codes [T, H], x_scale E8M0 [T, H/32],
+as SGLang's quantize_routed_input hands it to the reference) or bf16 (x_quant a
+bf16 [T, H] tensor with x_scale None, or ``x=`` in gate_topk_and_gemms: the
+chain quantizes it itself, as the reference's gate_route_quant slot does).
+Weights are the canonical layout (FlashInfer-shuffled ones go through
+``from_trtllm``); errors raise ValueError (shape/argument) or RuntimeError
+(device), as the reference's do.
 """
 
 from __future__ import annotations
@@ -203,6 +209,18 @@ class RoutedMoE:
             self._handle = None
 
     # ------------------------------------------------------------------ helpers
+    def _check_xq(self, x_quant: torch.Tensor, x_scale: torch.Tensor) -> int:
+        """Rows of an MXFP8 routed input (E4M3 codes [T, H], E8M0 scales [T, H/32])."""
+        for name, t, cols in (("x_quant", x_quant, self.hidden), ("x_scale", x_scale, self.hidden // 32)):
+            if t.element_size() != 1 or t.dim() != 2 or t.size(1) != cols or not t.is_contiguous() \
+                    or t.device != self.device:
+                raise ValueError(f"{name}: expected a contiguous 1-byte [T, {cols}] tensor on {self.device}, "
+                                 f"got {tuple(t.shape)} {t.dtype}")
+        rows = x_quant.size(0)
+        if x_scale.size(0) != rows or not 1 <= rows <= self.max_rows:
+            raise ValueError(f"x_quant / x_scale: {rows} / {x_scale.size(0)} rows (1..{self.max_rows})")
+        return rows
+
     def _check_x(self, x: torch.Tensor) -> int:
         if x.dtype != torch.bfloat16 or x.dim() != 2 or x.size(1) != self.hidden or not x.is_contiguous():
             raise ValueError(f"x: expected a contiguous bf16 [T, {self.hidden}] tensor, got {tuple(x.shape)} {x.dtype}")
@@ -225,44 +243,68 @@ class RoutedMoE:
         return rows[self.shared_row_base : self.shared_row_base + tokens]
 
     # ------------------------------------------------------------------ API
-    def __call__(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: Optional[torch.Tensor] = None):
-        """Route + gate_up + down on the current stream from given top-k ids;
-        returns (rows, weights, permuted): rows[permuted[t, k]] is slot (t, k)'s
-        expert output (-1: an expert another rank holds)."""
-        rows = self._check_x(x)
+    def __call__(self, x_quant: torch.Tensor, x_scale: Optional[torch.Tensor], topk_ids: torch.Tensor,
+                 topk_weights: Optional[torch.Tensor] = None):
+        """Route + gate_up + down on the current stream from given top-k ids
+        (RoutedExpertGemm.__call__(x_quant, x_scale, topk_ids, topk_weights)).
+        ``x_quant``/``x_scale``: the MXFP8 routed input, or a bf16 [T, H]
+        ``x_quant`` with ``x_scale`` None. Returns (rows, weights, permuted):
+        rows[permuted[t, k]] is slot (t, k)'s expert output (-1: an expert
+        another rank holds)."""
+        mx = x_scale is not None
+        rows = self._check_xq(x_quant, x_scale) if mx else self._check_x(x_quant)
         if topk_ids.dim() != 2 or tuple(topk_ids.shape) != (rows, self.top_k):
             raise ValueError(f"topk_ids: expected [{rows}, {self.top_k}], got {tuple(topk_ids.shape)}")
         ids = topk_ids.to(torch.int32).contiguous()
         permuted, record, out_rows = self._outputs(rows)
-        check(
-            lib().mm_layer_experts(
-                self._handle, x.data_ptr(), ids.data_ptr(), rows, permuted.data_ptr(), record.data_ptr(),
-                out_rows.data_ptr(), _stream(self.device),
-            ),
-            "mm_layer_experts",
-        )
+        if mx:
+            rc = lib().mm_layer_experts_mxfp8(self._handle, x_quant.data_ptr(), x_scale.data_ptr(), ids.data_ptr(),
+                                              rows, permuted.data_ptr(), record.data_ptr(), out_rows.data_ptr(),
+                                              _stream(self.device))
+        else:
+            rc = lib().mm_layer_experts(self._handle, x_quant.data_ptr(), ids.data_ptr(), rows, permuted.data_ptr(),
+                                        record.data_ptr(), out_rows.data_ptr(), _stream(self.device))
+        check(rc, "mm_layer_experts_mxfp8" if mx else "mm_layer_experts")
         self.last_record = record
         w = None if topk_weights is None else topk_weights.contiguous().view(rows, self.top_k)
         return out_rows, w, permuted
 
     def gate_topk_and_gemms(
         self,
-        x: torch.Tensor,
+        x_quant: Optional[torch.Tensor],
+        x_scale: Optional[torch.Tensor],
         logits: torch.Tensor,
         bias: Optional[torch.Tensor],
         routed_scaling_factor: float,
         num_valid: Optional[torch.Tensor] = None,
-        *,
-        score: str = "sigmoid",
-        renormalize: bool = True,
+        alt=None,
         renormalize_epsilon: float = 0.0,
         ids_out: Optional[torch.Tensor] = None,
-        alt=None,
+        x: Optional[torch.Tensor] = None,
+        early: bool = False,
+        *,
+        score: str = "sigmoid",
+        renormalize=True,
     ):
-        """Top-k from fp32 router logits, then route + gate_up + down. Returns
-        (rows, weights, permuted, ids). ``alt`` = (bias_alt, input_ids, token
-        id): rows whose token is that id rank with bias_alt (vision routing)."""
-        rows = self._check_x(x)
+        """Top-k from fp32 router logits, then route + gate_up + down, in the
+        reference's positional order (routed_expert_gemm.py:776-870). The
+        routed input is ``x_quant``/``x_scale`` (MXFP8), or ``x`` (bf16, which
+        then takes their place: pass None for both). ``alt`` = (bias_alt,
+        input_ids, token id): rows whose token is that id rank with bias_alt
+        (vision routing). ``early`` is accepted for the reference's signature;
+        the router launch here always releases this one early. ``score``:
+        sigmoid (default), softmax or sqrtsoftplus (the reference's DSV4.1
+        router); ``renormalize``: True (score / sum), False, or "scaled_bf16"
+        (GLM-5.3's bf16(scale * s / (sum + eps))). Returns (rows, weights,
+        permuted, ids)."""
+        del early
+        mx = x is None
+        if mx:
+            if x_quant is None or x_scale is None:
+                raise ValueError("gate_topk_and_gemms: pass x_quant and x_scale, or x")
+            rows = self._check_xq(x_quant, x_scale)
+        else:
+            rows = self._check_x(x)
         if logits.dtype != torch.float32 or tuple(logits.shape) != (rows, self.router_experts) or not logits.is_contiguous():
             raise ValueError(f"logits: expected contiguous fp32 [{rows}, {self.router_experts}]")
         weights = torch.empty((rows, self.top_k), dtype=torch.float32, device=self.device)
@@ -270,13 +312,14 @@ class RoutedMoE:
         g = gate_args(logits, bias, num_valid, score, renormalize, routed_scaling_factor, renormalize_epsilon, weights, ids,
                       alt)
         permuted, record, out_rows = self._outputs(rows)
-        check(
-            lib().mm_layer_gate_experts(
-                self._handle, x.data_ptr(), ctypes.byref(g), rows, permuted.data_ptr(), record.data_ptr(),
-                out_rows.data_ptr(), _stream(self.device),
-            ),
-            "mm_layer_gate_experts",
-        )
+        if mx:
+            rc = lib().mm_layer_gate_experts_mxfp8(self._handle, x_quant.data_ptr(), x_scale.data_ptr(), ctypes.byref(g),
+                                                   rows, permuted.data_ptr(), record.data_ptr(), out_rows.data_ptr(),
+                                                   _stream(self.device))
+        else:
+            rc = lib().mm_layer_gate_experts(self._handle, x.data_ptr(), ctypes.byref(g), rows, permuted.data_ptr(),
+                                             record.data_ptr(), out_rows.data_ptr(), _stream(self.device))
+        check(rc, "mm_layer_gate_experts_mxfp8" if mx else "mm_layer_gate_experts")
         self.last_record = record
         return out_rows, weights, permuted, ids
 
@@ -365,7 +408,7 @@ class RoutedMoE:
         a.bias = _ptr(bias)
         a.num_valid = _ptr(num_valid)
         a.score_func = _lib.SCORES[score]
-        a.renormalize = int(bool(renormalize))
+        a.renormalize = _lib.renorm_code(renormalize)
         a.routed_scaling = float(routed_scaling_factor)
         a.renorm_eps = float(renormalize_epsilon)
         a.tokens = tokens
@@ -398,8 +441,39 @@ class RoutedMoE:
                                             _stream(self.device)), "mm_layer_rerun_experts")
 
     def check(self) -> None:
-        """Synchronize and raise if a bounded device wait of this layer timed out."""
+        """Synchronize and raise (DeviceTimeoutError) if a bounded device wait of
+        this layer timed out."""
         check(lib().mm_layer_check(self._handle), "mm_layer_check")
+
+    def set_wait_budget(self, microseconds: int) -> None:
+        """Budget of every bounded device wait of this layer's expert launches
+        (default 1.5 s)."""
+        check(lib().mm_layer_set_wait_budget(self._handle, int(microseconds)), "mm_layer_set_wait_budget")
+
+    def block_downs(self) -> None:
+        """Test hook for the timeout path: re-arm the last front pass's work
+        tables with every gate_up -> down mailbox out of reach, so that the next
+        ``rerun_experts(..., rearm=False)`` ends on its bounded waits and
+        ``check`` raises DeviceTimeoutError."""
+        check(lib().mm_layer_block_downs(self._handle, _stream(self.device)), "mm_layer_block_downs")
+
+    def read_scratch(self, which: str) -> torch.Tensor:
+        """A uint8 copy of one of the layer's quantized-activation buffers:
+        "x_codes" [3, max_rows, H/2], "x_scales" [3, max_rows, H/block],
+        "h_codes" [3, rows_capacity, h_row], "h_scales" [3, rows_capacity,
+        h_scale_row] (terms past act_terms unused; h rows in permuted order)."""
+        code = {"x_codes": _lib.MM_SCRATCH_X_CODES, "x_scales": _lib.MM_SCRATCH_X_SCALES,
+                "h_codes": _lib.MM_SCRATCH_H_CODES, "h_scales": _lib.MM_SCRATCH_H_SCALES}[which]
+        n = int(lib().mm_layer_scratch_bytes(self._handle, code))
+        out = torch.empty(n, dtype=torch.uint8, device=self.device)
+        check(lib().mm_layer_read_scratch(self._handle, code, out.data_ptr(), n, _stream(self.device)),
+              "mm_layer_read_scratch")
+        info = _lib.MMLayerInfo()
+        check(lib().mm_layer_get_info(self._handle, ctypes.byref(info)), "mm_layer_get_info")
+        return out.view(3, -1, {"x_codes": self.hidden // 2,
+                                "x_scales": self.hidden // (16 if self.weight_format == "nvfp4" else 32),
+                                "h_codes": int(info.h_row_bytes),
+                                "h_scales": int(info.h_scale_row_bytes)}[which])
 
 
 # ---------------------------------------------------------------------- stateless ops
@@ -437,7 +511,7 @@ def gate_args(logits, bias, num_valid, score, renormalize, scale, eps, weights, 
     g.bias = _ptr(bias)
     g.num_valid = _ptr(num_valid)
     g.score_func = _lib.SCORES[score]
-    g.renormalize = int(bool(renormalize))
+    g.renormalize = _lib.renorm_code(renormalize)
     g.routed_scaling = float(scale)
     g.renorm_eps = float(eps)
     g.weights = weights.data_ptr()

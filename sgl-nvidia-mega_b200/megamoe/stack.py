@@ -30,7 +30,7 @@ class MoEStack:
 
     def __init__(self, layers: Sequence[RoutedMoE], router_weights: Sequence[torch.Tensor],
                  gammas: Sequence[torch.Tensor], comm, *, biases: Optional[Sequence[Optional[torch.Tensor]]] = None,
-                 routed_scaling_factor: float = 1.0, score: str = "sigmoid", renormalize: bool = True,
+                 routed_scaling_factor: float = 1.0, score: str = "sigmoid", renormalize=True,
                  renormalize_epsilon: float = 0.0):
         n = len(layers)
         if n < 1 or len(router_weights) != n or len(gammas) != n or (biases is not None and len(biases) != n):
@@ -53,7 +53,7 @@ class MoEStack:
         self.biases = list(biases) if biases is not None else [None] * n
         self.comm = comm
         self.scale, self.score, self.renormalize, self.eps = (float(routed_scaling_factor), score,
-                                                              bool(renormalize), float(renormalize_epsilon))
+                                                              renormalize, float(renormalize_epsilon))
         self.hidden, self.top_k, self.max_rows = first.hidden, first.top_k, first.max_rows
         dev = first.device
         self.device = dev
@@ -84,7 +84,7 @@ class MoEStack:
             a.bias = _ptr(self.biases[i])
             a.num_valid = None
             a.score_func = _lib.SCORES[self.score]
-            a.renormalize = int(self.renormalize)
+            a.renormalize = _lib.renorm_code(self.renormalize)
             a.routed_scaling = self.scale
             a.renorm_eps = self.eps
             a.tokens = tokens

@@ -166,7 +166,7 @@ def _run_and_check(layer, x, ids, weights, K, max_rows, act_terms=3, expert_offs
     moe = to_gpu_layer(layer, K, max_rows, act_terms=act_terms, router_experts=router_experts,
                        expert_offset=expert_offset, window=window)
     xg = x.cuda()
-    rows, _, perm = moe(xg, ids.cuda())
+    rows, _, perm = moe(xg, None, ids.cuda())
     out = moe.finalize(rows, weights.cuda(), perm)
     moe.check()
     rows_c = rows.float().cpu()
@@ -290,7 +290,7 @@ def test_experts_balanced_dealing_groups_sum_to_the_layer():
     parts = []
     for group in (0, 1):
         moe = mm.RoutedMoE(*wts, K, 8, deal_group=group)
-        rows, _, perm = moe(x.cuda(), ids.cuda())
+        rows, _, perm = moe(x.cuda(), None, ids.cuda())
         operm, orec = O.route(ids.numpy(), E, -1 - group)
         assert np.array_equal(perm.cpu().numpy(), operm)
         _, kn_rows, _ = O.moe_layer(x, ids.numpy(), w.numpy(), layer, numerics="kernel", deal_group=group)
@@ -350,7 +350,7 @@ def test_forward_matches_steps_and_graph():
     bufs = {}
     out = moe.forward(xg, router_weight=wg, bias=bg, routed_scaling_factor=2.5, buffers=bufs).clone()
     logits = mm.router_gemv(xg, wg)
-    rows, w, perm, ids = moe.gate_topk_and_gemms(xg, logits, bg, 2.5)
+    rows, w, perm, ids = moe.gate_topk_and_gemms(None, None, logits, bg, 2.5, x=xg)
     out2 = moe.finalize(rows, w, perm)
     assert torch.equal(out, out2)
     ow, oids = O.gate_topk(O.router_gemv(O.bf16_bits(x), O.bf16_bits(wr)), bias.numpy(), K, scale=2.5)
@@ -566,8 +566,9 @@ def test_front_rank_and_route_bitexact(score, kind, E, K):
             valid = T if trial == 0 else max(1, T - 2)
             nv = torch.tensor([valid], dtype=torch.int32, device="cuda")
             x = torch.randn((T, H), generator=g).to(torch.bfloat16)
-            _, w, perm, ids = moe.gate_topk_and_gemms(x.cuda(), logits.cuda(),
-                                                     None if bias is None else bias.cuda(), 2.5, nv, score=score)
+            _, w, perm, ids = moe.gate_topk_and_gemms(None, None, logits.cuda(),
+                                                     None if bias is None else bias.cuda(), 2.5, nv, x=x.cuda(),
+                                                     score=score)
             torch.cuda.synchronize()
             ow, oids = O.gate_topk(logits.numpy(), None if bias is None else bias.numpy(), K, score=score,
                                    scale=2.5, num_valid=valid)
@@ -592,8 +593,8 @@ def test_front_vision_alt_bias_and_ep(T):
     bias_alt = (torch.randn(E, generator=g) * 0.5).float()
     input_ids = torch.randint(0, 3, (T,), generator=g, dtype=torch.int32)
     x = torch.randn((T, H), generator=g).to(torch.bfloat16)
-    _, w, perm, ids = moe.gate_topk_and_gemms(x.cuda(), logits.cuda(), bias.cuda(), 2.5,
-                                             alt=(bias_alt.cuda(), input_ids.cuda(), 1))
+    _, w, perm, ids = moe.gate_topk_and_gemms(None, None, logits.cuda(), bias.cuda(), 2.5,
+                                             alt=(bias_alt.cuda(), input_ids.cuda(), 1), x=x.cuda())
     torch.cuda.synchronize()
     ow, oids = O.gate_topk(logits.numpy(), bias.numpy(), K, scale=2.5, bias_alt=bias_alt.numpy(),
                            input_ids=input_ids.numpy(), alt_token_id=1)

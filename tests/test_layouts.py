@@ -96,8 +96,8 @@ def test_layer_from_trtllm_weights_equals_canonical_layer():
     g = torch.Generator().manual_seed(8)
     ids = torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(T)]).int().to(dev)
     wts = torch.rand((T, K), generator=g).to(dev)
-    ra, _, pa = a(x.to(dev), ids, wts)
-    rb, _, pb = b(x.to(dev), ids, wts)
+    ra, _, pa = a(x.to(dev), None, ids, wts)
+    rb, _, pb = b(x.to(dev), None, ids, wts)
     assert torch.equal(pa, pb)
     sel = pa.flatten().long()  # the rows the slots point to (padding rows are never written)
     assert torch.equal(ra[sel], rb[sel])
@@ -120,8 +120,8 @@ def test_nvfp4_layer_from_trtllm_weights_equals_canonical_layer():
     g = torch.Generator().manual_seed(9)
     ids = torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(T)]).int().to(dev)
     wts = torch.rand((T, K), generator=g).to(dev)
-    ra, _, pa = a(x.to(dev), ids, wts)
-    rb, _, pb = b(x.to(dev), ids, wts)
+    ra, _, pa = a(x.to(dev), None, ids, wts)
+    rb, _, pb = b(x.to(dev), None, ids, wts)
     assert torch.equal(pa, pb)
     sel = pa.flatten().long()
     assert torch.equal(ra[sel], rb[sel])

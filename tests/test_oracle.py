@@ -345,3 +345,34 @@ def test_gate_topk_sqrtsoftplus_and_alt_bias():
     _, ids2 = O.gate_topk(logits, np.zeros(E, np.float32), K, score="sqrtsoftplus", bias_alt=bias_alt,
                           input_ids=toks, alt_token_id=7)
     assert [int(ids2[t, 0]) == 9 for t in range(T)] == [True, False, True, False, False, True]
+
+
+def test_scaled_bf16_weight_rule_known_answers():
+    """GLM-5.3's routing weights (glm5_3/sm103/moe/routing.py:3-11): the top-8 by
+    sigmoid + bias, w = bf16(scale * s / (sum + 1e-20)) with the scale applied
+    first and the sum in the order of a warp xor-butterfly over the slots,
+    ((s0 + s4) + (s2 + s6)) + ((s1 + s5) + (s3 + s7))."""
+    f32 = np.float32
+    g = np.random.default_rng(3)
+    E, K, T = 256, 8, 6
+    logits = g.standard_normal((T, E)).astype(np.float32)
+    bias = (g.standard_normal(E) * 0.01).astype(np.float32)
+    w, ids = O.gate_topk(logits, bias, K, renormalize="scaled_bf16", scale=2.5, eps=1e-20)
+    _, ids_sum = O.gate_topk(logits, bias, K, scale=2.5)
+    assert np.array_equal(ids, ids_sum)  # the rule changes the weights, not the selection
+    sig = O.lib().or_sigmoid
+    for t in range(T):
+        s = [f32(sig(float(logits[t, e]))) for e in ids[t]]
+        total = ((s[0] + s[4]) + (s[2] + s[6])) + ((s[1] + s[5]) + (s[3] + s[7]))
+        d = f32(total + f32(1e-20))
+        for k in range(K):
+            q = f32(f32(f32(2.5) * s[k]) / d)
+            b = np.array([q], dtype=np.float32).view(np.uint32)[0]
+            b = (b + 0x7FFF + ((b >> 16) & 1)) & 0xFFFF0000  # bf16 round to nearest even
+            assert w[t, k].view(np.uint32) == b, (t, k)
+    # a sum whose order shows: slots whose scores differ by 2^-24 relative
+    logits2 = np.full((1, 16), -30.0, dtype=np.float32)
+    logits2[0, :8] = [20.0, 0.0, 20.0, 0.0, 20.0, 0.0, 20.0, 0.0]
+    w2, ids2 = O.gate_topk(logits2, None, 8, renormalize="scaled_bf16", scale=1.0, eps=1e-20)
+    assert sorted(ids2[0].tolist()) == list(range(8))
+    assert np.all(w2.view(np.uint32) & 0xFFFF == 0)
