@@ -244,7 +244,9 @@ def test_swiglu_output_terms_bitexact(fmt, T):
             e = int(ids[tok, k])
 
             def acc(colv, wv):
-                a = [np.float32(terms[t][tok, colv] * wv) for t in range(3)]  # exact products
+                # exact products; each term's accumulator is a sum of K products from
+                # +0, so a zero product of a negative weight accumulates to +0, not -0
+                a = [np.float32(0.0) + np.float32(terms[t][tok, colv] * wv) for t in range(3)]
                 s = (a[0] + a[1]) + a[2]
                 return s * alpha if nv else s
 
