@@ -18,7 +18,7 @@ the next of 64 resident token batches (distinct routings); one step streams
 ~1.4 GB of expert weights, far above the 126 MB L2, so no flush is needed.
 The e2e figure goes through the public API call with host buffers.
 
-Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mm|reference|flashinfer]
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mm|reference|flashinfer|ref-sm100]
 Under torchrun each rank drives one GPU; rank 0 prints one JSON line.
 """
 
@@ -60,9 +60,11 @@ def parse_args():
                          "256 + 1 experts; TP x EP2 at N > 1)")
     ap.add_argument("--experts", type=int, default=None,
                     help="routed experts (default: the config's; fewer only for small profiling cases)")
-    ap.add_argument("--impl", choices=["mm", "reference", "flashinfer"], default="mm",
+    ap.add_argument("--impl", choices=["mm", "reference", "flashinfer", "ref-sm100"], default="mm",
                     help="mm: this library; reference: the CPU oracle port; flashinfer: SGLang's stock GPU path "
-                         "(FlashInfer TRT-LLM-gen fused MoE, a library) on the same workload, N = 1")
+                         "(FlashInfer TRT-LLM-gen fused MoE, a library) on the same workload, N = 1; ref-sm100: the "
+                         "reference's own SM100 routed pair beside this library at DeepSeek-V4.1 geometry, N = 1 "
+                         "(baseline/ref_sm100.py; needs baseline/stage_ref_sm100.py run first)")
     ap.add_argument("--fi-act", choices=["bf16", "mxfp8"], default="bf16",
                     help="--impl flashinfer: activations bf16, or MXFP8 quantized before the timed region")
     ap.add_argument("--combine", choices=["peer", "nccl"], default="peer",
@@ -1000,10 +1002,47 @@ def run_flashinfer(args):
     moe.check()
 
 
+def run_ref_sm100(args):
+    """B1: the reference's own SM100 routed pair (RoutedExpertGemm: route +
+    GEMM1 + GEMM2) and this library's __call__ on the same weights, routings and
+    MXFP8 inputs at DeepSeek-V4.1 geometry (hidden 5120, 384 experts, top-6,
+    slice 576), timed by the reference benchmark's CUDA-graph method; one JSON
+    line with both arms' µs per routed half per case (baseline/ref_sm100.py)."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    sys.path.insert(0, os.path.join(REPO, "baseline"))
+    import ref_sm100
+
+    reg, why = ref_sm100.reference_module()
+    if reg is None:
+        print(json.dumps({"impl": "ref-sm100", "unavailable": why}), flush=True)
+        return
+    torch.cuda.set_device(0)
+    rows = [args.tokens] if args.tokens is not None else [1, 6, 16, 48]
+    cases = ref_sm100.run(rows, [6, 16, 32, 384], repeats=max(3, args.warmup), replays=20, log=lambda _: None)
+    main_case = next((c for c in cases if c["rows"] == 6 and c["distinct"] == 16), cases[0])
+    line = {
+        "impl": "ref-sm100",
+        "metric": "routed-MoE half us (route + gate_up + down), DeepSeek-V4.1 geometry",
+        "value": main_case["mm_us"],
+        "unit": "us",
+        "higher_is_better": False,
+        "reference_value": main_case["reference_us"],
+        "n_gpus": 1,
+        "config": {"workload": "DeepSeek-V4.1 routed half: hidden 5120, 384 experts, top-6, intermediate slice 576 "
+                               "(reference padded to 640), MXFP4 weights, MXFP8 routed input; headline case 6 rows, "
+                               "16 distinct experts; CUDA graph of 39 halves over two layers, spacer-corrected"},
+        "cases": cases,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.impl == "ref-sm100":
+        run_ref_sm100(args)
     elif args.impl == "flashinfer":
         run_flashinfer(args)
     elif args.stack:

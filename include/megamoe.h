@@ -54,6 +54,14 @@ extern "C" {
 #define MM_SCORE_SOFTMAX 1      /* key = x + bias, w = softmax over the top-k   */
 #define MM_SCORE_SQRTSOFTPLUS 2 /* s = sqrt(log1p(exp(x))) (x above 20: sqrt x),
                                    key = s + bias, w = s / sum (DeepSeek-V4.1) */
+#define MM_SCORE_SQRTSOFTPLUS_DSV41 3 /* the same with the DeepSeek-V4.1 gate's own
+                                   numerics (gate_topk.cuh:99-198 built for
+                                   SGLang's Triton router): CUDA's expf / log1pf /
+                                   sqrtf under flush-to-zero and approximate sqrt,
+                                   NaN ranked first, the Triton reduction's sum
+                                   order, div.full; ids and weights equal the
+                                   reference kernel's bit for bit. top_k 3 or 6,
+                                   renormalize MM_RENORM_SUM only               */
 
 /* ---- routing weight rules (mm_gate_args.renormalize) ------------------- */
 #define MM_RENORM_NONE 0        /* w = s * scale                                  */
@@ -225,10 +233,12 @@ int mm_route(const int32_t *ids, int32_t *permuted, int32_t *record, int32_t tok
              int32_t top_k, int32_t experts, int32_t expert_offset, void *stream);
 
 /* The router top-k and the route record in ONE launch that allocates nothing.
- * No counterpart in the reference. For callers that cannot call cudaMalloc: code
- * running while a CUDA graph is captured, or inside a runtime whose memory pool
- * owns the device, with only its input and output buffers at hand (the same fused
- * launch inside mm_layer_* uses scratch that mm_layer_create allocates).
+ * No counterpart in the reference. For callers that cannot call cudaMalloc: a
+ * serving runtime that reserves the GPU's memory for its own caching pool at
+ * start-up (an allocation outside the pool fails or fragments it), or plugin
+ * code that is handed only its input and output pointers and has no allocator
+ * (the same fused launch inside mm_layer_* uses scratch that mm_layer_create
+ * allocates).
  * Outputs equal mm_gate_topk followed by mm_route. gate->ids may be NULL (ids
  * not returned). Scratch: 8.25 KB of the library's static device memory per
  * GPU, held until exit; tokens * top_k <= 2048, larger requests are rejected

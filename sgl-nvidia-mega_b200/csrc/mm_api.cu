@@ -4,6 +4,7 @@
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
+#include <algorithm>
 #include <cstring>
 #include <string>
 
@@ -110,6 +111,8 @@ struct mm_layer {
   uint8_t *xq = nullptr, *xs = nullptr, *hq = nullptr, *hs = nullptr;
   int4 *segs = nullptr;
   int *ctrl = nullptr, *flags = nullptr;
+  float *part = nullptr;     // split-K partial sums [grid][kPartFloats]
+  int *split_cnt = nullptr;  // split-K arrival counters [2 x grid]
   uint32_t *err = nullptr;
   float *logits = nullptr, *weights = nullptr;
   int *ids = nullptr, *permuted = nullptr, *record = nullptr;
@@ -134,7 +137,7 @@ static cudaError_t router_smem_attr() {
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess || dev < 0 || dev >= 64) return e;
   if (done[dev]) return cudaSuccess;
-  e = cudaFuncSetAttribute(router_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  e = cudaFuncSetAttribute(router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(router_smem_bytes(kMaxRouterHidden)));
   if (e == cudaSuccess) done[dev] = true;
   return e;
@@ -154,10 +157,9 @@ int mm_router_gemv(const uint16_t *x, const uint16_t *w, float *logits, int32_t 
   a.tokens = tokens;
   a.experts = experts;
   a.hidden = hidden;
-  a.gemv_ctas = (experts + 3) / 4;
   MM_CUDA(router_smem_attr());
-  dim3 grid(a.gemv_ctas, (tokens + 7) / 8);
-  MM_CUDA(launch(router_quant_kernel, grid, dim3(256), router_smem_bytes(hidden), stream, a));
+  dim3 grid((experts + 3) / 4, (tokens + 7) / 8);
+  MM_CUDA(launch(router_kernel, grid, dim3(256), router_smem_bytes(hidden), stream, a));
   return MM_OK;
 }
 
@@ -167,9 +169,15 @@ static int check_gate(const mm_gate_args *a, int tokens, int E, int K) {
   if (E < 1 || E > kMaxRouterExperts) return fail(MM_ERR_INVALID, "gate: %d experts outside 1..%d", E, kMaxRouterExperts);
   if (K < 1 || K > kMaxTopK || K > E) return fail(MM_ERR_INVALID, "gate: top_k %d outside 1..min(16, experts)", K);
   if (a->score_func != MM_SCORE_SIGMOID && a->score_func != MM_SCORE_SOFTMAX &&
-      a->score_func != MM_SCORE_SQRTSOFTPLUS)
-    return fail(MM_ERR_UNSUPPORTED, "gate: score function %d is not built (sigmoid, softmax, sqrtsoftplus)",
+      a->score_func != MM_SCORE_SQRTSOFTPLUS && a->score_func != MM_SCORE_SQRTSOFTPLUS_DSV41)
+    return fail(MM_ERR_UNSUPPORTED,
+                "gate: score function %d is not built (sigmoid, softmax, sqrtsoftplus, sqrtsoftplus_dsv41)",
                 a->score_func);
+  if (a->score_func == MM_SCORE_SQRTSOFTPLUS_DSV41 &&
+      ((K != 3 && K != 6) || a->renormalize != MM_RENORM_SUM))
+    return fail(MM_ERR_UNSUPPORTED,
+                "gate: the DeepSeek-V4.1 gate numerics serve top-3 or top-6 with the sum rule (top_k %d, "
+                "renormalize %d)", K, a->renormalize);
   if (a->renormalize < 0 || a->renormalize > MM_RENORM_SCALED_BF16)
     return fail(MM_ERR_INVALID, "gate: renormalize %d (0, 1 or MM_RENORM_SCALED_BF16)", a->renormalize);
   if (a->renormalize == MM_RENORM_SCALED_BF16 && a->score_func == MM_SCORE_SOFTMAX)
@@ -201,7 +209,8 @@ int mm_gate_topk(const mm_gate_args *args, int32_t tokens, int32_t router_expert
                  void *stream) {
   int rc = check_gate(args, tokens, router_experts, top_k);
   if (rc) return rc;
-  MM_CUDA(launch(gate_topk_kernel, dim3(tokens), dim3(512), 0, stream, gate_args(args, router_experts, top_k)));
+  MM_CUDA(launch(args->score_func == MM_SCORE_SQRTSOFTPLUS_DSV41 ? gate_topk_dsv41_kernel : gate_topk_kernel,
+                 dim3(tokens), dim3(512), 0, stream, gate_args(args, router_experts, top_k)));
   return MM_OK;
 }
 
@@ -258,7 +267,8 @@ int mm_finalize_partial(const float *partial, uint16_t *out, int32_t tokens, int
 static void free_layer(mm_layer *L) {
   if (!L) return;
   void *ptrs[] = {L->sfa13, L->sfa2, L->ssfa13, L->ssfa2, L->xq, L->xs, L->hq, L->hs, L->segs,
-                  L->ctrl, L->flags, L->err, L->logits, L->weights, L->ids, L->permuted, L->record, L->alpha};
+                  L->ctrl, L->flags, L->part, L->split_cnt, L->err, L->logits, L->weights, L->ids,
+                  L->permuted, L->record, L->alpha};
   for (void *p : ptrs)
     if (p) cudaFree(p);
   delete L;
@@ -330,10 +340,11 @@ int mm_layer_create(const mm_layer_desc *desc, mm_layer **out) {
   L->m2 = L->H / 128;
   L->ks1 = L->H / kStageK;
   L->ks2 = (L->I + kStageK - 1) / kStageK;  // the down GEMM's last stage may be partial
-  // short down units (one or two K stages: narrow tensor-parallel slices) take two
-  // 128-row tiles each, so one accumulator hand-off serves two tiles; MXFP4 only
-  // (NVFP4's scale columns leave TMEM room for one tile per accumulator)
-  L->tg2 = (!nv && L->ks2 <= 2) ? 2 : 1;
+  // short down units (one to three K stages: narrow tensor-parallel slices, DSV4.1's
+  // 576-wide slice) take two 128-row tiles each, so one accumulator hand-off serves
+  // two tiles; MXFP4 only (NVFP4's scale columns leave TMEM room for one tile per
+  // accumulator)
+  L->tg2 = (!nv && L->ks2 <= 3) ? 2 : 1;
   static_assert(Fmt<kFmtMx>::kAccCols == 2 * kBRows && Fmt<kFmtNv>::kAccCols == kBRows,
                 "two-tile down units need MXFP4's double-width accumulator buffers");
   L->u2 = (L->m2 + L->tg2 - 1) / L->tg2;
@@ -386,6 +397,9 @@ int mm_layer_create(const mm_layer_desc *desc, mm_layer **out) {
   ALLOC(L->segs, sizeof(int4) * L->max_segs);
   ALLOC(L->ctrl, sizeof(int) * kCtrlWords);
   ALLOC(L->flags, sizeof(int) * L->max_segs);
+  const size_t grid = static_cast<size_t>(kCtasPerSm) * L->num_sms;
+  ALLOC(L->part, sizeof(float) * kPartFloats * grid);
+  ALLOC(L->split_cnt, sizeof(int) * 2 * grid);
   ALLOC(L->err, sizeof(uint32_t));
   ALLOC(L->logits, sizeof(float) * L->Tmax * L->R);
   ALLOC(L->weights, sizeof(float) * L->Tmax * L->K);
@@ -394,6 +408,7 @@ int mm_layer_create(const mm_layer_desc *desc, mm_layer **out) {
   ALLOC(L->record, sizeof(int) * L->route_words_max);
 #undef ALLOC
   ce = cudaMemset(L->ctrl, 0, sizeof(int) * kCtrlWords);
+  if (ce == cudaSuccess) ce = cudaMemset(L->split_cnt, 0, sizeof(int) * 2 * grid);
   if (ce == cudaSuccess) ce = cudaMemset(L->err, 0, sizeof(uint32_t));
   if (ce == cudaSuccess) ce = cudaMemset(L->hq, 0, hq_bytes);
   if (ce == cudaSuccess) ce = cudaMemset(L->hs, 0, hs_bytes);
@@ -464,6 +479,8 @@ int mm_layer_create(const mm_layer_desc *desc, mm_layer **out) {
   ea.segs = L->segs;
   ea.ctrl = L->ctrl;
   ea.flags = L->flags;
+  ea.part = L->part;
+  ea.split_cnt = L->split_cnt;
   ea.err = L->err;
   ea.clamp = d.clamp;
   ea.shared_clamp = d.shared_clamp;
@@ -491,6 +508,9 @@ int mm_layer_create(const mm_layer_desc *desc, mm_layer **out) {
   ce = expert_kernel_configure(L->fmt);
   if (ce == cudaSuccess)
     ce = cudaFuncSetAttribute(front_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(route_smem_bytes(kMaxTokens, kMaxRouterExperts)));
+  if (ce == cudaSuccess)
+    ce = cudaFuncSetAttribute(front_dsv41_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               static_cast<int>(route_smem_bytes(kMaxTokens, kMaxRouterExperts)));
   if (ce != cudaSuccess) {
     free_layer(L);
@@ -531,44 +551,31 @@ static cudaError_t launch_experts(mm_layer *L, const ExpertArgs &ea, void *strea
   return expert_kernel_launch(L->fmt, kCtasPerSm * L->num_sms, ea, stream);
 }
 
-// One launch of the router GEMV (w non-null) and the MXFP4-terms quantization
-// of x (bf16, or MXFP8 codes x8 with scales s8) into the layer's scratch
-// (extra CTAs of the same grid).
-static int launch_router_quant(mm_layer *L, const uint16_t *x, const uint16_t *w, float *logits, int tokens,
-                               void *stream, const uint8_t *x8 = nullptr, const uint8_t *s8 = nullptr) {
-  if (w && (L->H % 1024 || L->H > kMaxRouterHidden))
+// The router GEMV of a layer step: logits = x w^T (fp32).
+static int launch_router(mm_layer *L, const uint16_t *x, const uint16_t *w, float *logits, int tokens,
+                         void *stream) {
+  if (L->H % 1024 || L->H > kMaxRouterHidden)
     return fail(MM_ERR_INVALID, "router GEMV: hidden %d must be a multiple of 1024, <= %d", L->H, kMaxRouterHidden);
-  if (w && !aligned(w, 16)) return fail(MM_ERR_INVALID, "router weight must be 16-byte aligned");
+  if (!aligned(w, 16)) return fail(MM_ERR_INVALID, "router weight must be 16-byte aligned");
   RouterArgs a = {};
   a.x = x;
-  a.x8 = x8;
-  a.s8 = s8;
   a.w = w;
   a.logits = logits;
   a.tokens = tokens;
   a.experts = L->R;
   a.hidden = L->H;
-  a.gemv_ctas = w ? (L->R + 3) / 4 : 0;
-  a.xq = L->xq;
-  a.xs = L->xs;
-  a.max_tokens = L->Tmax;
-  a.terms = L->terms;
-  a.fmt = L->fmt;
-  a.gs = L->gs1;
-  a.inv_gs = L->fmt == kFmtNv ? L->d.input_scale[0] : 1.0f;
-  const int quant_ctas = (tokens * (L->H / 32) + 255) / 256;
-  dim3 grid(a.gemv_ctas + quant_ctas, w ? (tokens + 7) / 8 : 1);
-  if (w) MM_CUDA(router_smem_attr());
-  MM_CUDA(launch(router_quant_kernel, grid, dim3(256), w ? router_smem_bytes(L->H) : 0, stream, a));
+  MM_CUDA(router_smem_attr());
+  MM_CUDA(launch(router_kernel, dim3((L->R + 3) / 4, (tokens + 7) / 8), dim3(256), router_smem_bytes(L->H), stream, a));
   return MM_OK;
 }
 
-// [quantization] + front (gate or given ids) + experts. The routed input is bf16
-// x, or MXFP8 (x8 codes [T, H], s8 E8M0 scales [T, H/32]) when x is null.
+// Front (gate or given ids, route, and the routed input's quantization) +
+// experts. The routed input is bf16 x, or MXFP8 (x8 codes [T, H], s8 E8M0
+// scales [T, H/32]) when x is null.
 static int run_front_and_experts(mm_layer *L, const uint16_t *x, const mm_gate_args *gate,
                                  const int32_t *ids, int tokens, int32_t *permuted, int32_t *record,
-                                 uint16_t *rows, void *stream, bool quant_done = false,
-                                 const uint8_t *x8 = nullptr, const uint8_t *s8 = nullptr) {
+                                 uint16_t *rows, void *stream, const uint8_t *x8 = nullptr,
+                                 const uint8_t *s8 = nullptr) {
   if ((!x && !(x8 && s8)) || !permuted || !record || !rows) return fail(MM_ERR_INVALID, "layer call: null pointer");
   if (tokens < 1 || tokens > L->Tmax) return fail(MM_ERR_INVALID, "tokens %d outside 1..%d", tokens, L->Tmax);
   if ((x && !aligned(x, 16)) || (x8 && !aligned(x8, 16)) || !aligned(rows, 16))
@@ -597,12 +604,37 @@ static int run_front_and_experts(mm_layer *L, const uint16_t *x, const mm_gate_a
   f.route.shared_row_base = L->shared_row_base;
   f.route.m1 = L->m1;
   f.route.m2 = L->u2;
+  f.route.ks1 = L->ks1;
+  f.route.grid = kCtasPerSm * L->num_sms;
+  f.route.split_cnt = L->split_cnt;
+  // the routed input's FP4 terms: one 32-element chunk per warp and pass, at most
+  // two quantization CTAs per SM
+  QuantArgs &q = f.quant;
+  q.x = x;
+  q.x8 = x ? nullptr : x8;
+  q.s8 = x ? nullptr : s8;
+  q.xq = L->xq;
+  q.xs = L->xs;
+  q.tokens = tokens;
+  q.hidden = L->H;
+  q.max_tokens = L->Tmax;
+  q.terms = L->terms;
+  q.fmt = L->fmt;
+  q.gs = L->gs1;
+  q.inv_gs = L->fmt == kFmtNv ? L->d.input_scale[0] : 1.0f;
+  q.ctas = std::min((tokens * (L->H / 32) + 15) / 16, 2 * L->num_sms);
   MM_CUDA(cudaSetDevice(L->d.device));
-  if (!quant_done) {
-    int rc = launch_router_quant(L, x, nullptr, nullptr, tokens, stream, x ? nullptr : x8, x ? nullptr : s8);
-    if (rc) return rc;
+  if (gate != nullptr && gate->score_func == MM_SCORE_SQRTSOFTPLUS_DSV41) {
+    // the DeepSeek-V4.1 gate's launch is compiled with flush-to-zero: the routed
+    // input's quantization runs in a front_kernel launch of its own (no rows) first
+    FrontArgs qf = {};
+    qf.quant = q;
+    MM_CUDA(launch(front_kernel, dim3(q.ctas), dim3(512), 0, stream, qf));
+    f.quant.ctas = 0;
+    MM_CUDA(launch(front_dsv41_kernel, dim3(tokens), dim3(512), route_smem_bytes(tokens, L->E), stream, f));
+  } else {
+    MM_CUDA(launch(front_kernel, dim3(tokens + q.ctas), dim3(512), route_smem_bytes(tokens, L->E), stream, f));
   }
-  MM_CUDA(launch(front_kernel, dim3(tokens), dim3(512), route_smem_bytes(tokens, L->E), stream, f));
   ExpertArgs ea = L->ea;
   ea.rows_out = rows;
   ea.record = record;
@@ -617,6 +649,7 @@ int mm_layer_rearm_experts(mm_layer *L, void *stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   MM_CUDA(cudaMemsetAsync(L->flags, 0, sizeof(int) * L->max_segs, s));
   MM_CUDA(cudaMemsetAsync(L->ctrl + kCtrlClaim, 0, sizeof(int), s));
+  MM_CUDA(cudaMemsetAsync(L->split_cnt, 0, sizeof(int) * 2 * kCtasPerSm * L->num_sms, s));
   return MM_OK;
 }
 
@@ -628,6 +661,7 @@ int mm_layer_block_downs(mm_layer *L, void *stream) {
   // to the down units' target, so their bounded waits run out
   MM_CUDA(cudaMemsetAsync(L->flags, 0xc0, sizeof(int) * L->max_segs, s));
   MM_CUDA(cudaMemsetAsync(L->ctrl + kCtrlClaim, 0, sizeof(int), s));
+  MM_CUDA(cudaMemsetAsync(L->split_cnt, 0, sizeof(int) * 2 * kCtasPerSm * L->num_sms, s));
   return MM_OK;
 }
 
@@ -669,7 +703,7 @@ int mm_layer_experts_mxfp8(mm_layer *L, const uint8_t *x_quant, const uint8_t *x
                            int32_t tokens, int32_t *permuted, int32_t *record, uint16_t *rows, void *stream) {
   if (!L) return fail(MM_ERR_INVALID, "null layer");
   if (!x_quant || !x_scale) return fail(MM_ERR_INVALID, "mm_layer_experts_mxfp8: null x_quant or x_scale");
-  return run_front_and_experts(L, nullptr, nullptr, ids, tokens, permuted, record, rows, stream, false, x_quant,
+  return run_front_and_experts(L, nullptr, nullptr, ids, tokens, permuted, record, rows, stream, x_quant,
                                x_scale);
 }
 
@@ -678,7 +712,7 @@ int mm_layer_gate_experts_mxfp8(mm_layer *L, const uint8_t *x_quant, const uint8
                                 uint16_t *rows, void *stream) {
   if (!L || !gate) return fail(MM_ERR_INVALID, "null layer or gate arguments");
   if (!x_quant || !x_scale) return fail(MM_ERR_INVALID, "mm_layer_gate_experts_mxfp8: null x_quant or x_scale");
-  return run_front_and_experts(L, nullptr, gate, nullptr, tokens, permuted, record, rows, stream, false, x_quant,
+  return run_front_and_experts(L, nullptr, gate, nullptr, tokens, permuted, record, rows, stream, x_quant,
                                x_scale);
 }
 
@@ -718,11 +752,11 @@ int mm_layer_forward(mm_layer *L, const mm_forward_args *a, void *stream) {
   const float *logits = a->logits;
   if (!a->x || !aligned(a->x, 16)) return fail(MM_ERR_INVALID, "mm_layer_forward: x must be a 16-byte aligned pointer");
   MM_CUDA(cudaSetDevice(L->d.device));
-  {
-    float *lo = a->router_w ? (a->logits_out ? a->logits_out : L->logits) : nullptr;
-    int rc = launch_router_quant(L, a->x, a->router_w, lo, T, stream);
+  if (a->router_w) {
+    float *lo = a->logits_out ? a->logits_out : L->logits;
+    int rc = launch_router(L, a->x, a->router_w, lo, T, stream);
     if (rc) return rc;
-    if (a->router_w) logits = lo;
+    logits = lo;
   }
   if (!logits) return fail(MM_ERR_INVALID, "mm_layer_forward: neither router_w nor logits");
   mm_gate_args g = {};
@@ -742,7 +776,7 @@ int mm_layer_forward(mm_layer *L, const mm_forward_args *a, void *stream) {
   int32_t *perm = a->permuted ? a->permuted : L->permuted;
   int32_t *rec = a->record ? a->record : L->record;
   if (!a->rows) return fail(MM_ERR_INVALID, "mm_layer_forward: null rows buffer");
-  int rc = run_front_and_experts(L, a->x, &g, nullptr, T, perm, rec, a->rows, stream, true);
+  int rc = run_front_and_experts(L, a->x, &g, nullptr, T, perm, rec, a->rows, stream);
   if (rc) return rc;
   const uint16_t *shared = L->has_shared ? a->rows + static_cast<size_t>(L->shared_row_base) * L->H : nullptr;
   if (a->residual) {

@@ -4,9 +4,11 @@
 //
 // Work: a segment is up to 16 consecutive permuted rows of one expert (the
 // shared expert's tokens form segments too). A gate_up unit streams one 128-row
-// tile of w13 (64 gate rows + the 64 matching up rows) through all of H and
-// multiplies it with the segment's rows; a down unit streams one 128-row tile of
-// w2 through all of I. Units are numbered [all gate_up units][all down units];
+// tile of w13 (64 gate rows + the 64 matching up rows) through all of H, or
+// through one of `split` K chunks of H when the step has fewer gate_up tiles
+// than the grid (split-K, mm_layout.cuh), and multiplies it with the segment's
+// rows; a down unit streams one 128-row tile of w2 (or two, for narrow MXFP4
+// slices) through all of I. Units are numbered [all gate_up units][all down units];
 // CTA b runs unit b first and then claims units from a global counter, so
 // every gate_up unit is taken before any later down unit; a down unit's
 // activations wait on its segment's mailbox (the number of finished gate_up
@@ -17,7 +19,7 @@
 // Arithmetic: tcgen05.mma kind::mxf4 block32 (E2M1 x E2M1, an E8M0 scale per 32
 // along K for both operands), M = 128 weight rows, N = terms * n activation
 // rows, K = 64 per instruction, fp32 accumulators in TMEM. The activations are
-// carried as MXFP4 terms (see quantize_block32_fp4), each term in its own
+// carried as MXFP4 terms (see quantize_block32_fp4_warp), each term in its own
 // accumulator columns; the epilogue adds the terms.
 //
 // Warp roles (224 threads):
@@ -44,20 +46,37 @@ namespace {
 
 constexpr uint32_t kATxBytes = kAStageBytes;  // packed codes land as they are
 
-// Unit u: gate_up units [0, nseg m1) (segment, 128-row gate_up tile m), then
-// down units (segment, down unit m covering w2 tiles [m tg2, m tg2 + tg2)).
-__device__ __forceinline__ void decode_unit(int u, int nseg, int m1, int m2, bool &g2, int &seg,
-                                            int &m) {
-  const int n1 = nseg * m1;
+// Unit u: gate_up units [0, nseg m1 split) (segment, 128-row gate_up tile m, K
+// chunk c), then down units (segment, down unit m covering w2 tiles
+// [m tg2, m tg2 + tg2); c = 0).
+__device__ __forceinline__ void decode_unit(int u, int nseg, int m1, int split, int m2, bool &g2, int &seg,
+                                            int &m, int &c) {
+  const int per1 = m1 * split;
+  const int n1 = nseg * per1;
   if (u < n1) {
     g2 = false;
-    seg = u / m1;
-    m = u - seg * m1;
+    seg = u / per1;
+    const int r = u - seg * per1;
+    m = r / split;
+    c = r - m * split;
   } else {
     g2 = true;
+    c = 0;
     const int v = u - n1;
     seg = v / m2;
     m = v - seg * m2;
+  }
+}
+
+// The K stages of a unit: [k0, k0 + n) of ks_u for gate_up chunk c of `split`;
+// a down unit's tiles one after the other (tiles x ks_u stages from 0).
+__device__ __forceinline__ void unit_stages(bool g2, int c, int split, int ks_u, int tiles, int &k0, int &n) {
+  if (g2) {
+    k0 = 0;
+    n = tiles * ks_u;
+  } else {
+    k0 = c * ks_u / split;
+    n = (c + 1) * ks_u / split - k0;
   }
 }
 
@@ -221,6 +240,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
       pdl_wait();
       const int nseg = p.ctrl[kCtrlSegments];
       const int total = p.ctrl[kCtrlUnits];
+      const int split = p.ctrl[kCtrlSplit];
       const uint64_t policy = policy_evict_first();
       uint32_t stage = 0, phase = 0, ws = 0, wphase = 0;
       // CTA b's first unit is unit b, unclaimed: the first wave gives every CTA
@@ -251,22 +271,25 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
         if (++ws == kWorkSlots) { ws = 0; wphase ^= 1u; }
         if (!have) break;
         bool g2;
-        int seg, m;
-        decode_unit(u, nseg, p.m1, p.u2, g2, seg, m);
+        int seg, m, c;
+        decode_unit(u, nseg, p.m1, split, p.u2, g2, seg, m, c);
         const int4 sg = seg_cache.get(p.segs, seg);
         const int e = sg.x < 0 ? 0 : sg.x;
         const bool sh = sg.x < 0;
         const CUtensorMap *map = g2 ? (sh ? &p.sw2_map : &p.w2_map) : (sh ? &p.sw13_map : &p.w13_map);
         // a down unit's stages run over its tiles, K stages within a tile; the
-        // tiles' scale chunks are consecutive ([expert][tile][K stage])
+        // tiles' scale chunks are consecutive ([expert][tile][K stage]); a
+        // gate_up chunk's stages are [k0, k0 + ks_n) of its tile
         const int ks_u = g2 ? p.ks2 : p.ks1;
         const int t0 = g2 ? m * kTg2 : m;
-        const int ks_n = (g2 ? (kTg2 == 1 ? 1 : min(kTg2, p.m2 - t0)) : 1) * ks_u;
+        int k0, ks_n;
+        unit_stages(g2, c, split, ks_u, kTg2 == 1 ? 1 : min(kTg2, p.m2 - t0), k0, ks_n);
         const uint8_t *sfa = g2 ? (sh ? p.ssfa2 : p.sfa2) : (sh ? p.ssfa13 : p.sfa13);
-        sfa += (static_cast<size_t>(e) * (g2 ? p.m2 : p.m1) + t0) * static_cast<size_t>(ks_u) * L::kSfStageBytes;
+        sfa += ((static_cast<size_t>(e) * (g2 ? p.m2 : p.m1) + t0) * static_cast<size_t>(ks_u) + k0) *
+               L::kSfStageBytes;
         const int claim_at = ks_n > 3 ? ks_n - 3 : 0;
         const bool refill = !b_claimed && a_end - a_next <= 1;
-        int tt = 0, kq = 0;  // tile of the unit (down units) and K stage within it
+        int tt = 0, kq = k0;  // tile of the unit (down units) and K stage within it
 #pragma unroll 1
         for (int ks = 0; ks < ks_n; ++ks) {
           if (refill && ks == claim_at) {
@@ -321,6 +344,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
     if (lane == 0) {
       pdl_wait();
       const int nseg = p.ctrl[kCtrlSegments];
+      const int split = p.ctrl[kCtrlSplit];
       uint32_t stage = 0, phase = 0, ws = 0, wphase = 0, acc = 0, acc_phase = 0;
       // descriptor words that never change: A/B 128-byte-swizzled K-major with
       // 1 KB between 8-row groups; scale chunks: 32 rows x 16 B, 128 B apart
@@ -336,22 +360,23 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
         if (++ws == kWorkSlots) { ws = 0; wphase ^= 1u; }
         if (u < 0) break;
         bool g2;
-        int seg, m;
-        decode_unit(u, nseg, p.m1, p.u2, g2, seg, m);
+        int seg, m, c;
+        decode_unit(u, nseg, p.m1, split, p.u2, g2, seg, m, c);
         const int4 sg = seg_cache.get(p.segs, seg);
         const uint32_t n = static_cast<uint32_t>((sg.z + 7) & ~7);
         const uint32_t nmma = n * static_cast<uint32_t>(p.terms);  // term 0 rows, term 1 rows, ...
         const uint32_t id0 = idesc_base | ((nmma >> 3) << 17);
         const uint32_t id2 = id0 | (2u << 4) | (2u << 29);  // MXFP4: the chunk's second byte pair
         const int ks_u = g2 ? p.ks2 : p.ks1;
-        const int ks_n = (g2 ? (kTg2 == 1 ? 1 : min(kTg2, p.m2 - m * kTg2)) : 1) * ks_u;
+        int k0, ks_n;
+        unit_stages(g2, c, split, ks_u, kTg2 == 1 ? 1 : min(kTg2, p.m2 - m * kTg2), k0, ks_n);
         if (!mbar_wait(bar(kBarAccEmpty + acc), acc_phase ^ 1u, err, kErrTimeoutAcc, wb)) break;
         tc_fence_after();
         // accumulator buffers tg2 x kBRows columns apart (single-tile layers keep them adjacent)
         const uint32_t acc_tmem = tbase + L::kTmemAcc + acc * static_cast<uint32_t>(kTg2 * kBRows);
         bool ok = true;
         uint32_t d_tmem = acc_tmem;  // the unit's current tile: its accumulator kBRows columns further
-        int kq = 0;                  // K stage within the tile
+        int kq = 0;                  // K stage within the tile (within the chunk: the first accumulates from 0)
 #pragma unroll 1
         for (int ks = 0; ks < ks_n; ++ks) {
           if (!mbar_wait(bar(kBarFull + stage), phase, err, kErrTimeoutFull, wb)) {
@@ -405,6 +430,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
     // of short down units of one segment pays the set-up once.
     pdl_wait();
     const int nseg = p.ctrl[kCtrlSegments];
+    const int split = p.ctrl[kCtrlSplit];
     uint32_t stage = 0, phase = 0, ws = 0, wphase = 0;
     SegCache seg_cache;
     int ready_seg = -1;                 // a segment whose mailbox is known complete
@@ -434,8 +460,8 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
       if (++ws == kWorkSlots) { ws = 0; wphase ^= 1u; }
       if (!okw || u < 0) break;
       bool g2;
-      int seg, m;
-      decode_unit(u, nseg, p.m1, p.u2, g2, seg, m);
+      int seg, m, c;
+      decode_unit(u, nseg, p.m1, split, p.u2, g2, seg, m, c);
       if (g2 && seg != ready_seg) {  // once complete, a mailbox stays complete in this launch
         int okf = 1;
         if (lane == 0) okf = wait_flag(p.flags + seg, 2 * p.m1, err, wb) ? 1 : 0;
@@ -486,11 +512,13 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
           smask = (rr < nb && r < rows) ? (smask | (1u << h)) : (smask & ~(1u << h));
         }
       }
-      // a down unit's tiles share their B: stage ks loads K stage ks % ks_u
+      // a down unit's tiles share their B: stage ks loads K stage ks % ks_u; a
+      // gate_up chunk loads K stages [k0, k0 + ks_n)
       const int ks_u = g2 ? p.ks2 : p.ks1;
-      const int ks_n = (g2 ? (kTg2 == 1 ? 1 : min(kTg2, p.m2 - m * kTg2)) : 1) * ks_u;
+      int k0, ks_n;
+      unit_stages(g2, c, split, ks_u, kTg2 == 1 ? 1 : min(kTg2, p.m2 - m * kTg2), k0, ks_n);
 #pragma unroll 1
-      for (int ks = 0, kq = 0; ks < ks_n; ++ks, kq = (kq + 1 == ks_u) ? 0 : kq + 1) {
+      for (int ks = 0, kq = k0; ks < ks_n; ++ks, kq = (kq + 1 == ks_u) ? 0 : kq + 1) {
         int oke = 1;
         if (lane == 0) oke = mbar_wait(bar(kBarEmpty + stage), phase ^ 1u, err, kErrTimeoutEmpty, wb) ? 1 : 0;
         oke = __shfl_sync(0xffffffffu, oke, 0);
@@ -520,14 +548,68 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
     // ============================ epilogue ===================================
     // No block-level barrier here: the gate_up hand-off between the up-row and
     // gate-row warps goes through two mbarriers with bounded waits, and each
-    // gate-row warp publishes its own h rows to the segment mailbox.
+    // gate-row warp publishes its own h rows to the segment mailbox. Split-K
+    // chunks hand off through global memory instead (mm_layout.cuh).
     pdl_wait();
     const int nseg = p.ctrl[kCtrlSegments];
+    const int split = p.ctrl[kCtrlSplit];
     const int q = warp & 3;             // TMEM lane quadrant of this warp
     const int row = 32 * q + lane;      // accumulator row (weight-tile row)
     float *ex = reinterpret_cast<float *>(sbase + L::kSmemEpi);
     uint32_t ws = 0, wphase = 0, acc = 0, acc_phase = 0, ex_phase = 0;
     SegCache seg_cache;
+    // SwiGLU (+ clamp) of the 32 features f = 64 m + 32 fq + lane of segment sg's
+    // rows (get(j, gate, up) gives row j's accumulator sums), requantized into
+    // h's FP4 terms, then this warp's increment of the segment's mailbox (two
+    // per gate_up tile)
+    auto swiglu_publish = [&](const int4 &sg, int seg, int m, int fq, auto &&get) {
+      const int rows = sg.z;
+      const float *lim = sg.x < 0 ? p.shared_clamp : p.clamp;
+      const bool clamped = lim != nullptr;
+      const float limit = clamped ? lim[sg.x < 0 ? 0 : sg.x] : 0.0f;
+      const int f = 64 * m + 32 * fq + lane;  // feature (column of h)
+      const size_t rowb = static_cast<size_t>(p.hq_row);
+      const size_t tq = static_cast<size_t>(p.rows_cap) * rowb;      // term stride of hq
+      const size_t ts = static_cast<size_t>(p.rows_cap) * p.hs_row;  // term stride of hs
+#pragma unroll
+      for (int j = 0; j < kSegRows; ++j) {
+        if (j >= rows) break;
+        float g, up;
+        get(j, g, up);
+        if (clamped) {
+          up = fminf(fmaxf(up, -limit), limit);
+          g = fminf(g, limit);
+        }
+        float r = __fmul_rn(up, __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
+        const size_t prow = static_cast<size_t>(sg.y + j);
+        // FP4 terms of the 32 features of this warp for token row j: one
+        // MXFP4 block of 32, or two NVFP4 blocks of 16 (lane halves)
+        for (int t = 0; t < p.terms; ++t) {
+          uint32_t nib, code;
+          if constexpr (kNv) {
+            float amax = fabsf(r);
+#pragma unroll
+            for (int off = 8; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+            code = nv4_scale_code(amax, p.gs2);
+            const float sv = e4m3_value(static_cast<uint8_t>(code));
+            nib = e2m1x2(__fmul_rn(r, nv4_multiplier(sv, p.gs2)), 0.0f) & 15u;
+            r = __fsub_rn(r, __fmul_rn(__fmul_rn(e2m1_value(nib), sv), p.inv_gs2));
+          } else {
+            const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(r))));
+            code = mx4_scale_code(amax);
+            nib = e2m1x2(__fmul_rn(r, mx_inverse(code)), 0.0f) & 15u;
+            r = __fsub_rn(r, __fmul_rn(e2m1_value(nib), mx_scale_value(code)));
+          }
+          const uint32_t up_nib = __shfl_down_sync(0xffffffffu, nib, 1);
+          if ((lane & 1) == 0) p.hq[t * tq + prow * rowb + (f >> 1)] = static_cast<uint8_t>(nib | (up_nib << 4));
+          if ((lane & (L::kBlock - 1)) == 0)
+            p.hs[t * ts + prow * p.hs_row + f / L::kBlock] = static_cast<uint8_t>(code);
+        }
+      }
+      __threadfence();
+      __syncwarp();
+      if (lane == 0) asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(p.flags + seg) : "memory");
+    };
 #pragma unroll 1
     while (true) {
       int u = -1, okw = 1;
@@ -543,8 +625,8 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
       if (++ws == kWorkSlots) { ws = 0; wphase ^= 1u; }
       if (!okw || u < 0) break;
       bool g2;
-      int seg, m;
-      decode_unit(u, nseg, p.m1, p.u2, g2, seg, m);
+      int seg, m, c;
+      decode_unit(u, nseg, p.m1, split, p.u2, g2, seg, m, c);
       const int4 sg = seg_cache.get(p.segs, seg);
       const int rows = sg.z;
       const int n = (rows + 7) & ~7;
@@ -557,6 +639,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
       const int tiles = g2 ? (kTg2 == 1 ? 1 : min(kTg2, p.m2 - m * kTg2)) : 1;
       const uint32_t acc_addr =
           tbase + (static_cast<uint32_t>(32 * q) << 16) + L::kTmemAcc + acc * static_cast<uint32_t>(kTg2 * kBRows);
+      const bool chunked = !g2 && split > 1;
 #pragma unroll 1
       for (int tt = 0; tt < tiles; ++tt) {
         uint32_t ra[32], rb[16];
@@ -579,12 +662,47 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
           if (p.terms > 2) a = __fadd_rn(a, __uint_as_float(n == 8 ? ra[16 + j] : rb[j]));
           v[j] = a;
         }
-        if constexpr (kNv) {  // the product of the two second-level scales
-          const float al = sg.x < 0 ? (g2 ? p.salpha2[0] : p.salpha13[0]) : (g2 ? p.alpha2[sg.x] : p.alpha13[sg.x]);
+        float al = 1.0f;  // NVFP4: the product of the two second-level scales (a split
+        if constexpr (kNv) {  // tile applies it once, to the sum of its chunks)
+          al = sg.x < 0 ? (g2 ? p.salpha2[0] : p.salpha13[0]) : (g2 ? p.alpha2[sg.x] : p.alpha13[sg.x]);
+          if (!chunked) {
 #pragma unroll
-          for (int j = 0; j < kSegRows; ++j) v[j] = __fmul_rn(v[j], al);
+            for (int j = 0; j < kSegRows; ++j) v[j] = __fmul_rn(v[j], al);
+          }
         }
-        if (!g2) {
+        if (chunked) {
+          // split-K chunk: this warp's rows of the chunk's partial sums go to the
+          // chunk's slot; the warp then counts in for its half of the tile's
+          // features (gate rows 32 fq + lane, up rows 64 + 32 fq + lane)
+          const int tile = u / split;
+          const int fq = q & 1;
+          float *mine = p.part + static_cast<size_t>(u) * kPartFloats + row;
+#pragma unroll
+          for (int j = 0; j < kSegRows; ++j)
+            if (j < rows) mine[j * 128] = v[j];
+          __threadfence();
+          __syncwarp();
+          int last = 0;
+          if (lane == 0) last = atomicAdd(p.split_cnt + 2 * tile + fq, 1) == 2 * split - 1 ? 1 : 0;
+          last = __shfl_sync(0xffffffffu, last, 0);
+          if (last) {
+            // the half's last warp: every chunk's partials, added in chunk order
+            __threadfence();
+            const float *base = p.part + static_cast<size_t>(tile) * split * kPartFloats + 32 * fq + lane;
+            swiglu_publish(sg, seg, m, fq, [&](int j, float &g, float &up) {
+              g = __ldcg(base + j * 128);
+              up = __ldcg(base + j * 128 + 64);
+              for (int cc = 1; cc < split; ++cc) {
+                g = __fadd_rn(g, __ldcg(base + cc * kPartFloats + j * 128));
+                up = __fadd_rn(up, __ldcg(base + cc * kPartFloats + j * 128 + 64));
+              }
+              if constexpr (kNv) {
+                g = __fmul_rn(g, al);
+                up = __fmul_rn(up, al);
+              }
+            });
+          }
+        } else if (!g2) {
           // rows 0..63: gate of features 64m + row; rows 64..127: up of the same features
           if (q >= 2) {
             if (lane == 0) ok = mbar_wait(bar(kBarExFree), ex_phase ^ 1u, err, kErrTimeoutAcc, wb) ? 1 : 0;
@@ -603,52 +721,10 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
             for (int j = 0; j < kSegRows; ++j) upv[j] = ex[row * kSegRows + j];
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(kBarExFree));
-            const float *lim = sg.x < 0 ? p.shared_clamp : p.clamp;
-            const bool clamped = lim != nullptr;
-            const float L = clamped ? lim[sg.x < 0 ? 0 : sg.x] : 0.0f;
-            const int f = 64 * m + 32 * q + lane;  // feature (column of h)
-            const size_t rowb = static_cast<size_t>(p.hq_row);
-            const size_t tq = static_cast<size_t>(p.rows_cap) * rowb;  // term stride of hq
-            const size_t ts = static_cast<size_t>(p.rows_cap) * p.hs_row;  // term stride of hs
-#pragma unroll
-            for (int j = 0; j < kSegRows; ++j) {
-              if (j >= rows) break;
-              float g = v[j];
-              float up = upv[j];
-              if (clamped) {
-                up = fminf(fmaxf(up, -L), L);
-                g = fminf(g, L);
-              }
-              float r = __fmul_rn(up, __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
-              const size_t prow = static_cast<size_t>(sg.y + j);
-              // FP4 terms of the 32 features of this warp for token row j: one
-              // MXFP4 block of 32, or two NVFP4 blocks of 16 (lane halves)
-              for (int t = 0; t < p.terms; ++t) {
-                uint32_t nib, code;
-                if constexpr (kNv) {
-                  float amax = fabsf(r);
-#pragma unroll
-                  for (int off = 8; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-                  code = nv4_scale_code(amax, p.gs2);
-                  const float sv = e4m3_value(static_cast<uint8_t>(code));
-                  nib = e2m1x2(__fmul_rn(r, nv4_multiplier(sv, p.gs2)), 0.0f) & 15u;
-                  r = __fsub_rn(r, __fmul_rn(__fmul_rn(e2m1_value(nib), sv), p.inv_gs2));
-                } else {
-                  const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(r))));
-                  code = mx4_scale_code(amax);
-                  nib = e2m1x2(__fmul_rn(r, mx_inverse(code)), 0.0f) & 15u;
-                  r = __fsub_rn(r, __fmul_rn(e2m1_value(nib), mx_scale_value(code)));
-                }
-                const uint32_t up_nib = __shfl_down_sync(0xffffffffu, nib, 1);
-                if ((lane & 1) == 0) p.hq[t * tq + prow * rowb + (f >> 1)] = static_cast<uint8_t>(nib | (up_nib << 4));
-                if ((lane & (L::kBlock - 1)) == 0)
-                  p.hs[t * ts + prow * p.hs_row + f / L::kBlock] = static_cast<uint8_t>(code);
-              }
-            }
-            // publish this warp's 32 features of every row: two increments per unit
-            __threadfence();
-            __syncwarp();
-            if (lane == 0) asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(p.flags + seg) : "memory");
+            swiglu_publish(sg, seg, m, q, [&](int j, float &g, float &up) {
+              g = v[j];
+              up = upv[j];
+            });
           }
           ex_phase ^= 1u;
         } else {

@@ -38,31 +38,39 @@ struct RouteArgs {
   int *flags;
   int has_shared;
   int shared_row_base;
-  int m1, m2;                // gate_up / down units per segment
+  int m1, m2;                // gate_up tiles / down units per segment
+  int ks1;                   // K stages of a gate_up tile
+  int grid;                  // the expert kernel's CTAs (the split-K choice)
+  int *split_cnt;            // [2 x grid] split-K arrival counters, zeroed when split > 1
+};
+
+// The routed input's quantization into FP4 terms (extra CTAs of the front launch).
+struct QuantArgs {
+  const uint16_t *x;         // bf16 [T, H], or null with
+  const uint8_t *x8;         //    MXFP8 [T, H] E4M3 codes and
+  const uint8_t *s8;         //    [T, H/32] E8M0 block scales
+  uint8_t *xq;               // [kMaxTerms][max_tokens][H/2] packed E2M1
+  uint8_t *xs;               // [kMaxTerms][max_tokens][H/32] E8M0 (NVFP4: [H/16] E4M3)
+  int tokens, hidden, max_tokens, terms;
+  int fmt;                   // kFmtMx or kFmtNv
+  float gs, inv_gs;          // NVFP4: 1 / input_scale[0] and input_scale[0]
+  int ctas;                  // quantization CTAs (after the T row CTAs); 0: none
 };
 
 struct FrontArgs {
   GateArgs gate;             // gate.logits null: ids are given in route.ids
   RouteArgs route;
+  QuantArgs quant;
 };
 
 constexpr int kMaxRouterParts = 14;  // H <= 14336 for the router GEMV (x tile in shared memory)
 constexpr int kMaxRouterHidden = 1024 * kMaxRouterParts;
 
 struct RouterArgs {
-  const uint16_t *x;         // bf16 [T, H] (GEMV input; quantized unless x8 is set)
-  const uint8_t *x8;         // or MXFP8 [T, H] E4M3 codes (quantization only), with
-  const uint8_t *s8;         //    [T, H/32] E8M0 block scales
-  const uint16_t *w;         // bf16 [E, H] (null when gemv_ctas == 0)
+  const uint16_t *x;         // bf16 [T, H]
+  const uint16_t *w;         // bf16 [E, H]
   float *logits;             // [T, E]
   int tokens, experts, hidden;
-  int gemv_ctas;             // E, or 0 for quantization only
-  uint8_t *xq;               // [kMaxTerms][max_tokens][H/2] packed E2M1, or null
-  uint8_t *xs;               // [kMaxTerms][max_tokens][H/32] E8M0 (NVFP4: [H/16] E4M3)
-  int max_tokens;
-  int terms;
-  int fmt;                   // kFmtMx or kFmtNv
-  float gs, inv_gs;          // NVFP4: 1 / input_scale[0] and input_scale[0]
 };
 
 struct alignas(64) ExpertArgs {
@@ -90,6 +98,8 @@ struct alignas(64) ExpertArgs {
   const int4 *segs;
   int *ctrl;
   int *flags;
+  float *part;               // [grid][kPartFloats] split-K partial sums
+  int *split_cnt;            // [2 x grid] split-K arrival counters (per tile and feature half)
   uint32_t *err;
   const float *clamp;        // [E] or null
   const float *shared_clamp; // [1] or null
@@ -110,64 +120,54 @@ struct FinalizeArgs {
   int tokens, top_k, hidden;
 };
 
-// MXFP4 terms of 32 fp32 values (one block): term t is the MXFP4 quantization
-// of the residual left by terms 0..t-1 (E8M0 code by mx4_scale_code, codes
-// e2m1(r * 2^(127-code)) RN saturating, residual r -= e2m1 * 2^(code-127)).
-// Writes 16 bytes of codes per term at q + t * q_stride and the code at
-// s + t * s_stride.
-__device__ __forceinline__ void quantize_block32_fp4(const float (&v)[32], int terms, uint8_t *q,
-                                                     size_t q_stride, uint8_t *s, size_t s_stride) {
-  float r[32];
-#pragma unroll
-  for (int i = 0; i < 32; ++i) r[i] = v[i];
+// Activation quantization into FP4 terms, one warp per 32 fp32 values, lane i
+// holding value i. Term t quantizes the residual r left by terms 0..t-1:
+//  * MXFP4 (one block of 32): E8M0 code c = mx4_scale_code(amax), codes
+//    e2m1(r * 2^(127-c)) RN saturating, r -= e2m1 * 2^(c-127); 16 bytes of
+//    codes per term at q + t * q_stride, the code at s + t * s_stride;
+//  * NVFP4 under the global scale gs (lanes 0-15 and 16-31 are two blocks of
+//    16): E4M3 scale sf = nv4_scale_code(amax, gs), codes e2m1(r * gs / sf) RN
+//    saturating, r -= (e2m1 * sf) * inv_gs; 8 bytes of codes per block and
+//    term, the two scale bytes at s + t * s_stride + {0, 1}.
+// amax is the (half-)warp maximum of |r|, NaN counted as 0 (the value of an
+// fmaxf chain from 0).
+__device__ __forceinline__ uint32_t amax_key(float r) {
+  const float a = fabsf(r);
+  return a != a ? 0u : __float_as_uint(a);
+}
+
+__device__ __forceinline__ void quantize_block32_fp4_warp(float r, int terms, uint8_t *q, size_t q_stride,
+                                                          uint8_t *s, size_t s_stride) {
+  const int lane = threadIdx.x & 31;
   for (int t = 0; t < terms; ++t) {
-    float amax = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(r[i]));
+    const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, amax_key(r)));
     const uint32_t c = mx4_scale_code(amax);
-    const float inv = mx_inverse(c);
-    const float sv = mx_scale_value(c);
-    uint32_t packed[4] = {0u, 0u, 0u, 0u};
-#pragma unroll
-    for (int i = 0; i < 32; i += 2) {
-      const uint32_t b = e2m1x2(__fmul_rn(r[i], inv), __fmul_rn(r[i + 1], inv));
-      packed[i >> 3] |= b << (8 * ((i >> 1) & 3));
-      r[i] = __fsub_rn(r[i], __fmul_rn(e2m1_value(b & 15u), sv));
-      r[i + 1] = __fsub_rn(r[i + 1], __fmul_rn(e2m1_value(b >> 4), sv));
-    }
-    *reinterpret_cast<uint4 *>(q + t * q_stride) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-    s[t * s_stride] = static_cast<uint8_t>(c);
+    const uint32_t nib = e2m1x2(__fmul_rn(r, mx_inverse(c)), 0.0f) & 15u;
+    r = __fsub_rn(r, __fmul_rn(e2m1_value(nib), mx_scale_value(c)));
+    const uint32_t hi = __shfl_down_sync(0xffffffffu, nib, 1);
+    if ((lane & 1) == 0) q[t * q_stride + (lane >> 1)] = static_cast<uint8_t>(nib | (hi << 4));
+    if (lane == 0) s[t * s_stride] = static_cast<uint8_t>(c);
   }
 }
 
-// NVFP4 terms of 16 fp32 values (one block) under the global scale gs: term t
-// is the NVFP4 quantization of the residual left by terms 0..t-1 (E4M3 scale
-// sf = nv4_scale_code(amax, gs), codes e2m1(r * gs / sf) RN saturating,
-// residual r -= (e2m1 * sf) * inv_gs). Writes 8 bytes of codes per term at
-// q + t * q_stride and the scale byte at s + t * s_stride.
-__device__ __forceinline__ void quantize_block16_nvfp4(const float *v, int terms, float gs, float inv_gs,
-                                                       uint8_t *q, size_t q_stride, uint8_t *s,
-                                                       size_t s_stride) {
-  float r[16];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) r[i] = v[i];
+__device__ __forceinline__ void quantize_block16x2_nvfp4_warp(float r, int terms, float gs, float inv_gs,
+                                                              uint8_t *q, size_t q_stride, uint8_t *s,
+                                                              size_t s_stride) {
+  const int lane = threadIdx.x & 31;
   for (int t = 0; t < terms; ++t) {
-    float amax = 0.0f;
+    uint32_t m = amax_key(r);
 #pragma unroll
-    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(r[i]));
-    const uint32_t c = nv4_scale_code(amax, gs);
-    const float sv = e4m3_value(static_cast<uint8_t>(c));
-    const float f = nv4_multiplier(sv, gs);
-    uint32_t packed[2] = {0u, 0u};
-#pragma unroll
-    for (int i = 0; i < 16; i += 2) {
-      const uint32_t b = e2m1x2(__fmul_rn(r[i], f), __fmul_rn(r[i + 1], f));
-      packed[i >> 3] |= b << (8 * ((i >> 1) & 3));
-      r[i] = __fsub_rn(r[i], __fmul_rn(__fmul_rn(e2m1_value(b & 15u), sv), inv_gs));
-      r[i + 1] = __fsub_rn(r[i + 1], __fmul_rn(__fmul_rn(e2m1_value(b >> 4), sv), inv_gs));
+    for (int off = 8; off >= 1; off >>= 1) {
+      const uint32_t o = __shfl_xor_sync(0xffffffffu, m, off);
+      m = o > m ? o : m;
     }
-    *reinterpret_cast<uint2 *>(q + t * q_stride) = make_uint2(packed[0], packed[1]);
-    s[t * s_stride] = static_cast<uint8_t>(c);
+    const uint32_t c = nv4_scale_code(__uint_as_float(m), gs);
+    const float sv = e4m3_value(static_cast<uint8_t>(c));
+    const uint32_t nib = e2m1x2(__fmul_rn(r, nv4_multiplier(sv, gs)), 0.0f) & 15u;
+    r = __fsub_rn(r, __fmul_rn(__fmul_rn(e2m1_value(nib), sv), inv_gs));
+    const uint32_t hi = __shfl_down_sync(0xffffffffu, nib, 1);
+    if ((lane & 1) == 0) q[t * q_stride + (lane >> 1)] = static_cast<uint8_t>(nib | (hi << 4));
+    if ((lane & 15) == 0) s[t * s_stride + (lane >> 4)] = static_cast<uint8_t>(c);
   }
 }
 
@@ -203,10 +203,13 @@ inline size_t route_smem_size(int tokens, int experts) {
 }
 
 // kernels (definitions in mm_route.cu, mm_experts.cu, mm_finalize.cu)
-__global__ void router_quant_kernel(RouterArgs a);
+__global__ void router_kernel(RouterArgs a);
 __global__ void gate_topk_kernel(GateArgs g);
 __global__ void route_kernel(RouteArgs r);
 __global__ void front_kernel(FrontArgs f);
+// the same two launches with the DeepSeek-V4.1 gate's numerics (mm_gate_dsv41.cu)
+__global__ void gate_topk_dsv41_kernel(GateArgs g);
+__global__ void front_dsv41_kernel(FrontArgs f);
 // The expert kernel of format fmt (kFmtMx / kFmtNv): the dynamic shared memory
 // attribute (once per process and format) and a launch of `ctas` CTAs.
 // Defined beside the kernel template, whose instantiations stay in that file.

@@ -52,7 +52,21 @@ constexpr int kCtrlSegments = 0;  // number of segments
 constexpr int kCtrlUnits = 1;     // gate_up units + down units
 constexpr int kCtrlClaim = 2;     // units claimed after the first wave (reset to 0 by the front kernel)
 constexpr int kCtrlTicket = 3;    // front kernel's last-CTA ticket (reset by the last CTA)
+constexpr int kCtrlSplit = 4;     // K chunks per gate_up tile (split-K), chosen by the front kernel
 constexpr int kCtrlWords = 8;
+
+// Split-K of the gate_up units. When a step's gate_up tiles (segments x I/64)
+// number fewer than the expert grid, each tile's K (H) is cut into `split`
+// chunks of at least two stages, one unit each, so that every CTA streams
+// weights from the first wave: split = min(kMaxSplit, grid / tiles, ks1 / 2).
+// A chunk's epilogue warps store their fp32 partial sums (terms added) to a
+// slot of their own, kPartFloats per chunk ([segment row j][tile row]); the last
+// of the 2 x split warps covering one half of the tile's features (its gate
+// rows and the matching up rows), counted per (tile, half), adds the chunks'
+// partials in chunk order and runs the SwiGLU epilogue. Chunk units number at
+// most the grid, so the partial slots are indexed by the unit id.
+constexpr int kMaxSplit = 8;
+constexpr int kPartFloats = kSegRows * 128;
 
 // ---- the persistent expert kernel's shared memory -----------------------------------
 // Weights and activations are both packed E2M1 (two codes per byte) with a block

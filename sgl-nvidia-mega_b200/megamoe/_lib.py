@@ -25,7 +25,9 @@ MM_IPC_HANDLE_BYTES = 64
 MM_SCORE_SIGMOID = 0
 MM_SCORE_SOFTMAX = 1
 MM_SCORE_SQRTSOFTPLUS = 2
-SCORES = {"sigmoid": MM_SCORE_SIGMOID, "softmax": MM_SCORE_SOFTMAX, "sqrtsoftplus": MM_SCORE_SQRTSOFTPLUS}
+MM_SCORE_SQRTSOFTPLUS_DSV41 = 3
+SCORES = {"sigmoid": MM_SCORE_SIGMOID, "softmax": MM_SCORE_SOFTMAX, "sqrtsoftplus": MM_SCORE_SQRTSOFTPLUS,
+          "sqrtsoftplus_dsv41": MM_SCORE_SQRTSOFTPLUS_DSV41}
 
 MM_RENORM_NONE = 0
 MM_RENORM_SUM = 1

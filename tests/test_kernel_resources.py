@@ -19,8 +19,9 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 
 def _ptxas_info(source):
-    res = subprocess.run([NVCC, "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++17",
-                          "-I", os.path.join(REPO, "include"), "-I", CSRC, "-Xptxas", "-v", "-c",
+    from megamoe import _build
+
+    res = subprocess.run([NVCC, *_build.compile_flags(source), "-Xptxas", "-v", "-c",
                           os.path.join(CSRC, source), "-o", os.devnull], capture_output=True, text=True, timeout=300)
     assert res.returncode == 0, res.stderr[-2000:]
     kernels, current = {}, None
@@ -45,7 +46,7 @@ ALLOWED_SPILL = {"_ZN2mm25finalize_allreduce_kernelILb1EEEvNS_8CommArgsE": 8}
 
 
 @pytest.mark.skipif(not os.path.exists(NVCC) and shutil.which("nvcc") is None, reason="nvcc not found")
-@pytest.mark.parametrize("source", ["mm_experts.cu", "mm_route.cu", "mm_finalize.cu", "mm_comm.cu"])
+@pytest.mark.parametrize("source", ["mm_experts.cu", "mm_route.cu", "mm_gate_dsv41.cu", "mm_finalize.cu", "mm_comm.cu"])
 def test_no_kernel_spills(source):
     kernels = _ptxas_info(source)
     assert kernels, "ptxas reported no kernels"

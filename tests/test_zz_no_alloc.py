@@ -1,11 +1,11 @@
 """The allocation-free router top-k + route record (mm_gate_route_noalloc)
 against the allocating path (mm_gate_topk, then mm_route), through the C ABI.
 
-mm_gate_route_noalloc serves callers that cannot call cudaMalloc: code that runs
-while a CUDA graph is being captured, or inside a serving runtime whose memory
-pool owns the device and hands it only input and output buffers. Its scratch (a
-ticket and the staged top-k ids) is a static device array of the library instead
-of memory from mm_layer_create. It must give the same ids, weights, slot -> row
+mm_gate_route_noalloc serves callers that cannot call cudaMalloc: a serving
+runtime that reserves the GPU's memory for its own pool at start-up, or plugin
+code handed only its input and output pointers. Its scratch (a ticket and the
+staged top-k ids) is a static device array of the library instead of memory
+from mm_layer_create. It must give the same ids, weights, slot -> row
 map and route record bit for bit, including on consecutive calls that reuse the
 shared scratch, and reject requests larger than that scratch."""
 
