@@ -623,17 +623,19 @@ static int run_front_and_experts(mm_layer *L, const uint16_t *x, const mm_gate_a
   q.gs = L->gs1;
   q.inv_gs = L->fmt == kFmtNv ? L->d.input_scale[0] : 1.0f;
   q.ctas = std::min((tokens * (L->H / 32) + 15) / 16, 2 * L->num_sms);
+  f.row_ctas = gate ? tokens : 1;
   MM_CUDA(cudaSetDevice(L->d.device));
   if (gate != nullptr && gate->score_func == MM_SCORE_SQRTSOFTPLUS_DSV41) {
     // the DeepSeek-V4.1 gate's launch is compiled with flush-to-zero: the routed
     // input's quantization runs in a front_kernel launch of its own (no rows) first
     FrontArgs qf = {};
     qf.quant = q;
+    qf.row_ctas = 0;
     MM_CUDA(launch(front_kernel, dim3(q.ctas), dim3(512), 0, stream, qf));
     f.quant.ctas = 0;
-    MM_CUDA(launch(front_dsv41_kernel, dim3(tokens), dim3(512), route_smem_bytes(tokens, L->E), stream, f));
+    MM_CUDA(launch(front_dsv41_kernel, dim3(f.row_ctas), dim3(512), route_smem_bytes(tokens, L->E), stream, f));
   } else {
-    MM_CUDA(launch(front_kernel, dim3(tokens + q.ctas), dim3(512), route_smem_bytes(tokens, L->E), stream, f));
+    MM_CUDA(launch(front_kernel, dim3(f.row_ctas + q.ctas), dim3(512), route_smem_bytes(tokens, L->E), stream, f));
   }
   ExpertArgs ea = L->ea;
   ea.rows_out = rows;

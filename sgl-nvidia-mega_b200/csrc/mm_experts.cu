@@ -559,10 +559,11 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
     uint32_t ws = 0, wphase = 0, acc = 0, acc_phase = 0, ex_phase = 0;
     SegCache seg_cache;
     // SwiGLU (+ clamp) of the 32 features f = 64 m + 32 fq + lane of segment sg's
-    // rows (get(j, gate, up) gives row j's accumulator sums), requantized into
-    // h's FP4 terms, then this warp's increment of the segment's mailbox (two
-    // per gate_up tile)
-    auto swiglu_publish = [&](const int4 &sg, int seg, int m, int fq, auto &&get) {
+    // rows (gate gv, up uv), requantized into h's FP4 terms, then this warp's
+    // increment of the segment's mailbox (two per gate_up tile). One call site:
+    // the split-K and the whole-tile paths both end here.
+    auto swiglu_publish = [&](const int4 &sg, int seg, int m, int fq, const float (&gv)[kSegRows],
+                              const float (&uv)[kSegRows]) {
       const int rows = sg.z;
       const float *lim = sg.x < 0 ? p.shared_clamp : p.clamp;
       const bool clamped = lim != nullptr;
@@ -574,8 +575,8 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
 #pragma unroll
       for (int j = 0; j < kSegRows; ++j) {
         if (j >= rows) break;
-        float g, up;
-        get(j, g, up);
+        float g = gv[j];
+        float up = uv[j];
         if (clamped) {
           up = fminf(fmaxf(up, -limit), limit);
           g = fminf(g, limit);
@@ -670,41 +671,51 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
             for (int j = 0; j < kSegRows; ++j) v[j] = __fmul_rn(v[j], al);
           }
         }
-        if (chunked) {
-          // split-K chunk: this warp's rows of the chunk's partial sums go to the
-          // chunk's slot; the warp then counts in for its half of the tile's
-          // features (gate rows 32 fq + lane, up rows 64 + 32 fq + lane)
-          const int tile = u / split;
-          const int fq = q & 1;
-          float *mine = p.part + static_cast<size_t>(u) * kPartFloats + row;
+        if (!g2) {
+          // gate_up: v becomes the gate and upv the up sums of features
+          // 64 m + 32 fq + lane, for the warp that runs the SwiGLU (fq its half)
+          float upv[kSegRows];
+          int fq = -1;
+          if (chunked) {
+            // split-K chunk: this warp's rows of the chunk's partial sums go to
+            // the chunk's slot; the warp then counts in for its half of the
+            // tile's features (gate rows 32 fq + lane, up rows 64 + 32 fq + lane)
+            const int tile = u / split;
+            float *mine = p.part + static_cast<size_t>(u) * kPartFloats + row;
 #pragma unroll
-          for (int j = 0; j < kSegRows; ++j)
-            if (j < rows) mine[j * 128] = v[j];
-          __threadfence();
-          __syncwarp();
-          int last = 0;
-          if (lane == 0) last = atomicAdd(p.split_cnt + 2 * tile + fq, 1) == 2 * split - 1 ? 1 : 0;
-          last = __shfl_sync(0xffffffffu, last, 0);
-          if (last) {
-            // the half's last warp: every chunk's partials, added in chunk order
+            for (int j = 0; j < kSegRows; ++j)
+              if (j < rows) mine[j * 128] = v[j];
             __threadfence();
-            const float *base = p.part + static_cast<size_t>(tile) * split * kPartFloats + 32 * fq + lane;
-            swiglu_publish(sg, seg, m, fq, [&](int j, float &g, float &up) {
-              g = __ldcg(base + j * 128);
-              up = __ldcg(base + j * 128 + 64);
-              for (int cc = 1; cc < split; ++cc) {
-                g = __fadd_rn(g, __ldcg(base + cc * kPartFloats + j * 128));
-                up = __fadd_rn(up, __ldcg(base + cc * kPartFloats + j * 128 + 64));
+            __syncwarp();
+            int last = 0;
+            if (lane == 0) last = atomicAdd(p.split_cnt + 2 * tile + (q & 1), 1) == 2 * split - 1 ? 1 : 0;
+            last = __shfl_sync(0xffffffffu, last, 0);
+            if (last) {
+              // the half's last warp: every chunk's partials, added in chunk order
+              __threadfence();
+              fq = q & 1;
+              const float *base = p.part + static_cast<size_t>(tile) * split * kPartFloats + 32 * fq + lane;
+#pragma unroll
+              for (int j = 0; j < kSegRows; ++j) {
+                float g = 0.0f, up = 0.0f;
+                if (j < rows) {
+                  g = __ldcg(base + j * 128);
+                  up = __ldcg(base + j * 128 + 64);
+                  for (int cc = 1; cc < split; ++cc) {
+                    g = __fadd_rn(g, __ldcg(base + cc * kPartFloats + j * 128));
+                    up = __fadd_rn(up, __ldcg(base + cc * kPartFloats + j * 128 + 64));
+                  }
+                  if constexpr (kNv) {
+                    g = __fmul_rn(g, al);
+                    up = __fmul_rn(up, al);
+                  }
+                }
+                v[j] = g;
+                upv[j] = up;
               }
-              if constexpr (kNv) {
-                g = __fmul_rn(g, al);
-                up = __fmul_rn(up, al);
-              }
-            });
-          }
-        } else if (!g2) {
-          // rows 0..63: gate of features 64m + row; rows 64..127: up of the same features
-          if (q >= 2) {
+            }
+          } else if (q >= 2) {
+            // rows 64..127 (up of features 64m + row - 64): to the gate-row warp
             if (lane == 0) ok = mbar_wait(bar(kBarExFree), ex_phase ^ 1u, err, kErrTimeoutAcc, wb) ? 1 : 0;
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
@@ -712,21 +723,20 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
             for (int j = 0; j < kSegRows; ++j) ex[(row - 64) * kSegRows + j] = v[j];
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(kBarExFull));
+            ex_phase ^= 1u;
           } else {
+            // rows 0..63: gate of features 64m + row, the up sums from the exchange
             if (lane == 0) ok = mbar_wait(bar(kBarExFull), ex_phase, err, kErrTimeoutAcc, wb) ? 1 : 0;
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
-            float upv[kSegRows];
 #pragma unroll
             for (int j = 0; j < kSegRows; ++j) upv[j] = ex[row * kSegRows + j];
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(kBarExFree));
-            swiglu_publish(sg, seg, m, q, [&](int j, float &g, float &up) {
-              g = v[j];
-              up = upv[j];
-            });
+            ex_phase ^= 1u;
+            fq = q;
           }
-          ex_phase ^= 1u;
+          if (fq >= 0) swiglu_publish(sg, seg, m, fq, v, upv);
         } else {
           // features 128 (m tg2 + tt) + row of the segment's rows, bf16
           const size_t col = static_cast<size_t>(128 * (m * kTg2 + tt) + row);

@@ -139,7 +139,8 @@ __device__ void gate_row(const GateArgs &g, int row, int valid_rows, GateSmem &s
 // ============================================================================
 inline __device__ void block_exclusive_scan_512(int *vals /*[1024] pairs*/, int n, int *warp_tot,
                                          int &total) {
-  // vals[0..n) in place -> exclusive prefix; n <= 1024; each thread two entries
+  // vals[0..n) in place -> exclusive prefix; n <= 1024; each thread two entries;
+  // every thread adds the warp totals before its warp itself (16 broadcast reads)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int a = 2 * tid < n ? vals[2 * tid] : 0;
   const int b = 2 * tid + 1 < n ? vals[2 * tid + 1] : 0;
@@ -152,18 +153,15 @@ inline __device__ void block_exclusive_scan_512(int *vals /*[1024] pairs*/, int 
   }
   if (lane == 31) warp_tot[warp] = inc;
   __syncthreads();
-  if (warp == 0) {
-    int t = lane < 16 ? warp_tot[lane] : 0;
+  int before = 0, all = 0;
 #pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      const int up = __shfl_up_sync(0xffffffffu, t, off);
-      if (lane >= off) t += up;
-    }
-    if (lane < 16) warp_tot[lane] = t;
+  for (int w = 0; w < 16; ++w) {
+    const int t = warp_tot[w];
+    before += w < warp ? t : 0;
+    all += t;
   }
-  __syncthreads();
-  const int base = inc - local + (warp > 0 ? warp_tot[warp - 1] : 0);
-  total = warp_tot[15];
+  const int base = inc - local + before;
+  total = all;
   if (2 * tid < n) vals[2 * tid] = base;
   if (2 * tid + 1 < n) vals[2 * tid + 1] = base + a;
   __syncthreads();
@@ -183,8 +181,6 @@ inline __device__ void build_route(const RouteArgs &r, unsigned char *smem_raw) 
   const int cw = route_cta_words(max_ctas);
   const int limit_off = 4 + cw, token_off = 4 + 2 * cw;
   const int rec_words = token_off + kTile * max_ctas;
-  for (int i = tid; i < E * words; i += blockDim.x) rowmask[i] = 0u;
-  for (int i = tid; i < rec_words; i += blockDim.x) r.record[i] = 0;
   // balanced dealing (route.cuh:39-46): a negative offset selects group
   // -1 - offset of two; ids are global, and of the step's distinct experts in
   // id order the k-th belongs to group k % 2
@@ -192,10 +188,13 @@ inline __device__ void build_route(const RouteArgs &r, unsigned char *smem_raw) 
   const int group = deal ? -1 - r.expert_offset : 0;
   const int offset = deal ? 0 : r.expert_offset;
   // this thread's slots s = tid + 512 i (the ids were written by other CTAs:
-  // L2); the local experts of the first two are kept for the second pass below
+  // L2, loaded before the zeroing below); the local experts of the first two are
+  // kept for the second pass
   const int e0 = tid < slots ? __ldcg(r.ids + tid) - offset : -1;
   const int e1 = tid + 512 < slots ? __ldcg(r.ids + tid + 512) - offset : -1;
   auto slot_expert = [&](int s) { return s == tid ? e0 : (s == tid + 512 ? e1 : __ldcg(r.ids + s) - offset); };
+  for (int i = tid; i < E * words; i += blockDim.x) rowmask[i] = 0u;
+  for (int i = tid; i < rec_words; i += blockDim.x) r.record[i] = 0;
   __syncthreads();
   for (int s = tid; s < slots; s += blockDim.x) {
     const int t = s / K;
@@ -275,11 +274,17 @@ inline __device__ void build_route(const RouteArgs &r, unsigned char *smem_raw) 
     const int nseg = shared_segs + total_segs;
     for (int j = tid; j < nseg; j += blockDim.x) r.flags[j] = 0;
     // split-K of the gate_up tiles when they are fewer than the expert grid
-    // (kMaxSplit in mm_layout.cuh)
+    // (kMaxSplit in mm_layout.cuh): as many chunks as leave every down unit a
+    // CTA of the first wave too (their weights stream while the gate_up chunks
+    // run), else as many as fill the grid
     const int tiles1 = nseg * r.m1;
+    const int units2 = nseg * r.m2;
     int split = 1;
-    if (r.split_cnt != nullptr && tiles1 > 0 && tiles1 < r.grid)
-      split = max(1, min(min(kMaxSplit, r.grid / tiles1), r.ks1 / 2));
+    if (r.split_cnt != nullptr && tiles1 > 0 && tiles1 < r.grid) {
+      split = (r.grid - units2) / tiles1;
+      if (split < 2) split = r.grid / tiles1;
+      split = max(1, min(min(kMaxSplit, split), r.ks1 / 2));
+    }
     if (split > 1)
       for (int j = tid; j < 2 * tiles1; j += blockDim.x) r.split_cnt[j] = 0;
     if (tid == 0) {
@@ -320,11 +325,12 @@ __device__ __forceinline__ void quantize_x(const QuantArgs &a, int cta) {
   }
 }
 
-// The front launch's body: grid = T row CTAs + f.quant.ctas, block 512. Each
-// row CTA ranks its row (or takes given ids); the last row CTA to finish builds
-// the route record and the work tables. The quantization CTAs (kQuant only)
-// write the routed input's FP4 terms meanwhile, after the grid-dependency wait
-// (the previous step's expert launch reads the same buffers); with T = 0 the
+// The front launch's body: grid = f.row_ctas row CTAs + f.quant.ctas, block
+// 512. With a gate each of the T row CTAs ranks its row and the last to finish
+// builds the route record and the work tables; with given ids (or one row) one
+// row CTA builds them at once. The quantization CTAs (kQuant only) write the
+// routed input's FP4 terms meanwhile, after the grid-dependency wait (the
+// previous step's expert launch reads the same buffers); with no row CTAs the
 // launch only quantizes. Dynamic shared memory: route_smem_size(T, experts).
 template <class N, bool kQuant>
 __device__ __forceinline__ void front_body(const FrontArgs &f, unsigned char *front_smem) {
@@ -332,8 +338,8 @@ __device__ __forceinline__ void front_body(const FrontArgs &f, unsigned char *fr
   __shared__ int is_last;
   pdl_wait();
   if constexpr (kQuant) {
-    if (static_cast<int>(blockIdx.x) >= f.route.tokens) {
-      quantize_x(f.quant, blockIdx.x - f.route.tokens);
+    if (static_cast<int>(blockIdx.x) >= f.row_ctas) {
+      quantize_x(f.quant, blockIdx.x - f.row_ctas);
       return;
     }
   }
@@ -342,11 +348,16 @@ __device__ __forceinline__ void front_body(const FrontArgs &f, unsigned char *fr
     const int valid = f.gate.num_valid != nullptr ? *f.gate.num_valid : f.route.tokens;
     gate_row<N>(f.gate, row, valid, gsm);
   }
+  if (f.row_ctas == 1) {  // one row, or given ids: this CTA builds the route, no ticket
+    __syncthreads();
+    build_route(f.route, front_smem);
+    return;
+  }
   __syncthreads();
   if (threadIdx.x == 0) {  // thread 0 (warp 0, lane 0) wrote the row's ids and weights
     __threadfence();
     const int ticket = atomicAdd(&f.route.ctrl[kCtrlTicket], 1);
-    is_last = ticket == f.route.tokens - 1;
+    is_last = ticket == f.row_ctas - 1;
   }
   __syncthreads();
   if (!is_last) return;

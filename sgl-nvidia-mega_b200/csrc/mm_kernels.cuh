@@ -61,6 +61,7 @@ struct FrontArgs {
   GateArgs gate;             // gate.logits null: ids are given in route.ids
   RouteArgs route;
   QuantArgs quant;
+  int row_ctas;              // T with a gate (one per row), 1 with given ids, 0: quantization only
 };
 
 constexpr int kMaxRouterParts = 14;  // H <= 14336 for the router GEMV (x tile in shared memory)

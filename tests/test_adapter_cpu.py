@@ -103,7 +103,7 @@ def test_gate_topk_and_gemms_with_the_reference_arguments(adapter):
     assert kind == "gate"
     assert args[0] is x_q and args[1] is x_s and args[2] is logits and args[3] is bias
     assert args[4:] == (1.5, nv, alt, 1e-20, ids_out, None, True)
-    assert kw == {"score": "sqrtsoftplus"}
+    assert kw == {"score": "sqrtsoftplus_dsv41"}  # top-6: the reference gate's own numerics
     # slot gate_route_quant: the bf16 input replaces x_q / x_s
     x = torch.zeros((T, H), dtype=torch.bfloat16)
     adapter.gate_topk_and_gemms(None, None, logits, bias, 1.5, None, x=x)
