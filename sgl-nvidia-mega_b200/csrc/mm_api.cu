@@ -111,6 +111,7 @@ struct mm_layer {
   uint8_t *xq = nullptr, *xs = nullptr, *hq = nullptr, *hs = nullptr;
   int4 *segs = nullptr;
   int *ctrl = nullptr, *flags = nullptr;
+  int *seg_tok = nullptr;    // [max_segs][kSegRows] segment row -> token
   float *part = nullptr;     // split-K partial sums [grid][kPartFloats]
   int *split_cnt = nullptr;  // split-K arrival counters [2 x grid]
   uint32_t *err = nullptr;
@@ -267,7 +268,7 @@ int mm_finalize_partial(const float *partial, uint16_t *out, int32_t tokens, int
 static void free_layer(mm_layer *L) {
   if (!L) return;
   void *ptrs[] = {L->sfa13, L->sfa2, L->ssfa13, L->ssfa2, L->xq, L->xs, L->hq, L->hs, L->segs,
-                  L->ctrl, L->flags, L->part, L->split_cnt, L->err, L->logits, L->weights, L->ids,
+                  L->ctrl, L->flags, L->seg_tok, L->part, L->split_cnt, L->err, L->logits, L->weights, L->ids,
                   L->permuted, L->record, L->alpha};
   for (void *p : ptrs)
     if (p) cudaFree(p);
@@ -397,6 +398,7 @@ int mm_layer_create(const mm_layer_desc *desc, mm_layer **out) {
   ALLOC(L->segs, sizeof(int4) * L->max_segs);
   ALLOC(L->ctrl, sizeof(int) * kCtrlWords);
   ALLOC(L->flags, sizeof(int) * L->max_segs);
+  ALLOC(L->seg_tok, sizeof(int) * kSegRows * L->max_segs);
   const size_t grid = static_cast<size_t>(kCtasPerSm) * L->num_sms;
   ALLOC(L->part, sizeof(float) * kPartFloats * grid);
   ALLOC(L->split_cnt, sizeof(int) * 2 * grid);
@@ -479,6 +481,7 @@ int mm_layer_create(const mm_layer_desc *desc, mm_layer **out) {
   ea.segs = L->segs;
   ea.ctrl = L->ctrl;
   ea.flags = L->flags;
+  ea.seg_tok = L->seg_tok;
   ea.part = L->part;
   ea.split_cnt = L->split_cnt;
   ea.err = L->err;
@@ -607,6 +610,7 @@ static int run_front_and_experts(mm_layer *L, const uint16_t *x, const mm_gate_a
   f.route.ks1 = L->ks1;
   f.route.grid = kCtasPerSm * L->num_sms;
   f.route.split_cnt = L->split_cnt;
+  f.route.seg_tok = L->seg_tok;
   // the routed input's FP4 terms: one 32-element chunk per warp and pass, at most
   // two quantization CTAs per SM
   QuantArgs &q = f.quant;
@@ -639,8 +643,6 @@ static int run_front_and_experts(mm_layer *L, const uint16_t *x, const mm_gate_a
   }
   ExpertArgs ea = L->ea;
   ea.rows_out = rows;
-  ea.record = record;
-  ea.token_off = 4 + 2 * route_cta_words(route_max_ctas(tokens, L->K, L->E));
   MM_CUDA(launch_experts(L, ea, stream));
   return MM_OK;
 }
@@ -682,8 +684,6 @@ int mm_layer_rerun_experts(mm_layer *L, int32_t tokens, const int32_t *record, u
   MM_CUDA(cudaSetDevice(L->d.device));
   ExpertArgs ea = L->ea;
   ea.rows_out = rows;
-  ea.record = record;
-  ea.token_off = 4 + 2 * route_cta_words(route_max_ctas(tokens, L->K, L->E));
   MM_CUDA(launch_experts(L, ea, stream));
   return MM_OK;
 }

@@ -472,16 +472,16 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
       if (seg != share_seg || g2 != share_g2) {
         share_seg = seg;
         share_g2 = g2;
+        // a gate_up unit's x rows are its segment's tokens: the list is loaded
+        // beside the segment descriptor (one L2 round trip for both)
+        const int tok = !g2 && lane < kSegRows ? __ldcg(p.seg_tok + seg * kSegRows + lane) : 0;
         const int4 sg = seg_cache.get(p.segs, seg);
         const int rows = sg.z;
         const int n = (rows + 7) & ~7;
         nb = n * p.terms;  // B rows of this unit
         // source row of segment row `lane` (lanes >= rows: row 0, never read)
         int src = 0;
-        if (lane < rows) {
-          if (g2) src = sg.y + lane;
-          else src = sg.w >= 0 ? sg.w + lane : __ldg(p.record + p.token_off + sg.y + lane);
-        }
+        if (lane < rows) src = g2 ? sg.y + lane : tok;
         const int K = g2 ? p.inter : p.hidden;
         dq = g2 ? p.hq : p.xq;
         dsc = g2 ? p.hs : p.xs;

@@ -34,12 +34,44 @@ __device__ __forceinline__ unsigned long long pack_key(uint32_t key, int e) {
   return (static_cast<unsigned long long>(key) << 32) | static_cast<uint32_t>(0xffffffffu - e);
 }
 
+// The merge of warp 0: the 16 warps' K candidates each, packed densely (flat
+// index w K + k; lane l holds l, l + 32, ...; a candidate is key + 1 and
+// expert id, key 0: empty or taken). Each round takes the largest key by a
+// warp reduction, then the lowest expert id among its holders by a second one
+// -- the same pick as the largest packed (key, ~id) -- into sm.sel[k].
+template <int kPer>
+__device__ __forceinline__ void merge_candidates(GateSmem &sm, int K, int lane) {
+  uint32_t ckey[kPer], cid[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int f = lane + 32 * j;
+    const unsigned long long c = f < 16 * K ? sm.cand[f / K][f % K] : 0ull;
+    ckey[j] = c == 0ull ? 0u : static_cast<uint32_t>(c >> 32) + 1u;
+    cid[j] = 0xffffffffu - static_cast<uint32_t>(c);
+  }
+  for (int k = 0; k < K; ++k) {
+    uint32_t lm = 0u;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) lm = ckey[j] > lm ? ckey[j] : lm;
+    const uint32_t m = __reduce_max_sync(0xffffffffu, lm);
+    uint32_t lid = 0xffffffffu;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) lid = (m != 0u && ckey[j] == m && cid[j] < lid) ? cid[j] : lid;
+    const uint32_t wid = __reduce_min_sync(0xffffffffu, lid);
+#pragma unroll
+    for (int j = 0; j < kPer; ++j)
+      if (ckey[j] == m && cid[j] == wid) ckey[j] = 0u;
+    if (lane == 0) sm.sel[k] = static_cast<int>(wid);  // 0xffffffff (-1) when nothing is left
+  }
+}
+
 // Computes ids/weights of row `row` and writes them to ids_out/weights_out.
 // N is the routing numerics: N::score(g, logit) the unbiased score,
 // N::key(score, bias) its order-preserving ranking key (larger ranks first; at
-// most 0xff800000), N::weights(g, sm, w) the K routing weights of the selected
-// experts sm.sel[0..K) from sm.score / sm.logit. Selection is the same for all:
-// the K largest keys, the lowest expert id winning a tie.
+// most 0xff800000), N::weight(g, sm, k) the routing weight of the k-th selected
+// expert sm.sel[k] from sm.score / sm.logit (lane k of warp 0 computes it; every
+// lane evaluates the row's sum in the same order). Selection is the same for
+// all: the K largest keys, the lowest expert id winning a tie.
 template <class N>
 __device__ void gate_row(const GateArgs &g, int row, int valid_rows, GateSmem &sm) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -91,44 +123,14 @@ __device__ void gate_row(const GateArgs &g, int row, int valid_rows, GateSmem &s
   }
   __syncthreads();
   if (warp == 0) {
-    // merge 16 warps x K candidates: lane l holds warps' entries l, l+32, ...
-    // (a candidate is key + 1 and expert id; key 0: empty or taken). Each
-    // round: the largest key by a warp reduction, then the lowest expert id
-    // among its holders by a second one -- the same pick as the largest
-    // packed (key, ~id).
-    constexpr int kPer = 16 * kMaxTopK / 32;
-    uint32_t ckey[kPer], cid[kPer];
-#pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-      const int idx = lane + 32 * j;  // idx = warp_id * kMaxTopK + k
-      const int cw = idx / kMaxTopK, ck = idx % kMaxTopK;
-      const unsigned long long c = (ck < K) ? sm.cand[cw][ck] : 0ull;
-      ckey[j] = c == 0ull ? 0u : static_cast<uint32_t>(c >> 32) + 1u;
-      cid[j] = 0xffffffffu - static_cast<uint32_t>(c);
-    }
-    for (int k = 0; k < K; ++k) {
-      uint32_t lm = 0u;
-#pragma unroll
-      for (int j = 0; j < kPer; ++j) lm = ckey[j] > lm ? ckey[j] : lm;
-      const uint32_t m = __reduce_max_sync(0xffffffffu, lm);
-      uint32_t lid = 0xffffffffu;
-#pragma unroll
-      for (int j = 0; j < kPer; ++j) lid = (m != 0u && ckey[j] == m && cid[j] < lid) ? cid[j] : lid;
-      const uint32_t wid = __reduce_min_sync(0xffffffffu, lid);
-#pragma unroll
-      for (int j = 0; j < kPer; ++j)
-        if (ckey[j] == m && cid[j] == wid) ckey[j] = 0u;
-      if (lane == 0) sm.sel[k] = static_cast<int>(wid);  // 0xffffffff (-1) when nothing is left
-    }
+    if (K <= 8) merge_candidates<4>(sm, K, lane);
+    else merge_candidates<8>(sm, K, lane);
     __syncwarp();
-    if (lane == 0) {
+    if (lane < K) {  // lane k: slot k's id and weight
       const bool valid = row < valid_rows;
-      float w[kMaxTopK];
-      N::weights(g, sm, w);
-      for (int k = 0; k < K; ++k) {
-        g.ids_out[static_cast<size_t>(row) * K + k] = valid ? sm.sel[k] : -1;
-        g.weights_out[static_cast<size_t>(row) * K + k] = valid ? w[k] : 0.0f;
-      }
+      const float wk = N::weight(g, sm, lane);
+      g.ids_out[static_cast<size_t>(row) * K + lane] = valid ? sm.sel[lane] : -1;
+      g.weights_out[static_cast<size_t>(row) * K + lane] = valid ? wk : 0.0f;
     }
   }
 }
@@ -231,6 +233,8 @@ inline __device__ void build_route(const RouteArgs &r, unsigned char *smem_raw) 
   }
   __syncthreads();
   const int total_ctas = packed_total & 0xffff, total_segs = packed_total >> 16;
+  // the expert kernel's segment table lists the shared expert's segments first
+  const int shared_segs = r.segs != nullptr && r.has_shared ? (T + kSegRows - 1) / kSegRows : 0;
   if (tid == 0) {
     r.record[0] = total_ctas * kTile;
     r.record[1] = total_ctas;
@@ -249,6 +253,8 @@ inline __device__ void build_route(const RouteArgs &r, unsigned char *smem_raw) 
     const int base_row = first[e] * kTile;
     r.permuted[s] = base_row + rank;
     r.record[token_off + base_row + rank] = t;
+    if (r.segs != nullptr)  // the token of the row in its segment's list
+      r.seg_tok[(shared_segs + seg_first[e] + rank / kSegRows) * kSegRows + rank % kSegRows] = t;
     if (rank % kTile == 0) {
       const int cta = first[e] + rank / kTile;
       r.record[4 + cta] = e;
@@ -257,11 +263,11 @@ inline __device__ void build_route(const RouteArgs &r, unsigned char *smem_raw) 
   }
   // expert-kernel work tables (shared expert's segments first)
   if (r.segs != nullptr) {
-    const int shared_segs = r.has_shared ? (T + kSegRows - 1) / kSegRows : 0;
     for (int j = tid; j < shared_segs; j += blockDim.x) {
       const int rows = min(kSegRows, T - j * kSegRows);
       r.segs[j] = make_int4(-1, r.shared_row_base + j * kSegRows, rows, j * kSegRows);
     }
+    for (int i = tid; i < shared_segs * kSegRows; i += blockDim.x) r.seg_tok[i] = i;  // the shared expert's rows: tokens in order
     for (int e = tid; e < E; e += blockDim.x) {
       const int c = counts[e];
       const int nseg = (c + kSegRows - 1) / kSegRows;

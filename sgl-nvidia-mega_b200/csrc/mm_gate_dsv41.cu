@@ -49,13 +49,15 @@ struct Dsv41Routing {
     const uint32_t bits = __float_as_uint(v);
     return (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);
   }
-  static __device__ __forceinline__ void weights(const GateArgs &g, const GateSmem &sm, float (&w)[kMaxTopK]) {
+  static __device__ __forceinline__ float weight(const GateArgs &g, const GateSmem &sm, int k) {
     const int K = g.top_k;  // 3 or 6 (the host checks)
-    for (int k = 0; k < K; ++k) w[k] = sm.score[sm.sel[k]];
+    float w[6];
+#pragma unroll
+    for (int i = 0; i < 6; ++i) w[i] = i < K ? sm.score[sm.sel[i]] : 0.0f;
     const float sum = K == 6 ? ((w[0] + w[2]) + (w[1] + w[3])) + (w[4] + w[5]) : (w[0] + w[2]) + w[1];
     const float eps = g.renorm_eps;
     const float norm = eps > 0.0f ? sum + eps : (sum > 0.0f ? sum : 1.0f);
-    for (int k = 0; k < K; ++k) w[k] = div_full(w[k], norm) * g.routed_scaling;
+    return div_full(sm.score[sm.sel[k]], norm) * g.routed_scaling;
   }
 };
 

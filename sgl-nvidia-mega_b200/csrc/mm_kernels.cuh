@@ -42,6 +42,7 @@ struct RouteArgs {
   int ks1;                   // K stages of a gate_up tile
   int grid;                  // the expert kernel's CTAs (the split-K choice)
   int *split_cnt;            // [2 x grid] split-K arrival counters, zeroed when split > 1
+  int *seg_tok;              // [segments][kSegRows] the token of each segment row
 };
 
 // The routed input's quantization into FP4 terms (extra CTAs of the front launch).
@@ -95,7 +96,7 @@ struct alignas(64) ExpertArgs {
   const float *salpha2;      // [1]
   float gs2, inv_gs2;        // 1 / input_scale[1] and input_scale[1]
   uint16_t *rows_out;        // [rows_cap][H] bf16
-  const int *record;
+  const int *seg_tok;        // [segments][kSegRows] the token of each segment row
   const int4 *segs;
   int *ctrl;
   int *flags;
@@ -104,7 +105,7 @@ struct alignas(64) ExpertArgs {
   uint32_t *err;
   const float *clamp;        // [E] or null
   const float *shared_clamp; // [1] or null
-  int hidden, inter, max_tokens, rows_cap, terms, token_off;
+  int hidden, inter, max_tokens, rows_cap, terms;
   int hq_row, hs_row;        // bytes per h row / h scale row: I rounded up to 256 features, zero past I
   int m1, m2, ks1, ks2;      // gate_up units / down tiles per segment; K stages of each
   int tg2, u2;               // down tiles per down unit; down units per segment (ceil(m2 / tg2))

@@ -44,7 +44,7 @@ struct Segment {   // int4 in memory
   int expert;      // local expert index, -1 for the shared expert
   int row_base;    // first permuted row (rows_out / hq row)
   int rows;        // 1..kSegRows
-  int token_base;  // shared expert: token of row_base; routed: -1 (tokens from the record)
+  int token_base;  // shared expert: token of row_base; routed: -1 (each row's token: the segment's token list)
 };
 
 // ctrl words

@@ -147,47 +147,45 @@ struct IeeeRouting {
     return l;  // softmax: rank the (biased) logits
   }
   static __device__ __forceinline__ uint32_t key(float s, float b) { return routing_key(__fadd_rn(s, b)); }
-  static __device__ __forceinline__ void weights(const GateArgs &g, const GateSmem &sm, float (&w)[kMaxTopK]) {
+  // the weight of selected slot k; the row's sum is evaluated the same way, in
+  // the same order, by every lane that calls this
+  static __device__ __forceinline__ float weight(const GateArgs &g, const GateSmem &sm, int k) {
     const int K = g.top_k;
     if (g.score_func == MM_SCORE_SOFTMAX) {
       float m = sm.logit[sm.sel[0]];
-      for (int k = 1; k < K; ++k) m = fmaxf(m, sm.logit[sm.sel[k]]);
-      float sum = 0.0f;
-      for (int k = 0; k < K; ++k) {
-        w[k] = det_exp(__fsub_rn(sm.logit[sm.sel[k]], m));
-        sum = __fadd_rn(sum, w[k]);
+      for (int i = 1; i < K; ++i) m = fmaxf(m, sm.logit[sm.sel[i]]);
+      float sum = 0.0f, mine = 0.0f;
+      for (int i = 0; i < K; ++i) {
+        const float e = det_exp(__fsub_rn(sm.logit[sm.sel[i]], m));
+        sum = __fadd_rn(sum, e);
+        if (i == k) mine = e;
       }
-      for (int k = 0; k < K; ++k) w[k] = __fmul_rn(__fdiv_rn(w[k], sum), g.routed_scaling);
-    } else {
-      float sum = 0.0f;
-      for (int k = 0; k < K; ++k) {
-        w[k] = sm.score[sm.sel[k]];
-        sum = __fadd_rn(sum, w[k]);
-      }
-      if (g.renormalize == MM_RENORM_SCALED_BF16) {
-        // GLM-5.3's rule (glm5_3/sm103/moe/routing.py:3-11, ptx_tc.py routing_weight):
-        // the selected scores summed in the order of a warp xor-butterfly whose
-        // lane k holds slot k (the halving [i] += [i + off], off = 8, 4, 2, 1, is
-        // lane 0's order), then w = bf16(scale * s / (sum + eps)), scale first;
-        // IEEE division where the reference divides approximately
-        float t[kMaxTopK];
-#pragma unroll
-        for (int k = 0; k < kMaxTopK; ++k) t[k] = k < K ? w[k] : 0.0f;
-#pragma unroll
-        for (int off = kMaxTopK / 2; off >= 1; off >>= 1)
-#pragma unroll
-          for (int i = 0; i < off; ++i) t[i] = __fadd_rn(t[i], t[i + off]);
-        const float d = __fadd_rn(t[0], g.renorm_eps);
-        for (int k = 0; k < K; ++k)
-          w[k] = bf16_bits_to_float(float_to_bf16_bits(__fdiv_rn(__fmul_rn(g.routed_scaling, w[k]), d)));
-      } else if (g.renormalize) {
-        const float norm = g.renorm_eps > 0.0f ? __fadd_rn(sum, g.renorm_eps)
-                                               : (sum > 0.0f ? sum : 1.0f);
-        for (int k = 0; k < K; ++k) w[k] = __fmul_rn(__fdiv_rn(w[k], norm), g.routed_scaling);
-      } else {
-        for (int k = 0; k < K; ++k) w[k] = __fmul_rn(w[k], g.routed_scaling);
-      }
+      return __fmul_rn(__fdiv_rn(mine, sum), g.routed_scaling);
     }
+    const float mine = sm.score[sm.sel[k]];
+    if (g.renormalize == MM_RENORM_SCALED_BF16) {
+      // GLM-5.3's rule (glm5_3/sm103/moe/routing.py:3-11, ptx_tc.py routing_weight):
+      // the selected scores summed in the order of a warp xor-butterfly whose
+      // lane k holds slot k (the halving [i] += [i + off], off = 8, 4, 2, 1, is
+      // lane 0's order), then w = bf16(scale * s / (sum + eps)), scale first;
+      // IEEE division where the reference divides approximately
+      float t[kMaxTopK];
+#pragma unroll
+      for (int i = 0; i < kMaxTopK; ++i) t[i] = i < K ? sm.score[sm.sel[i]] : 0.0f;
+#pragma unroll
+      for (int off = kMaxTopK / 2; off >= 1; off >>= 1)
+#pragma unroll
+        for (int i = 0; i < off; ++i) t[i] = __fadd_rn(t[i], t[i + off]);
+      const float d = __fadd_rn(t[0], g.renorm_eps);
+      return bf16_bits_to_float(float_to_bf16_bits(__fdiv_rn(__fmul_rn(g.routed_scaling, mine), d)));
+    }
+    if (g.renormalize) {
+      float sum = 0.0f;
+      for (int i = 0; i < K; ++i) sum = __fadd_rn(sum, sm.score[sm.sel[i]]);
+      const float norm = g.renorm_eps > 0.0f ? __fadd_rn(sum, g.renorm_eps) : (sum > 0.0f ? sum : 1.0f);
+      return __fmul_rn(__fdiv_rn(mine, norm), g.routed_scaling);
+    }
+    return __fmul_rn(mine, g.routed_scaling);
   }
 };
 
