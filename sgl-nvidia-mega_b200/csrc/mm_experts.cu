@@ -298,7 +298,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
             b_end = b_next + batch;
             b_claimed = true;
           }
-          if (!mbar_wait(bar(kBarEmpty + stage), phase ^ 1u, err, kErrTimeoutEmpty, wb)) {
+          if (filled >= kStages && !mbar_wait(bar(kBarEmpty + stage), phase ^ 1u, err, kErrTimeoutEmpty, wb)) {
             ok = false;
             break;
           }
@@ -444,6 +444,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
     uint32_t s_base[2];  // scale bytes of B rows lane and lane + 32 at stage 0 (chunk c: + 4 c)
     uint32_t pmask = 0, smask = 0;  // bit i: piece i / scale row half i holds a segment row (else zero-fill)
     int nb = 0;
+    int fills = 0;  // stages filled, counted up to kStages
     const uint8_t *dq = nullptr, *dsc = nullptr;
 #pragma unroll 1
     while (true) {
@@ -477,7 +478,8 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
         const int tok = !g2 && lane < kSegRows ? __ldcg(p.seg_tok + seg * kSegRows + lane) : 0;
         const int4 sg = seg_cache.get(p.segs, seg);
         const int rows = sg.z;
-        const int n = (rows + 7) & ~7;
+        const int n = (rows + 7) & ~7;  // 8 or 16 (rows <= kSegRows)
+        const int nsh = n == 8 ? 3 : 4;
         nb = n * p.terms;  // B rows of this unit
         // source row of segment row `lane` (lanes >= rows: row 0, never read)
         int src = 0;
@@ -491,23 +493,30 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
         const uint32_t term_q = static_cast<uint32_t>(g2 ? p.rows_cap : p.max_tokens) * rowb;
         const uint32_t srow = g2 ? static_cast<uint32_t>(p.hs_row) : static_cast<uint32_t>(K / L::kBlock);
         const uint32_t term_s = static_cast<uint32_t>(g2 ? p.rows_cap : p.max_tokens) * srow;
+        // piece i's segment row (quarter + 4 i) & (n - 1) is quarter + 4 (i % (n / 4)):
+        // a lane reads two source rows (n = 8) or four (n = 16)
+        int src_q[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) src_q[j] = __shfl_sync(0xffffffffu, src, quarter + 4 * j);
 #pragma unroll
         for (int i = 0; i < kPieces; ++i) {
           const int rr = quarter + 4 * i;
-          const int t = rr / n;
-          const int r = rr - t * n;
-          const int sr = __shfl_sync(0xffffffffu, src, r & 31);
+          const int t = rr >> nsh;
+          const int r = rr & (n - 1);
+          const int sr = n == 8 ? src_q[i & 1] : src_q[i & 3];
           soff[i] = static_cast<uint32_t>(t) * term_q + static_cast<uint32_t>(sr) * rowb + pc * 16;
           doff[i] = (rr >> 3) * 1024 + (rr & 7) * 128 + ((pc ^ (rr & 7)) << 4);
           pmask = (rr < nb && r < rows) ? (pmask | (1u << i)) : (pmask & ~(1u << i));
         }
-        // scale pieces: B rows rr = lane and lane + 32, every chunk of the stage
+        // scale pieces: B rows rr = lane and lane + 32 (segment row lane % n for
+        // both), every chunk of the stage
+        const int s_src = __shfl_sync(0xffffffffu, src, lane & (n - 1));
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           const int rr = lane + 32 * h;
-          const int t = rr / n;
-          const int r = rr - t * n;
-          const int sr = __shfl_sync(0xffffffffu, src, r & 31);
+          const int t = rr >> nsh;
+          const int r = rr & (n - 1);
+          const int sr = s_src;
           s_base[h] = static_cast<uint32_t>(t) * term_s + static_cast<uint32_t>(sr) * srow;
           smask = (rr < nb && r < rows) ? (smask | (1u << h)) : (smask & ~(1u << h));
         }
@@ -519,10 +528,14 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
       unit_stages(g2, c, split, ks_u, kTg2 == 1 ? 1 : min(kTg2, p.m2 - m * kTg2), k0, ks_n);
 #pragma unroll 1
       for (int ks = 0, kq = k0; ks < ks_n; ++ks, kq = (kq + 1 == ks_u) ? 0 : kq + 1) {
-        int oke = 1;
-        if (lane == 0) oke = mbar_wait(bar(kBarEmpty + stage), phase ^ 1u, err, kErrTimeoutEmpty, wb) ? 1 : 0;
-        oke = __shfl_sync(0xffffffffu, oke, 0);
-        if (!oke) break;
+        if (fills < kStages) {
+          ++fills;  // the ring's first pass: every slot is still empty
+        } else {
+          int oke = 1;
+          if (lane == 0) oke = mbar_wait(bar(kBarEmpty + stage), phase ^ 1u, err, kErrTimeoutEmpty, wb) ? 1 : 0;
+          oke = __shfl_sync(0xffffffffu, oke, 0);
+          if (!oke) break;
+        }
         const uint32_t sb = base + L::kSmemB + stage * kBStageBytes;
         const uint8_t *gq = dq + kq * kRowBytes;
 #pragma unroll
@@ -699,11 +712,23 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
               for (int j = 0; j < kSegRows; ++j) {
                 float g = 0.0f, up = 0.0f;
                 if (j < rows) {
-                  g = __ldcg(base + j * 128);
-                  up = __ldcg(base + j * 128 + 64);
-                  for (int cc = 1; cc < split; ++cc) {
-                    g = __fadd_rn(g, __ldcg(base + cc * kPartFloats + j * 128));
-                    up = __fadd_rn(up, __ldcg(base + cc * kPartFloats + j * 128 + 64));
+                  // every chunk's loads in flight at once, then the sum in chunk order
+                  float gp[kMaxSplit], upp[kMaxSplit];
+#pragma unroll
+                  for (int cc = 0; cc < kMaxSplit; ++cc) {
+                    if (cc < split) {
+                      gp[cc] = __ldcg(base + cc * kPartFloats + j * 128);
+                      upp[cc] = __ldcg(base + cc * kPartFloats + j * 128 + 64);
+                    }
+                  }
+                  g = gp[0];
+                  up = upp[0];
+#pragma unroll
+                  for (int cc = 1; cc < kMaxSplit; ++cc) {
+                    if (cc < split) {
+                      g = __fadd_rn(g, gp[cc]);
+                      up = __fadd_rn(up, upp[cc]);
+                    }
                   }
                   if constexpr (kNv) {
                     g = __fmul_rn(g, al);
