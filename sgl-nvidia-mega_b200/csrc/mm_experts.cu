@@ -86,6 +86,18 @@ __device__ __forceinline__ int ld_acquire(const int *p) {
   return v;
 }
 
+// Split-K count-in: one acquire-release atomic on lane 0, between two warp
+// barriers. The warp barrier before it orders the other lanes' partial-sum
+// stores before lane 0's release (release is cumulative); the one after it
+// orders their loads of the other chunks' partials after lane 0's acquire.
+// A gpu-scope acquire-release fence, not the sequentially consistent one of
+// __threadfence.
+__device__ __forceinline__ int atom_add_acq_rel(int *p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
 __device__ __forceinline__ int ld_shared_volatile(const int *p) {
   return *reinterpret_cast<const volatile int *>(p);
 }
@@ -620,7 +632,8 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
             p.hs[t * ts + prow * p.hs_row + f / L::kBlock] = static_cast<uint8_t>(code);
         }
       }
-      __threadfence();
+      // every lane's h bytes, then lane 0's release increment (cumulative over
+      // the warp barrier) publishes them
       __syncwarp();
       if (lane == 0) asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(p.flags + seg) : "memory");
     };
@@ -698,14 +711,13 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
 #pragma unroll
             for (int j = 0; j < kSegRows; ++j)
               if (j < rows) mine[j * 128] = v[j];
-            __threadfence();
             __syncwarp();
             int last = 0;
-            if (lane == 0) last = atomicAdd(p.split_cnt + 2 * tile + (q & 1), 1) == 2 * split - 1 ? 1 : 0;
+            if (lane == 0) last = atom_add_acq_rel(p.split_cnt + 2 * tile + (q & 1), 1) == 2 * split - 1 ? 1 : 0;
             last = __shfl_sync(0xffffffffu, last, 0);
+            __syncwarp();
             if (last) {
               // the half's last warp: every chunk's partials, added in chunk order
-              __threadfence();
               fq = q & 1;
               const float *base = p.part + static_cast<size_t>(tile) * split * kPartFloats + 32 * fq + lane;
 #pragma unroll
