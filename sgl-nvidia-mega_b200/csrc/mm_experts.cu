@@ -123,8 +123,7 @@ __device__ bool wait_flag(const int *flag, int target, uint32_t *err, uint64_t b
   if (ld_acquire(flag) >= target) return true;
   const uint64_t t0 = globaltimer();
 #pragma unroll 1
-  for (uint32_t i = 0;; ++i) {
-    __nanosleep(64);
+  for (uint32_t i = 0;; ++i) {  // each poll is an L2 round trip: no sleep between them
     if (ld_acquire(flag) >= target) return true;
     if ((i & 15u) == 0u) {
       if (error_set(err)) return false;
@@ -475,13 +474,6 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
       bool g2;
       int seg, m, c;
       decode_unit(u, nseg, p.m1, split, p.u2, g2, seg, m, c);
-      if (g2 && seg != ready_seg) {  // once complete, a mailbox stays complete in this launch
-        int okf = 1;
-        if (lane == 0) okf = wait_flag(p.flags + seg, 2 * p.m1, err, wb) ? 1 : 0;
-        okf = __shfl_sync(0xffffffffu, okf, 0);
-        if (!okf) break;
-        ready_seg = seg;
-      }
       if (seg != share_seg || g2 != share_g2) {
         share_seg = seg;
         share_g2 = g2;
@@ -532,6 +524,16 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
           s_base[h] = static_cast<uint32_t>(t) * term_s + static_cast<uint32_t>(sr) * srow;
           smask = (rr < nb && r < rows) ? (smask | (1u << h)) : (smask & ~(1u << h));
         }
+      }
+      // a down unit's rows are its segment's h rows: the shares above depend
+      // only on the segment descriptor, so they are ready when the mailbox
+      // completes (once complete, a mailbox stays complete in this launch)
+      if (g2 && seg != ready_seg) {
+        int okf = 1;
+        if (lane == 0) okf = wait_flag(p.flags + seg, 2 * p.m1, err, wb) ? 1 : 0;
+        okf = __shfl_sync(0xffffffffu, okf, 0);
+        if (!okf) break;
+        ready_seg = seg;
       }
       // a down unit's tiles share their B: stage ks loads K stage ks % ks_u; a
       // gate_up chunk loads K stages [k0, k0 + ks_n)
@@ -597,39 +599,76 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
       const size_t rowb = static_cast<size_t>(p.hq_row);
       const size_t tq = static_cast<size_t>(p.rows_cap) * rowb;      // term stride of hq
       const size_t ts = static_cast<size_t>(p.rows_cap) * p.hs_row;  // term stride of hs
-#pragma unroll
-      for (int j = 0; j < kSegRows; ++j) {
-        if (j >= rows) break;
-        float g = gv[j];
-        float up = uv[j];
+      // one row's SwiGLU and FP4 terms (the token row sg.y + j): h = up *
+      // silu(gate), then one MXFP4 block of 32 or two NVFP4 blocks of 16 (lane
+      // halves) per term, each term quantizing the previous terms' remainder
+      auto silu_row = [&](float g, float up) {
         if (clamped) {
           up = fminf(fmaxf(up, -limit), limit);
           g = fminf(g, limit);
         }
-        float r = __fmul_rn(up, __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
-        const size_t prow = static_cast<size_t>(sg.y + j);
-        // FP4 terms of the 32 features of this warp for token row j: one
-        // MXFP4 block of 32, or two NVFP4 blocks of 16 (lane halves)
-        for (int t = 0; t < p.terms; ++t) {
-          uint32_t nib, code;
-          if constexpr (kNv) {
-            float amax = fabsf(r);
+        return __fmul_rn(up, __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
+      };
+      auto quant_term = [&](float &r, uint32_t &nib, uint32_t &code) {
+        if constexpr (kNv) {
+          float amax = fabsf(r);
 #pragma unroll
-            for (int off = 8; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-            code = nv4_scale_code(amax, p.gs2);
-            const float sv = e4m3_value(static_cast<uint8_t>(code));
-            nib = e2m1x2(__fmul_rn(r, nv4_multiplier(sv, p.gs2)), 0.0f) & 15u;
-            r = __fsub_rn(r, __fmul_rn(__fmul_rn(e2m1_value(nib), sv), p.inv_gs2));
-          } else {
-            const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(r))));
-            code = mx4_scale_code(amax);
-            nib = e2m1x2(__fmul_rn(r, mx_inverse(code)), 0.0f) & 15u;
-            r = __fsub_rn(r, __fmul_rn(e2m1_value(nib), mx_scale_value(code)));
-          }
-          const uint32_t up_nib = __shfl_down_sync(0xffffffffu, nib, 1);
+          for (int off = 8; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+          code = nv4_scale_code(amax, p.gs2);
+          const float sv = e4m3_value(static_cast<uint8_t>(code));
+          nib = e2m1x2(__fmul_rn(r, nv4_multiplier(sv, p.gs2)), 0.0f) & 15u;
+          r = __fsub_rn(r, __fmul_rn(__fmul_rn(e2m1_value(nib), sv), p.inv_gs2));
+        } else {
+          const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(r))));
+          code = mx4_scale_code(amax);
+          nib = e2m1x2(__fmul_rn(r, mx_inverse(code)), 0.0f) & 15u;
+          r = __fsub_rn(r, __fmul_rn(e2m1_value(nib), mx_scale_value(code)));
+        }
+      };
+      auto store_term = [&](int t, int j, uint32_t nib, uint32_t code) {
+        const uint32_t up_nib = __shfl_down_sync(0xffffffffu, nib, 1);
+        const size_t prow = static_cast<size_t>(sg.y + j);
+        if (j < rows) {
           if ((lane & 1) == 0) p.hq[t * tq + prow * rowb + (f >> 1)] = static_cast<uint8_t>(nib | (up_nib << 4));
           if ((lane & (L::kBlock - 1)) == 0)
             p.hs[t * ts + prow * p.hs_row + f / L::kBlock] = static_cast<uint8_t>(code);
+        }
+      };
+      if (rows <= 2) {
+        // a row or two (small batches): one row at a time, the shortest code
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          if (j >= rows) break;
+          float r = silu_row(gv[j], uv[j]);
+          for (int t = 0; t < p.terms; ++t) {
+            uint32_t nib, code;
+            quant_term(r, nib, code);
+            store_term(t, j, nib, code);
+          }
+        }
+      } else {
+        // rows in groups of kG: each row's quantization is a chain of warp
+        // reductions and conversions, so independent rows in flight hide its
+        // latency (rows past `rows` run on zeros and are not stored)
+        constexpr int kG = 4;
+#pragma unroll
+        for (int j0 = 0; j0 < kSegRows; j0 += kG) {
+          if (j0 >= rows) break;
+          float r[kG];
+#pragma unroll
+          for (int i = 0; i < kG; ++i) {
+            const bool live = j0 + i < rows;
+            r[i] = silu_row(live ? gv[j0 + i] : 0.0f, live ? uv[j0 + i] : 0.0f);
+          }
+#pragma unroll
+          for (int t = 0; t < kMaxTerms; ++t) {
+            if (t >= p.terms) break;
+            uint32_t nib[kG], code[kG];
+#pragma unroll
+            for (int i = 0; i < kG; ++i) quant_term(r[i], nib[i], code[i]);
+#pragma unroll
+            for (int i = 0; i < kG; ++i) store_term(t, j0 + i, nib[i], code[i]);
+          }
         }
       }
       // every lane's h bytes, then lane 0's release increment (cumulative over
