@@ -86,17 +86,22 @@ __device__ __forceinline__ int ld_acquire(const int *p) {
   return v;
 }
 
-// Split-K count-in: one acquire-release atomic on lane 0, between two warp
-// barriers. The warp barrier before it orders the other lanes' partial-sum
-// stores before lane 0's release (release is cumulative); the one after it
-// orders their loads of the other chunks' partials after lane 0's acquire.
-// A gpu-scope acquire-release fence, not the sequentially consistent one of
-// __threadfence.
+// Split-K count-in of a one- or two-row segment: one acquire-release atomic on
+// lane 0, between two warp barriers. The warp barrier before it orders the
+// other lanes' partial-sum stores before lane 0's release (release is
+// cumulative); the one after it orders their loads of the other chunks'
+// partials after lane 0's acquire.
 __device__ __forceinline__ int atom_add_acq_rel(int *p, int v) {
   int old;
   asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
   return old;
 }
+
+// Mailbox increments that complete one gate_up tile of a segment: one per half
+// of the tile's features (its SwiGLU warp, or a split-K tile's last warp of
+// the half when the segment has one or two rows), or one per epilogue warp of
+// every chunk when a split-K tile's rows are shared out.
+__device__ __forceinline__ int tile_publishes(int split, int rows) { return split > 1 && rows > 2 ? 4 * split : 2; }
 
 __device__ __forceinline__ int ld_shared_volatile(const int *p) {
   return *reinterpret_cast<const volatile int *>(p);
@@ -530,7 +535,8 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
       // completes (once complete, a mailbox stays complete in this launch)
       if (g2 && seg != ready_seg) {
         int okf = 1;
-        if (lane == 0) okf = wait_flag(p.flags + seg, 2 * p.m1, err, wb) ? 1 : 0;
+        const int target = p.m1 * tile_publishes(split, seg_cache.get(p.segs, seg).z);
+        if (lane == 0) okf = wait_flag(p.flags + seg, target, err, wb) ? 1 : 0;
         okf = __shfl_sync(0xffffffffu, okf, 0);
         if (!okf) break;
         ready_seg = seg;
@@ -585,13 +591,13 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
     float *ex = reinterpret_cast<float *>(sbase + L::kSmemEpi);
     uint32_t ws = 0, wphase = 0, acc = 0, acc_phase = 0, ex_phase = 0;
     SegCache seg_cache;
-    // SwiGLU (+ clamp) of the 32 features f = 64 m + 32 fq + lane of segment sg's
-    // rows (gate gv, up uv), requantized into h's FP4 terms, then this warp's
-    // increment of the segment's mailbox (two per gate_up tile). One call site:
-    // the split-K and the whole-tile paths both end here.
+    // SwiGLU (+ clamp) of the 32 features f = 64 m + 32 fq + lane of `rows` token
+    // rows of segment sg from row j_base on (gate gv[i], up uv[i] for row
+    // j_base + i), requantized into h's FP4 terms, then this warp's increment of
+    // the segment's mailbox (two per whole gate_up tile, four per split-K chunk).
+    // One call site: the split-K and the whole-tile paths both end here.
     auto swiglu_publish = [&](const int4 &sg, int seg, int m, int fq, const float (&gv)[kSegRows],
-                              const float (&uv)[kSegRows]) {
-      const int rows = sg.z;
+                              const float (&uv)[kSegRows], int j_base, int rows) {
       const float *lim = sg.x < 0 ? p.shared_clamp : p.clamp;
       const bool clamped = lim != nullptr;
       const float limit = clamped ? lim[sg.x < 0 ? 0 : sg.x] : 0.0f;
@@ -627,7 +633,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
       };
       auto store_term = [&](int t, int j, uint32_t nib, uint32_t code) {
         const uint32_t up_nib = __shfl_down_sync(0xffffffffu, nib, 1);
-        const size_t prow = static_cast<size_t>(sg.y + j);
+        const size_t prow = static_cast<size_t>(sg.y + j_base + j);
         if (j < rows) {
           if ((lane & 1) == 0) p.hq[t * tq + prow * rowb + (f >> 1)] = static_cast<uint8_t>(nib | (up_nib << 4));
           if ((lane & (L::kBlock - 1)) == 0)
@@ -647,27 +653,38 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
           }
         }
       } else {
-        // rows in groups of kG: each row's quantization is a chain of warp
-        // reductions and conversions, so independent rows in flight hide its
-        // latency (rows past `rows` run on zeros and are not stored)
+        // rows in groups of kG, one group per pass of a compact loop: each row's
+        // quantization is a chain of warp reductions and conversions, so
+        // independent rows in flight hide its latency; the rows' values rotate
+        // down by a group after each pass (register indices stay fixed), and
+        // rows past `rows` run on zeros and are not stored
         constexpr int kG = 4;
+        float gq[kSegRows], uq[kSegRows];
 #pragma unroll
-        for (int j0 = 0; j0 < kSegRows; j0 += kG) {
-          if (j0 >= rows) break;
+        for (int j = 0; j < kSegRows; ++j) {
+          gq[j] = gv[j];
+          uq[j] = uv[j];
+        }
+#pragma unroll 1
+        for (int j0 = 0; j0 < rows; j0 += kG) {
           float r[kG];
 #pragma unroll
           for (int i = 0; i < kG; ++i) {
             const bool live = j0 + i < rows;
-            r[i] = silu_row(live ? gv[j0 + i] : 0.0f, live ? uv[j0 + i] : 0.0f);
+            r[i] = silu_row(live ? gq[i] : 0.0f, live ? uq[i] : 0.0f);
           }
-#pragma unroll
-          for (int t = 0; t < kMaxTerms; ++t) {
-            if (t >= p.terms) break;
+#pragma unroll 1
+          for (int t = 0; t < p.terms; ++t) {
             uint32_t nib[kG], code[kG];
 #pragma unroll
             for (int i = 0; i < kG; ++i) quant_term(r[i], nib[i], code[i]);
 #pragma unroll
             for (int i = 0; i < kG; ++i) store_term(t, j0 + i, nib[i], code[i]);
+          }
+#pragma unroll
+          for (int i = 0; i + kG < kSegRows; ++i) {
+            gq[i] = gq[i + kG];
+            uq[i] = uq[i + kG];
           }
         }
       }
@@ -741,53 +758,106 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
           // 64 m + 32 fq + lane, for the warp that runs the SwiGLU (fq its half)
           float upv[kSegRows];
           int fq = -1;
+          int j_base = 0, nj = rows;
           if (chunked) {
             // split-K chunk: this warp's rows of the chunk's partial sums go to
-            // the chunk's slot; the warp then counts in for its half of the
-            // tile's features (gate rows 32 fq + lane, up rows 64 + 32 fq + lane)
+            // the chunk's slot, then the tile's chunks are added in chunk order
             const int tile = u / split;
+            const int chunk = u - tile * split;
             float *mine = p.part + static_cast<size_t>(u) * kPartFloats + row;
 #pragma unroll
             for (int j = 0; j < kSegRows; ++j)
               if (j < rows) mine[j * 128] = v[j];
             __syncwarp();
-            int last = 0;
-            if (lane == 0) last = atom_add_acq_rel(p.split_cnt + 2 * tile + (q & 1), 1) == 2 * split - 1 ? 1 : 0;
-            last = __shfl_sync(0xffffffffu, last, 0);
-            __syncwarp();
-            if (last) {
-              // the half's last warp: every chunk's partials, added in chunk order
-              fq = q & 1;
-              const float *base = p.part + static_cast<size_t>(tile) * split * kPartFloats + 32 * fq + lane;
+            if (rows <= 2) {
+              // a row or two: the warp counts in for its half of the features
+              // (gate rows 32 fq + lane, up rows 64 + 32 fq + lane); the half's
+              // last warp adds every chunk, each row's chunks all in flight
+              int last = 0;
+              if (lane == 0) last = atom_add_acq_rel(p.split_cnt + 2 * tile + (q & 1), 1) == 2 * split - 1 ? 1 : 0;
+              last = __shfl_sync(0xffffffffu, last, 0);
+              __syncwarp();
+              if (last) {
+                fq = q & 1;
+                const float *base = p.part + static_cast<size_t>(tile) * split * kPartFloats + 32 * fq + lane;
 #pragma unroll
-              for (int j = 0; j < kSegRows; ++j) {
-                float g = 0.0f, up = 0.0f;
-                if (j < rows) {
-                  // every chunk's loads in flight at once, then the sum in chunk order
-                  float gp[kMaxSplit], upp[kMaxSplit];
+                for (int j = 0; j < 2; ++j) {
+                  float g = 0.0f, up = 0.0f;
+                  if (j < rows) {
+                    float gp[kMaxSplit], upp[kMaxSplit];
 #pragma unroll
-                  for (int cc = 0; cc < kMaxSplit; ++cc) {
-                    if (cc < split) {
-                      gp[cc] = __ldcg(base + cc * kPartFloats + j * 128);
-                      upp[cc] = __ldcg(base + cc * kPartFloats + j * 128 + 64);
+                    for (int cc = 0; cc < kMaxSplit; ++cc) {
+                      if (cc < split) {
+                        gp[cc] = __ldcg(base + cc * kPartFloats + j * 128);
+                        upp[cc] = __ldcg(base + cc * kPartFloats + j * 128 + 64);
+                      }
+                    }
+                    g = gp[0];
+                    up = upp[0];
+#pragma unroll
+                    for (int cc = 1; cc < kMaxSplit; ++cc) {
+                      if (cc < split) {
+                        g = __fadd_rn(g, gp[cc]);
+                        up = __fadd_rn(up, upp[cc]);
+                      }
                     }
                   }
-                  g = gp[0];
-                  up = upp[0];
-#pragma unroll
-                  for (int cc = 1; cc < kMaxSplit; ++cc) {
-                    if (cc < split) {
-                      g = __fadd_rn(g, gp[cc]);
-                      up = __fadd_rn(up, upp[cc]);
-                    }
-                  }
-                  if constexpr (kNv) {
-                    g = __fmul_rn(g, al);
-                    up = __fmul_rn(up, al);
-                  }
+                  v[j] = g;
+                  upv[j] = up;
                 }
-                v[j] = g;
-                upv[j] = up;
+              }
+            } else {
+              // more rows: every warp of the tile's chunks counts in (4 per
+              // chunk) and waits for all of them (the chunks are first-wave
+              // units, resident together); the 2 x split warps of each half of
+              // the features then each finish a block of the token rows
+              int okc = 1;
+              if (lane == 0) {
+                asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(p.split_cnt + 2 * tile) : "memory");
+                okc = wait_flag(p.split_cnt + 2 * tile, 4 * split, err, wb) ? 1 : 0;
+              }
+              okc = __shfl_sync(0xffffffffu, okc, 0);
+              __syncwarp();  // lane 0's acquire orders the warp's loads below
+              if (!okc) {
+                ok = 0;
+                break;
+              }
+              fq = q & 1;
+              const int nw = 2 * split;  // >= 4: at most 4 rows per warp
+              const int per = (rows + nw - 1) / nw;
+              j_base = min(rows, (2 * chunk + (q >> 1)) * per);
+              nj = min(rows - j_base, per);
+              // the warp's rows, chunk by chunk, added in chunk order (rows past
+              // nj read an in-slot row and are never stored)
+              const float *base = p.part + static_cast<size_t>(tile) * split * kPartFloats + 32 * fq + lane;
+              int ro[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) ro[i] = min(j_base + i, kSegRows - 1) * 128;
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                v[i] = __ldcg(base + ro[i]);
+                upv[i] = __ldcg(base + ro[i] + 64);
+              }
+#pragma unroll 1
+              for (int cc = 1; cc < split; ++cc) {
+                float gp[4], upp[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  gp[i] = __ldcg(base + cc * kPartFloats + ro[i]);
+                  upp[i] = __ldcg(base + cc * kPartFloats + ro[i] + 64);
+                }
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  v[i] = __fadd_rn(v[i], gp[i]);
+                  upv[i] = __fadd_rn(upv[i], upp[i]);
+                }
+              }
+            }
+            if constexpr (kNv) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                v[i] = __fmul_rn(v[i], al);
+                upv[i] = __fmul_rn(upv[i], al);
               }
             }
           } else if (q >= 2) {
@@ -812,7 +882,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
             ex_phase ^= 1u;
             fq = q;
           }
-          if (fq >= 0) swiglu_publish(sg, seg, m, fq, v, upv);
+          if (fq >= 0) swiglu_publish(sg, seg, m, fq, v, upv, j_base, nj);
         } else {
           // features 128 (m tg2 + tt) + row of the segment's rows, bf16
           const size_t col = static_cast<size_t>(128 * (m * kTg2 + tt) + row);

@@ -23,6 +23,7 @@
 // tanh.approx / libm / approximate-reciprocal sequences, whose bits no CPU code
 // can reproduce; everything else is the reference's rule.
 #pragma once
+#include <cuda_fp16.h>
 #include <cstdint>
 #include <cuda_bf16.h>
 
@@ -190,13 +191,13 @@ __device__ __forceinline__ uint32_t e2m1x2(float lo, float hi) {
       : "f"(hi), "f"(lo));
   return r & 0xffu;
 }
-// exact value of an E2M1 code (bits 0-3)
+// exact value of an E2M1 code (bits 0-3): the hardware conversion of the code,
+// as the low nibble of an e2m1x2 byte, to the low half of an f16x2 (every E2M1
+// value, 0 0.5 1 1.5 2 3 4 6 and their negatives, is exact in f16)
 __device__ __forceinline__ float e2m1_value(uint32_t code) {
-  const uint32_t mag = code & 7u;
-  // 0, 0.5, 1, 1.5, 2, 3, 4, 6
-  const float v = mag < 4u ? 0.5f * static_cast<float>(mag)
-                           : (mag < 6u ? static_cast<float>(mag - 2u) : static_cast<float>(2u * mag - 8u));
-  return (code & 8u) ? -v : v;
+  uint32_t h2;
+  asm("{\n\t.reg .b8 t;\n\tcvt.u8.u32 t, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}" : "=r"(h2) : "r"(code & 15u));
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(h2 & 0xffffu)));
 }
 
 __device__ __forceinline__ float bf16_bits_to_float(uint16_t b) {
