@@ -640,51 +640,122 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
             p.hs[t * ts + prow * p.hs_row + f / L::kBlock] = static_cast<uint8_t>(code);
         }
       };
-      if (rows <= 2) {
-        // a row or two (small batches): one row at a time, the shortest code
+      bool staged = false;
+      if constexpr (!kNv) staged = rows > 4;
+      if (staged) {
+        // MXFP4, more than 4 rows (a whole tile: a split-K warp has at most 4):
+        // the SwiGLU with lane = feature, then through this gate warp's part of
+        // the exchange (its up sums already in registers; released once read
+        // back) each token row's block of 32 features goes to two lanes (lane
+        // 2 r + hh: features 16 hh .. 16 hh + 15 of row r). A term's block amax
+        // is a 16-element local maximum and one shuffle (of the magnitudes'
+        // bits, as a warp reduction of them), and two features convert per
+        // instruction; each element's arithmetic is the one-lane-per-feature
+        // form's, so the bytes are the same. (Up to 4 rows the
+        // lane-per-feature forms below are shorter.)
+        float *qx = ex + 32 * fq * kSegRows;  // this gate warp's rows of the exchange
+        {
+          // one row per pass of a compact loop, the rows rotating down
+          float gq[kSegRows], uq[kSegRows];
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          if (j >= rows) break;
-          float r = silu_row(gv[j], uv[j]);
-          for (int t = 0; t < p.terms; ++t) {
-            uint32_t nib, code;
-            quant_term(r, nib, code);
-            store_term(t, j, nib, code);
+          for (int j = 0; j < kSegRows; ++j) {
+            gq[j] = gv[j];
+            uq[j] = uv[j];
+          }
+#pragma unroll 1
+          for (int j = 0; j < rows; ++j) {
+            qx[j * 32 + lane] = silu_row(gq[0], uq[0]);
+#pragma unroll
+            for (int i = 0; i + 1 < kSegRows; ++i) {
+              gq[i] = gq[i + 1];
+              uq[i] = uq[i + 1];
+            }
+          }
+        }
+        __syncwarp();
+        const int jr = lane >> 1, hh = lane & 1;
+        const bool live = jr < rows;
+        float x[16];
+        const float4 *src = reinterpret_cast<const float4 *>(qx + (live ? jr : 0) * 32 + 16 * hh);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float4 w = src[k];
+          x[4 * k] = live ? w.x : 0.0f;
+          x[4 * k + 1] = live ? w.y : 0.0f;
+          x[4 * k + 2] = live ? w.z : 0.0f;
+          x[4 * k + 3] = live ? w.w : 0.0f;
+        }
+        __syncwarp();  // the tile is read: the exchange is free for the next unit's up rows
+        if (lane == 0) mbar_arrive(bar(kBarExFree));
+        const size_t prow = static_cast<size_t>(sg.y + j_base + (live ? jr : 0));
+        const int f0 = 64 * m + 32 * fq;  // the block's first feature
+        for (int t = 0; t < p.terms; ++t) {
+          uint32_t abits = 0u;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) abits = max(abits, __float_as_uint(fabsf(x[i])));
+          abits = max(abits, __shfl_xor_sync(0xffffffffu, abits, 1));
+          const uint32_t code = mx4_scale_code(__uint_as_float(abits));
+          const float inv = mx_inverse(code), sv = mx_scale_value(code);
+          uint32_t w[2] = {0u, 0u};
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const uint32_t b = e2m1x2(__fmul_rn(x[2 * k], inv), __fmul_rn(x[2 * k + 1], inv));
+            w[k >> 2] |= b << (8 * (k & 3));
+            x[2 * k] = __fsub_rn(x[2 * k], __fmul_rn(e2m1_value(b), sv));
+            x[2 * k + 1] = __fsub_rn(x[2 * k + 1], __fmul_rn(e2m1_value(b >> 4), sv));
+          }
+          if (live) {
+            *reinterpret_cast<uint2 *>(p.hq + t * tq + prow * rowb + (f0 >> 1) + 8 * hh) = make_uint2(w[0], w[1]);
+            if (hh == 0) p.hs[t * ts + prow * p.hs_row + f0 / L::kBlock] = static_cast<uint8_t>(code);
           }
         }
       } else {
-        // rows in groups of kG, one group per pass of a compact loop: each row's
-        // quantization is a chain of warp reductions and conversions, so
-        // independent rows in flight hide its latency; the rows' values rotate
-        // down by a group after each pass (register indices stay fixed), and
-        // rows past `rows` run on zeros and are not stored
-        constexpr int kG = 4;
-        float gq[kSegRows], uq[kSegRows];
-#pragma unroll
-        for (int j = 0; j < kSegRows; ++j) {
-          gq[j] = gv[j];
-          uq[j] = uv[j];
-        }
-#pragma unroll 1
-        for (int j0 = 0; j0 < rows; j0 += kG) {
-          float r[kG];
-#pragma unroll
-          for (int i = 0; i < kG; ++i) {
-            const bool live = j0 + i < rows;
-            r[i] = silu_row(live ? gq[i] : 0.0f, live ? uq[i] : 0.0f);
+        if (rows <= 2) {
+          // a row or two (small batches): one row at a time, the shortest code
+  #pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            if (j >= rows) break;
+            float r = silu_row(gv[j], uv[j]);
+            for (int t = 0; t < p.terms; ++t) {
+              uint32_t nib, code;
+              quant_term(r, nib, code);
+              store_term(t, j, nib, code);
+            }
           }
-#pragma unroll 1
-          for (int t = 0; t < p.terms; ++t) {
-            uint32_t nib[kG], code[kG];
-#pragma unroll
-            for (int i = 0; i < kG; ++i) quant_term(r[i], nib[i], code[i]);
-#pragma unroll
-            for (int i = 0; i < kG; ++i) store_term(t, j0 + i, nib[i], code[i]);
+        } else {
+          // rows in groups of kG, one group per pass of a compact loop: each row's
+          // quantization is a chain of warp reductions and conversions, so
+          // independent rows in flight hide its latency; the rows' values rotate
+          // down by a group after each pass (register indices stay fixed), and
+          // rows past `rows` run on zeros and are not stored
+          constexpr int kG = 4;
+          float gq[kSegRows], uq[kSegRows];
+  #pragma unroll
+          for (int j = 0; j < kSegRows; ++j) {
+            gq[j] = gv[j];
+            uq[j] = uv[j];
           }
-#pragma unroll
-          for (int i = 0; i + kG < kSegRows; ++i) {
-            gq[i] = gq[i + kG];
-            uq[i] = uq[i + kG];
+  #pragma unroll 1
+          for (int j0 = 0; j0 < rows; j0 += kG) {
+            float r[kG];
+  #pragma unroll
+            for (int i = 0; i < kG; ++i) {
+              const bool live = j0 + i < rows;
+              r[i] = silu_row(live ? gq[i] : 0.0f, live ? uq[i] : 0.0f);
+            }
+  #pragma unroll 1
+            for (int t = 0; t < p.terms; ++t) {
+              uint32_t nib[kG], code[kG];
+  #pragma unroll
+              for (int i = 0; i < kG; ++i) quant_term(r[i], nib[i], code[i]);
+  #pragma unroll
+              for (int i = 0; i < kG; ++i) store_term(t, j0 + i, nib[i], code[i]);
+            }
+  #pragma unroll
+            for (int i = 0; i + kG < kSegRows; ++i) {
+              gq[i] = gq[i + kG];
+              uq[i] = uq[i + kG];
+            }
           }
         }
       }
@@ -878,7 +949,10 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
 #pragma unroll
             for (int j = 0; j < kSegRows; ++j) upv[j] = ex[row * kSegRows + j];
             __syncwarp();
-            if (lane == 0) mbar_arrive(bar(kBarExFree));
+            // MXFP4 with more than 4 rows stages its requantization in this
+            // warp's part of the exchange and releases it there
+            if (kNv || rows <= 4)
+              if (lane == 0) mbar_arrive(bar(kBarExFree));
             ex_phase ^= 1u;
             fq = q;
           }
