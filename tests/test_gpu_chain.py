@@ -146,6 +146,26 @@ def test_route_bitexact(T, K, E):
         assert np.array_equal(rec.cpu().numpy(), orec), (T, K, E, distinct, offset)
 
 
+@pytest.mark.parametrize("T,K,E", [(1, 8, 384), (2, 6, 64), (4, 8, 16), (5, 6, 384), (3, 2, 8), (16, 2, 16)])
+def test_route_decode_batches_and_foreign_ids(T, K, E):
+    """Decode-sized steps (up to 32 slots) with padded ids (-1), ids of no
+    local expert and every window / dealing mode, against the oracle. A row's
+    ids are distinct, as the reference's route assumes (route.cuh)."""
+    mm = _mm()
+    g = torch.Generator().manual_seed(31 * T + K + E)
+    for offset, local in ((0, E), (E // 2, E // 2), (0, E // 2), (-1, E), (-2, E)):
+        for trial in range(4):
+            ids = _random_ids(T, K, E, g, distinct=(None, K + 1, 2 * K, None)[trial])
+            if trial & 1:
+                ids[T - 1, K - 1] = -1                       # a padded slot
+            if trial & 2 and offset >= 0:
+                ids[T // 2, 0] = E + 3                       # no expert of the window
+            perm, rec = mm.route(ids.cuda(), local, offset)
+            operm, orec = O.route(ids.numpy(), local, offset)
+            assert np.array_equal(perm.cpu().numpy(), operm), (T, K, E, offset, trial)
+            assert np.array_equal(rec.cpu().numpy(), orec), (T, K, E, offset, trial)
+
+
 def test_finalize_bitexact():
     mm = _mm()
     g = torch.Generator().manual_seed(3)
