@@ -559,7 +559,8 @@ static int launch_router(mm_layer *L, const uint16_t *x, const uint16_t *w, floa
                          void *stream) {
   if (L->H % 1024 || L->H > kMaxRouterHidden)
     return fail(MM_ERR_INVALID, "router GEMV: hidden %d must be a multiple of 1024, <= %d", L->H, kMaxRouterHidden);
-  if (!aligned(w, 16)) return fail(MM_ERR_INVALID, "router weight must be 16-byte aligned");
+  if (!aligned(w, 16) || !aligned(x, 16))
+    return fail(MM_ERR_INVALID, "router GEMV: x and the router weight must be 16-byte aligned");
   RouterArgs a = {};
   a.x = x;
   a.w = w;
@@ -567,6 +568,7 @@ static int launch_router(mm_layer *L, const uint16_t *x, const uint16_t *w, floa
   a.tokens = tokens;
   a.experts = L->R;
   a.hidden = L->H;
+  a.err = L->err;
   MM_CUDA(router_smem_attr());
   MM_CUDA(launch(router_kernel, dim3((L->R + 3) / 4, (tokens + 7) / 8), dim3(256), router_smem_bytes(L->H), stream, a));
   return MM_OK;

@@ -73,6 +73,7 @@ struct RouterArgs {
   const uint16_t *w;         // bf16 [E, H]
   float *logits;             // [T, E]
   int tokens, experts, hidden;
+  uint32_t *err;             // a layer's error word (the x staging wait), or null
 };
 
 struct alignas(64) ExpertArgs {

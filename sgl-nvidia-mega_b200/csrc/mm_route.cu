@@ -36,7 +36,9 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
   pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // GEMV tile: experts [4 blockIdx.x, +4) x tokens [8 blockIdx.y, +8). The 8
-  // token rows of x are staged once in shared memory (cp.async). Warp w takes
+  // token rows of x are staged once in shared memory, one bulk copy per row
+  // completing on one mbarrier (a few instructions where 16-byte copies took
+  // thousands). Warp w takes
   // the 1024-wide K parts w, w + 8 for all four experts, so each x load feeds
   // four experts; lane l sums elements 8 (l + 32 j) .. + 8 of the part for every
   // (expert, token), and a reduce-scatter butterfly over the 32 (expert, token)
@@ -63,19 +65,43 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
                                 lane + 32 * j)
                         : make_uint4(0u, 0u, 0u, 0u);
   };
+  __shared__ __align__(8) uint64_t x_full;
+  const uint32_t xbar = static_cast<uint32_t>(__cvta_generic_to_shared(&x_full));
+  if (threadIdx.x == 0) {
+    mbar_init(xbar, 1);
+    fence_barrier_init();
+  }
   uint4 wv[4][4];
   load_w(warp, wv);
+  __syncthreads();
   pdl_wait();
-  {
-    const int per_row = a.hidden >> 3;  // uint4 per token row
+  if (threadIdx.x == 0) {
+    // rows of H bf16 (a multiple of 1024 elements) from 16-byte aligned x
+    const uint32_t row_bytes = static_cast<uint32_t>(a.hidden) * 2u;
     const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(xs));
-    for (int i = threadIdx.x; i < nt * per_row; i += blockDim.x) {
-      const int t = i / per_row, c = i - t * per_row;
-      cp_async_16(sbase + 16u * static_cast<uint32_t>(i),
-                  reinterpret_cast<const uint4 *>(a.x + static_cast<size_t>(t0 + t) * a.hidden) + c, 16u);
+    const uint64_t keep = policy_evict_last();  // every expert tile's CTA reads these rows
+    mbar_expect_tx(xbar, static_cast<uint32_t>(nt) * row_bytes);
+    for (int t = 0; t < nt; ++t)
+      bulk_load(sbase + static_cast<uint32_t>(t) * row_bytes, a.x + static_cast<size_t>(t0 + t) * a.hidden,
+                row_bytes, xbar, keep);
+  }
+  {
+    // bounded wait (the copies read caller-checked memory; the bound only
+    // guarantees that the launch ends): on expiry the layer's error word says
+    // so and no logits are written
+    bool landed = false;
+#pragma unroll 1
+    for (int i = 0; i < 256 && !landed; ++i) landed = mbar_try_wait(xbar, 0);
+    if (!landed) {
+      const uint64_t w0 = globaltimer();
+#pragma unroll 1
+      while (!(landed = mbar_try_wait(xbar, 0)) && globaltimer() - w0 < kWaitBudgetNs) {
+      }
     }
-    asm volatile("cp.async.wait_all;" ::: "memory");
-    __syncthreads();
+    if (__syncthreads_or(landed ? 0 : 1)) {
+      if (threadIdx.x == 0 && a.err != nullptr) error_raise(a.err, kErrTimeoutFull);
+      return;
+    }
   }
 #pragma unroll 1
   for (int part = warp; part < parts; part += 8) {
