@@ -107,7 +107,8 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
   for (int part = warp; part < parts; part += 8) {
     if (part != warp) load_w(part, wv);
     // per lane: 4 experts x 8 tokens chains, each in the element order above;
-    // rows t >= nt are stale smem and never stored
+    // rows t >= nt (a tile of fewer tokens: decode) run no chain and are never
+    // stored
     const uint4 *xr = reinterpret_cast<const uint4 *>(xs + 1024 * part);
     const int row_u4 = a.hidden >> 3;
     float v[32];  // v[8 es + t]
@@ -117,6 +118,7 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
     for (int j = 0; j < 4; ++j) {
 #pragma unroll
       for (int t = 0; t < 8; ++t) {
+        if (t >= nt) break;
         const uint4 xv = xr[t * row_u4 + lane + 32 * j];
         const uint32_t xq[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
