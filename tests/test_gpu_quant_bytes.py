@@ -216,11 +216,16 @@ def _x_for_exact_h(T, H, seed):
 
 
 @pytest.mark.parametrize("fmt", ["mxfp4", "nvfp4"])
-@pytest.mark.parametrize("T", [3, 8])
-def test_swiglu_output_terms_bitexact(fmt, T):
-    H, I, E, K = 1024, 256, 4, 2
-    layer, cols, wvals = _exact_h_layer(fmt, H, I, E, seed=11 + T)
-    moe = _moe(layer, K, 16)
+@pytest.mark.parametrize("H,T", [(1024, 3), (1024, 8), (1024, 24), (512, 8), (512, 24)])
+def test_swiglu_output_terms_bitexact(fmt, H, T):
+    """h's terms for every requantization path: hidden 1024 splits the gate_up
+    tiles (K chunks; one- or two-row segments finish in the half's last warp,
+    more rows are shared out over the chunks' warps), hidden 512 leaves them
+    whole (a row or two one at a time, 3-4 rows in a group, more rows staged
+    two lanes per MXFP4 block); 24 tokens over 4 experts give ~12 rows each."""
+    I, E, K = 256, 4, 2
+    layer, cols, wvals = _exact_h_layer(fmt, H, I, E, seed=11 + T + H)
+    moe = _moe(layer, K, max(16, T))
     x = _x_for_exact_h(T, H, seed=T)
     g = torch.Generator().manual_seed(100 + T)
     ids = torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(T)]).int()
