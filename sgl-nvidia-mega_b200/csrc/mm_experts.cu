@@ -393,6 +393,11 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
         bool ok = true;
         uint32_t d_tmem = acc_tmem;  // the unit's current tile: its accumulator kBRows columns further
         int kq = 0;                  // K stage within the tile (within the chunk: the first accumulates from 0)
+        // a down unit of two one-stage tiles: both tiles multiply the activation
+        // rows (and B scales) of its first stage; that slot is released after the
+        // second tile's MMAs, and the loader copies the rows once
+        const bool share_b = kTg2 == 2 && g2 && ks_u == 1 && ks_n == 2;
+        uint32_t keep_stage = 0;
 #pragma unroll 1
         for (int ks = 0; ks < ks_n; ++ks) {
           if (!mbar_wait(bar(kBarFull + stage), phase, err, kErrTimeoutFull, wb)) {
@@ -401,17 +406,19 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
           }
           tc_fence_after();
           fence_proxy_async_smem();  // activation rows and B scales arrived via cp.async
+          const bool reuse = share_b && ks == 1;  // the second tile: B of the first stage
+          const uint32_t b_stage = reuse ? keep_stage : stage;
           const uint32_t sfa_t = tbase + L::kTmemSfa + stage * L::kTmemSfCols;
-          const uint32_t sfb_t = tbase + L::kTmemSfb + stage * L::kTmemSfCols;
+          const uint32_t sfb_t = tbase + L::kTmemSfb + b_stage * L::kTmemSfCols;
           const uint64_t sfa_d = sf_hi | ((base + L::kSmemSfa + stage * L::kSfStageBytes) >> 4);
           const uint64_t sfb_d = sf_hi | ((base + L::kSmemSfb + stage * L::kSfStageBytes) >> 4);
 #pragma unroll
           for (int c = 0; c < L::kChunks; ++c) {
             tc_cp_32x128b_warpx4(sfa_t + 4 * c, sfa_d + ((512 * c) >> 4));
-            tc_cp_32x128b_warpx4(sfb_t + 4 * c, sfb_d + ((512 * c) >> 4));
+            if (!reuse) tc_cp_32x128b_warpx4(sfb_t + 4 * c, sfb_d + ((512 * c) >> 4));
           }
           const uint64_t a_d = sw_hi | ((base + L::kSmemA + stage * kAStageBytes) >> 4);
-          const uint64_t b_d = sw_hi | ((base + L::kSmemB + stage * kBStageBytes) >> 4);
+          const uint64_t b_d = sw_hi | ((base + L::kSmemB + b_stage * kBStageBytes) >> 4);
           // four K = 64 steps of 32 bytes along the 128-byte swizzled row.
           // MXFP4: scale chunk k / 2 holds the k-blocks of steps 2j, 2j + 1 at
           // byte pairs 0 and 2; NVFP4: chunk k holds step k's four k-blocks
@@ -423,7 +430,12 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
               mma_mxf4(d_tmem, a_d + 2 * k, b_d + 2 * k, (k & 1) ? id2 : id0, sfa_t + 4 * (k >> 1),
                        sfb_t + 4 * (k >> 1), (kq | k) != 0 ? 1u : 0u);
           }
-          tc_commit(bar(kBarEmpty + stage));
+          if (share_b && ks == 0) {
+            keep_stage = stage;  // released with the second tile's stage
+          } else {
+            if (reuse) tc_commit(bar(kBarEmpty + keep_stage));
+            tc_commit(bar(kBarEmpty + stage));
+          }
           if (++kq == ks_u) { kq = 0; d_tmem += kBRows; }
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
         }
@@ -546,6 +558,7 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
       const int ks_u = g2 ? p.ks2 : p.ks1;
       int k0, ks_n;
       unit_stages(g2, c, split, ks_u, kTg2 == 1 ? 1 : min(kTg2, p.m2 - m * kTg2), k0, ks_n);
+      const bool share_b = kTg2 == 2 && g2 && ks_u == 1 && ks_n == 2;  // as the MMA warp decides
 #pragma unroll 1
       for (int ks = 0, kq = k0; ks < ks_n; ++ks, kq = (kq + 1 == ks_u) ? 0 : kq + 1) {
         if (fills < kStages) {
@@ -556,20 +569,25 @@ __global__ void __launch_bounds__(kExpertThreads, kCtasPerSm) expert_kernel(cons
           oke = __shfl_sync(0xffffffffu, oke, 0);
           if (!oke) break;
         }
-        const uint32_t sb = base + L::kSmemB + stage * kBStageBytes;
-        const uint8_t *gq = dq + kq * kRowBytes;
+        // a down unit of two one-stage tiles: the second tile's MMA reads the
+        // first stage's rows, so its stage only gets this loader's arrival (after
+        // the first stage's copies land: the arrival follows all prior copies)
+        if (!(share_b && ks == 1)) {
+          const uint32_t sb = base + L::kSmemB + stage * kBStageBytes;
+          const uint8_t *gq = dq + kq * kRowBytes;
 #pragma unroll
-        for (int i = 0; i < kPieces; ++i) {
-          if (quarter + 4 * i < nb) cp_async_16(sb + doff[i], gq + soff[i], ((pmask >> i) & 1u) * 16u);
-        }
-        const uint32_t ssb = base + L::kSmemSfb + stage * L::kSfStageBytes;
-        const uint8_t *gs = dsc + kq * L::kSfRow;
+          for (int i = 0; i < kPieces; ++i) {
+            if (quarter + 4 * i < nb) cp_async_16(sb + doff[i], gq + soff[i], ((pmask >> i) & 1u) * 16u);
+          }
+          const uint32_t ssb = base + L::kSmemSfb + stage * L::kSfStageBytes;
+          const uint8_t *gs = dsc + kq * L::kSfRow;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          if (lane + 32 * h < nb) {
+          for (int h = 0; h < 2; ++h) {
+            if (lane + 32 * h < nb) {
 #pragma unroll
-            for (int c = 0; c < kC; ++c)  // chunk c, row lane + 32 h: byte 16 (row % 32) + 4 (row / 32)
-              cp_async_4(ssb + c * 512 + lane * 16 + h * 4, gs + s_base[h] + c * 4, ((smask >> h) & 1u) * 4u);
+              for (int c = 0; c < kC; ++c)  // chunk c, row lane + 32 h: byte 16 (row % 32) + 4 (row / 32)
+                cp_async_4(ssb + c * 512 + lane * 16 + h * 4, gs + s_base[h] + c * 4, ((smask >> h) & 1u) * 4u);
+            }
           }
         }
         cp_async_arrive_noinc(bar(kBarFull + stage));
