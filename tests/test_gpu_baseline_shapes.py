@@ -88,8 +88,11 @@ def test_config2_layer(tokens):
     _check_layer("2", tokens)
 
 
-def test_config3_tp8_slice():
-    _check_layer("2", 32, world=8)
+@pytest.mark.parametrize("tokens", [8, 32])
+def test_config3_tp8_slice(tokens):
+    """Rank 0's TP8 slice (intermediate 256: one-stage down tiles, two per unit
+    sharing one activation copy); at 8 tokens the gate_up tiles also split K."""
+    _check_layer("2", tokens, world=8)
 
 
 def test_config4_nvfp4_layer_with_glm_weights():
